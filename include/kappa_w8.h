@@ -1,0 +1,201 @@
+/*
+ * kappa_w8.h — C ABI of the B200 (sm_100a) W8 fake-quant feed-forward path.
+ *
+ * This library replaces the int8-weight ("W8") feed-forward hot path of the
+ * JAX inference library kappa (baricev/kappa, version 0.0.1).  kappa has no
+ * FFI layer of its own: its boundary is a set of pure Python functions.  Each
+ * entry point below names the kappa function (file:line, paths relative to
+ * the kappa project root) whose behaviour it reproduces.
+ *
+ * Conventions shared by every entry point
+ *   - Pointers are CUDA device pointers unless stated otherwise; the caller
+ *     owns every buffer.  The library never allocates on these paths: scratch
+ *     memory comes from the caller through (workspace, workspace_bytes), and
+ *     each *_workspace_size() query states how much is needed.
+ *   - Work is enqueued on `stream` (a cudaStream_t) and is stream ordered.
+ *     Nothing synchronises the host except kw8_device_status().
+ *   - Return value: KW8_OK (0) or a negative kw8_status.  A human readable
+ *     message for the last failure on the calling thread is returned by
+ *     kw8_last_error().
+ *   - Activations are bf16, row major [tokens][features].
+ *   - W8 weights are int8 stored K-major ("contraction axis innermost"):
+ *     a weight that maps K inputs to N outputs is [N][K] int8, row stride K.
+ *     Stacked expert weights are [E][N][K].  kappa's logical layouts
+ *     ([E, D, I] for gate/up, [E, I, D] for down, [2, H, D] for the Gemma
+ *     gating einsum) are views of these buffers; the Python layer
+ *     (kappa_b200) keeps kappa's logical shapes.
+ *   - K must be a multiple of 16 (row starts stay 16-byte aligned, which the
+ *     TMA engine requires); other shapes return KW8_ERR_UNSUPPORTED.
+ */
+#ifndef KAPPA_W8_H_
+#define KAPPA_W8_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* kw8_stream_t; /* identical to cudaStream_t */
+
+typedef enum kw8_status {
+  KW8_OK = 0,
+  KW8_ERR_INVALID_ARG = -1,    /* null pointer, bad shape, bad enum        */
+  KW8_ERR_UNSUPPORTED = -2,    /* shape outside what the kernels handle    */
+  KW8_ERR_CUDA = -3,           /* a CUDA runtime / driver call failed      */
+  KW8_ERR_WORKSPACE = -4,      /* workspace missing or too small           */
+  KW8_ERR_DEVICE_TIMEOUT = -5, /* a kernel's bounded wait ran out          */
+} kw8_status;
+
+typedef enum kw8_dtype { KW8_DT_F32 = 0, KW8_DT_BF16 = 1 } kw8_dtype;
+
+typedef enum kw8_act {
+  KW8_ACT_GELU_TANH = 0, /* jax.nn.gelu default (approximate=True)          */
+  KW8_ACT_SILU = 1,      /* jax.nn.silu                                      */
+} kw8_act;
+
+/* One W8 weight: int8 values plus either one scale for the whole tensor
+ * (kappa's Q8Weight, kappa/qwen3/quant.py:15-19) or one scale per output
+ * channel (per expert when stacked): [groups][N] scales.                    */
+typedef struct kw8_weight {
+  const int8_t* q;     /* [groups][N][K] int8, K contiguous                 */
+  const void* scale;   /* 1 value, or [groups][N] values                    */
+  int32_t scale_dtype; /* kw8_dtype of `scale`                              */
+  int32_t per_channel; /* 0: one scale; 1: [groups][N] scales               */
+} kw8_weight;
+
+/* ---------------------------------------------------------------- misc -- */
+
+/* Message for the last failing call on this host thread ("" if none).      */
+const char* kw8_last_error(void);
+
+/* ABI version of this library (bumped on any signature change).            */
+int32_t kw8_abi_version(void);
+
+/* Reads and clears the device-side status word that kernels set when a
+ * bounded wait runs out (KW8_ERR_DEVICE_TIMEOUT) or a kernel-side check
+ * fails.  Synchronises `stream`.  *status_out receives 0 or a kw8_status.   */
+int kw8_device_status(int32_t* status_out, kw8_stream_t stream);
+
+/* Tuning and testing knobs, process wide; no kappa counterpart (kappa
+ * leaves kernel choice to XLA).
+ *   option 0 (GEMM path): 0 automatic, 1 tensor-core GEMM, 2 GEMV;
+ *   option 1 (token tile of the tensor-core GEMM): 0 automatic, or a
+ *            multiple of 16 in [16, 256].                                   */
+int kw8_set_option(int32_t option, int64_t value);
+
+/* ------------------------------------------------------- quantisation -- */
+
+/* quantize_weight (kappa/qwen3/quant.py:41-48), per tensor or per channel.
+ *   w        : f32 or bf16 weight with logical shape [outer][K][N] given by
+ *              element strides (stride_outer, stride_k, stride_n), so both
+ *              [.., K, N] (N contiguous) and [.., N, K] (K contiguous)
+ *              inputs are accepted without a copy.
+ *   per_channel = 0 : amax over the whole tensor (kappa's behaviour);
+ *   per_channel = 1 : amax over K for every (outer, n) output channel.
+ *   scale = max(amax / 127, FLT_MIN) in fp32 (IEEE division);
+ *   q     = clip(round_half_even(w / scale), -128, 127)  using the fp32 scale;
+ *   stored scale = scale rounded (RNE) to scale_dtype.
+ *   q_out     : [outer][N][K] int8 (K-major).
+ *   scale_out : 1 value (per tensor) or [outer][N] values, scale_dtype.
+ *   workspace : >= kw8_quantize_workspace_size(outer, N) bytes, 4-byte
+ *               aligned (per-channel absmax scratch).                       */
+size_t kw8_quantize_workspace_size(int64_t outer, int64_t N);
+int kw8_quantize(const void* w, int32_t w_dtype, int64_t outer, int64_t K,
+                 int64_t N, int64_t stride_outer, int64_t stride_k,
+                 int64_t stride_n, int32_t per_channel, int32_t scale_dtype,
+                 int8_t* q_out, void* scale_out, void* workspace,
+                 size_t workspace_bytes, kw8_stream_t stream);
+
+/* to_compute_dtype (kappa/qwen3/quant.py:34-38) for a W8 weight:
+ * out[g][n][k] = dtype(q[g][n][k]) * dtype(scale)  (one rounding per
+ * product, as kappa's `values.astype(dt) * scale.astype(dt)`).
+ * out is [groups][N][K] in out_dtype.                                       */
+int kw8_dequantize(kw8_weight w, int64_t groups, int64_t N, int64_t K,
+                   int32_t out_dtype, void* out, kw8_stream_t stream);
+
+/* ----------------------------------------------------------- dense FFN -- */
+
+/* Gated dense FFN:
+ *   Gemma3 feed_forward (kappa/gemma3/ffn.py:10-26) with act = GELU_TANH and
+ *     gate = gating[0], up = gating[1] ([H][D] each, transpose_gating_einsum
+ *     layout), down = linear viewed K-major ([D][H]);
+ *   Qwen3 swiglu_ffn (kappa/qwen3/ffn.py:12-22) with act = SILU.
+ *   out = (act(x·gateᵀ·s_g) * (x·upᵀ·s_u)) · downᵀ · s_d
+ * x [T][D] bf16; out [T][D] in out_dtype (bf16 normally; f32 gives the
+ * unrounded partial sum a tensor-parallel all-reduce wants).                */
+size_t kw8_dense_ffn_workspace_size(int64_t T, int64_t D, int64_t H);
+int kw8_dense_ffn(const void* x, int64_t T, int64_t D, int64_t H,
+                  kw8_weight gate, kw8_weight up, kw8_weight down, int32_t act,
+                  int32_t out_dtype, void* out, void* workspace,
+                  size_t workspace_bytes, kw8_stream_t stream);
+
+/* ------------------------------------------------------------------ MoE -- */
+
+/* Router of moe_swiglu_ffn: _route (kappa/qwen3/ffn_moe.py:38-56).
+ *   logits[t][e] = Σ_d f32(x[t][d]) * f32(dequant(router))[d][e]   (fp32)
+ *   top-k with ties to the lower expert index (jax.lax.top_k),
+ *   w = bf16(softmax(top-k logits)).
+ * router: [E][D] int8 (K-major view of kappa's [D, E]).
+ * logits_out [T][E] f32 (may be workspace), idx_out [T][k] int32,
+ * w_out [T][k] bf16.                                                         */
+int kw8_moe_route(const void* x, int64_t T, int64_t D, int64_t E, int32_t k,
+                  kw8_weight router, float* logits_out, int32_t* idx_out,
+                  void* w_out, kw8_stream_t stream);
+
+/* The top-k + softmax half of _route alone, on caller-provided logits.     */
+int kw8_moe_topk(const float* logits, int64_t T, int64_t E, int32_t k,
+                 int32_t* idx_out, void* w_out, kw8_stream_t stream);
+
+/* Permutation of _moe_ragged (kappa/qwen3/ffn_moe.py:189-200): the stable
+ * argsort of the flattened expert ids and bincount, plus the fixed-capacity
+ * slot rule of _moe_fixed_capacity (ffn_moe.py:130-141).
+ *   idx [T*k] int32 expert ids (row major [T][k]).
+ *   capacity: rows kept per expert (slot < capacity); <0 means dropless.
+ *   sorted_token [T*k]: token of each sorted row (only the first
+ *       Σ group_sizes rows are written);
+ *   inv_pos [T*k]: sorted row of flat entry i, or -1 if it was dropped;
+ *   group_sizes [E] (rows kept), group_offsets [E+1] (exclusive prefix).    */
+int kw8_moe_permute(const int32_t* idx, int64_t T, int32_t k, int64_t E,
+                    int64_t capacity, int32_t* sorted_token, int32_t* inv_pos,
+                    int32_t* group_sizes, int32_t* group_offsets,
+                    kw8_stream_t stream);
+
+/* Expert FFN over permuted rows: the three ragged_dot calls and the SwiGLU
+ * of _moe_ragged (kappa/qwen3/ffn_moe.py:202-210), run as grouped W8A16
+ * GEMMs.  xs [rows][D] bf16 sorted by expert; group_offsets [E+1] on device;
+ * gate/up [E][I][D], down [E][D][I] int8; ys [rows][D] bf16 where
+ * rows = capacity of the buffers (T*k).                                     */
+size_t kw8_moe_expert_ffn_workspace_size(int64_t rows, int64_t D, int64_t I,
+                                         int64_t E);
+int kw8_moe_expert_ffn(const void* xs, int64_t rows, int64_t D, int64_t I,
+                       int64_t E, const int32_t* group_offsets,
+                       kw8_weight gate, kw8_weight up, kw8_weight down,
+                       void* ys, void* workspace, size_t workspace_bytes,
+                       kw8_stream_t stream);
+
+/* Combine / unpermute (kappa/qwen3/ffn_moe.py:212-215):
+ *   out[t] = bf16( Σ_j f32(w[t][j]) * f32(ys[inv_pos[t*k+j]]) ), entries
+ *   with inv_pos < 0 skipped.  fp32 sum in j order (kappa uses a bf16
+ *   scatter-add whose order XLA chooses).                                   */
+int kw8_moe_combine(const void* ys, const int32_t* inv_pos, const void* w,
+                    int64_t T, int32_t k, int64_t D, void* out,
+                    kw8_stream_t stream);
+
+/* Whole MoE layer: moe_swiglu_ffn (kappa/qwen3/ffn_moe.py:226-299) for the
+ * dropless implementations (ragged_jax, ragged_tokamax, gather_einsum —
+ * mathematically the same function) and, with capacity >= 0, the
+ * fixed_capacity one.  x [T][D] bf16 -> out [T][D] bf16.                    */
+size_t kw8_moe_ffn_workspace_size(int64_t T, int64_t D, int64_t I, int64_t E,
+                                  int32_t k);
+int kw8_moe_ffn(const void* x, int64_t T, int64_t D, int64_t I, int64_t E,
+                int32_t k, int64_t capacity, kw8_weight router,
+                kw8_weight gate, kw8_weight up, kw8_weight down, void* out,
+                void* workspace, size_t workspace_bytes, kw8_stream_t stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* KAPPA_W8_H_ */

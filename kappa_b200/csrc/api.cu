@@ -1,0 +1,395 @@
+// extern "C" entry points of libkappa_w8 (declared in include/kappa_w8.h).
+#include <atomic>
+#include <climits>
+
+#include "gemm_simt.cuh"
+#include "gemm_tc.cuh"
+#include "moe.cuh"
+#include "quant.cuh"
+
+namespace kw8 {
+const char* last_error();
+void clear_error();
+int read_device_status(int32_t* out, cudaStream_t stream);
+
+namespace {
+
+std::atomic<int> g_opt_path{0};        // 0 auto, 1 tensor core, 2 GEMV
+std::atomic<int> g_opt_token_tile{0};  // 0 auto, else 16..256 (multiple of 16)
+
+// Carves 256-byte aligned sub-buffers out of the caller's workspace.  With
+// base == nullptr it only measures.
+struct Carver {
+  uint8_t* base;
+  size_t cap;
+  size_t off = 0;
+  bool ok = true;
+  Carver(void* b, size_t c) : base(static_cast<uint8_t*>(b)), cap(c) {}
+  template <class T>
+  T* take(int64_t count) {
+    const size_t a = (off + 255) & ~static_cast<size_t>(255);
+    const size_t need = a + static_cast<size_t>(count < 0 ? 0 : count) * sizeof(T);
+    off = need;
+    if (base == nullptr) return nullptr;
+    if (need > cap) {
+      ok = false;
+      return nullptr;
+    }
+    return reinterpret_cast<T*>(base + a);
+  }
+};
+
+int round16(int64_t v) { return static_cast<int>((v + 15) & ~int64_t(15)); }
+
+// Token tile for the tensor-core path: about 1.5x the mean rows per group,
+// 16..256.  Small tiles keep the token TMA box (loaded in full every
+// stage) from dwarfing the weight tile when groups are small.
+int pick_nt(int64_t rows, int64_t groups) {
+  const int forced = g_opt_token_tile.load();
+  if (forced >= 16 && forced <= kTcMaxNT && forced % 16 == 0) return forced;
+  const int64_t mean = (rows + groups - 1) / (groups > 0 ? groups : 1);
+  int64_t nt = round16((mean * 3 + 1) / 2);
+  if (nt < 16) nt = 16;
+  if (nt > kTcMaxNT) nt = kTcMaxNT;
+  return static_cast<int>(nt);
+}
+
+// GEMV (SIMT) path when groups hold about one GEMV tile of rows or fewer.
+bool use_simt(int64_t rows, int64_t groups) {
+  const int p = g_opt_path.load();
+  if (p == 1) return false;
+  if (p == 2) return true;
+  return rows <= static_cast<int64_t>(kSimtTN) * (groups > 0 ? groups : 1) / 2 ||
+         rows <= kSimtTN;
+}
+
+int check_weight(const kw8_weight& w, const char* name) {
+  KW8_REQUIRE(w.q != nullptr && w.scale != nullptr, KW8_ERR_INVALID_ARG, "%s: null pointer", name);
+  KW8_REQUIRE(w.scale_dtype == KW8_DT_F32 || w.scale_dtype == KW8_DT_BF16, KW8_ERR_INVALID_ARG,
+              "%s: scale dtype must be f32 or bf16", name);
+  KW8_REQUIRE(w.per_channel == 0 || w.per_channel == 1, KW8_ERR_INVALID_ARG,
+              "%s: per_channel must be 0 or 1", name);
+  return KW8_OK;
+}
+
+GemmArgs base_args(const kw8_weight& a, const kw8_weight* b) {
+  GemmArgs g{};
+  g.scale_a = a.scale;
+  g.scale_a_dtype = a.scale_dtype;
+  g.scale_a_pc = a.per_channel;
+  if (b) {
+    g.scale_b = b->scale;
+    g.scale_b_dtype = b->scale_dtype;
+    g.scale_b_pc = b->per_channel;
+  } else {
+    g.scale_b = a.scale;
+    g.scale_b_dtype = a.scale_dtype;
+    g.scale_b_pc = a.per_channel;
+  }
+  return g;
+}
+
+// One grouped GEMM through the chosen path.
+int run_gemm(bool simt, int mode, const kw8_weight& a, const kw8_weight* b, int64_t groups,
+             int64_t N_out, int64_t K, const void* x, int64_t x_rows, int64_t ldx,
+             GemmArgs args, cudaStream_t stream) {
+  if (simt) {
+    args.nt = kSimtTN;
+    return launch_gemm_simt(mode, a.q, b ? b->q : nullptr, groups, N_out, K, x, x_rows, ldx, args,
+                            stream);
+  }
+  return launch_gemm_tc(mode, a.q, b ? b->q : nullptr, groups, N_out, K, x, x_rows, ldx, args,
+                        stream);
+}
+
+struct MoeBuffers {
+  float* logits;
+  int32_t* idx;
+  __nv_bfloat16* w;
+  int32_t* sorted_token;
+  int32_t* inv_pos;
+  int32_t* group_sizes;
+  int32_t* group_offsets;
+  TileEntry* tiles;
+  int32_t* num_tiles;
+  __nv_bfloat16* xs;
+  __nv_bfloat16* h;
+  __nv_bfloat16* ys;
+};
+
+struct ExpertBuffers {
+  TileEntry* tiles;
+  int32_t* num_tiles;
+  __nv_bfloat16* h;
+};
+
+int64_t tile_capacity(int64_t rows, int64_t groups, int nt_min) {
+  return groups + (rows + nt_min - 1) / nt_min + 1;
+}
+
+ExpertBuffers carve_expert(Carver& c, int64_t rows, int64_t I, int64_t E) {
+  ExpertBuffers b;
+  b.tiles = c.take<TileEntry>(tile_capacity(rows, E, 8));
+  b.num_tiles = c.take<int32_t>(1);
+  b.h = c.take<__nv_bfloat16>(rows * I);
+  return b;
+}
+
+MoeBuffers carve_moe(Carver& c, int64_t T, int64_t D, int64_t I, int64_t E, int k) {
+  MoeBuffers b;
+  const int64_t m = T * k;
+  b.logits = c.take<float>(T * E);
+  b.idx = c.take<int32_t>(m);
+  b.w = c.take<__nv_bfloat16>(m);
+  b.sorted_token = c.take<int32_t>(m);
+  b.inv_pos = c.take<int32_t>(m);
+  b.group_sizes = c.take<int32_t>(E);
+  b.group_offsets = c.take<int32_t>(E + 1);
+  b.tiles = c.take<TileEntry>(tile_capacity(m, E, 8));
+  b.num_tiles = c.take<int32_t>(1);
+  b.xs = c.take<__nv_bfloat16>(m * D);
+  b.h = c.take<__nv_bfloat16>(m * I);
+  b.ys = c.take<__nv_bfloat16>(m * D);
+  return b;
+}
+
+// Expert FFN over rows already sorted by group (gate/up + SwiGLU, down).
+int expert_ffn(const void* xs, int64_t rows, int64_t D, int64_t I, int64_t E,
+               const int32_t* group_offsets, const kw8_weight& gate, const kw8_weight& up,
+               const kw8_weight& down, void* ys, const ExpertBuffers& b, cudaStream_t stream) {
+  const bool simt = use_simt(rows, E);
+  const int nt = simt ? kSimtTN : pick_nt(rows, E);
+  int rc = launch_build_tiles(group_offsets, E, nt, b.tiles, b.num_tiles, stream);
+  if (rc) return rc;
+  GemmArgs g = base_args(gate, &up);
+  g.tiles = b.tiles;
+  g.num_tiles = b.num_tiles;
+  g.nt = nt;
+  g.out = b.h;
+  g.ld_out = I;
+  rc = run_gemm(simt, EPI_PAIR_SILU, gate, &up, E, I, D, xs, rows, D, g, stream);
+  if (rc) return rc;
+  GemmArgs d = base_args(down, nullptr);
+  d.tiles = b.tiles;
+  d.num_tiles = b.num_tiles;
+  d.nt = nt;
+  d.out = ys;
+  d.ld_out = D;
+  return run_gemm(simt, EPI_PLAIN_BF16, down, nullptr, E, D, I, b.h, rows, I, d, stream);
+}
+
+int route(const void* x, int64_t T, int64_t D, int64_t E, int k, const kw8_weight& router,
+          float* logits, int32_t* idx, void* w, cudaStream_t stream) {
+  const bool simt = use_simt(T, 1);
+  GemmArgs r = base_args(router, nullptr);
+  r.tiles = nullptr;
+  r.num_tiles = nullptr;
+  r.dense_rows = static_cast<int>(T);
+  r.nt = simt ? kSimtTN : pick_nt(T, 1);
+  r.out = logits;
+  r.ld_out = E;
+  int rc = run_gemm(simt, EPI_PLAIN_F32, router, nullptr, 1, E, D, x, T, D, r, stream);
+  if (rc) return rc;
+  return launch_topk(logits, T, E, k, idx, w, stream);
+}
+
+}  // namespace
+}  // namespace kw8
+
+using namespace kw8;
+
+#define KW8_API_BEGIN clear_error();
+
+extern "C" {
+
+const char* kw8_last_error(void) { return kw8::last_error(); }
+
+int32_t kw8_abi_version(void) { return 1; }
+
+int kw8_device_status(int32_t* status_out, kw8_stream_t stream) {
+  KW8_API_BEGIN
+  return read_device_status(status_out, stream);
+}
+
+int kw8_set_option(int32_t option, int64_t value) {
+  KW8_API_BEGIN
+  if (option == 0) {
+    KW8_REQUIRE(value >= 0 && value <= 2, KW8_ERR_INVALID_ARG, "path must be 0, 1 or 2");
+    g_opt_path.store(static_cast<int>(value));
+    return KW8_OK;
+  }
+  if (option == 1) {
+    KW8_REQUIRE(value == 0 || (value >= 16 && value <= kTcMaxNT && value % 16 == 0),
+                KW8_ERR_INVALID_ARG, "token tile must be 0 or a multiple of 16 in [16, 256]");
+    g_opt_token_tile.store(static_cast<int>(value));
+    return KW8_OK;
+  }
+  return fail(KW8_ERR_INVALID_ARG, "unknown option %d", option);
+}
+
+size_t kw8_quantize_workspace_size(int64_t outer, int64_t N) {
+  return kw8::quantize_workspace_size(outer, N);
+}
+
+int kw8_quantize(const void* w, int32_t w_dtype, int64_t outer, int64_t K, int64_t N,
+                 int64_t stride_outer, int64_t stride_k, int64_t stride_n, int32_t per_channel,
+                 int32_t scale_dtype, int8_t* q_out, void* scale_out, void* workspace,
+                 size_t workspace_bytes, kw8_stream_t stream) {
+  KW8_API_BEGIN
+  KW8_REQUIRE(per_channel == 0 || per_channel == 1, KW8_ERR_INVALID_ARG, "per_channel must be 0/1");
+  return launch_quantize(w, w_dtype, outer, K, N, stride_outer, stride_k, stride_n, per_channel,
+                         scale_dtype, q_out, scale_out, workspace, workspace_bytes, stream);
+}
+
+int kw8_dequantize(kw8_weight w, int64_t groups, int64_t N, int64_t K, int32_t out_dtype,
+                   void* out, kw8_stream_t stream) {
+  KW8_API_BEGIN
+  int rc = check_weight(w, "weight");
+  if (rc) return rc;
+  return launch_dequantize(w, groups, N, K, out_dtype, out, stream);
+}
+
+size_t kw8_dense_ffn_workspace_size(int64_t T, int64_t D, int64_t H) {
+  (void)D;
+  Carver c(nullptr, SIZE_MAX);
+  c.take<__nv_bfloat16>(T * H);
+  return c.off;
+}
+
+int kw8_dense_ffn(const void* x, int64_t T, int64_t D, int64_t H, kw8_weight gate, kw8_weight up,
+                  kw8_weight down, int32_t act, int32_t out_dtype, void* out, void* workspace,
+                  size_t workspace_bytes, kw8_stream_t stream) {
+  KW8_API_BEGIN
+  KW8_REQUIRE(x && out, KW8_ERR_INVALID_ARG, "null x/out");
+  KW8_REQUIRE(T >= 0 && D > 0 && H > 0, KW8_ERR_INVALID_ARG, "bad shape");
+  KW8_REQUIRE(act == KW8_ACT_GELU_TANH || act == KW8_ACT_SILU, KW8_ERR_INVALID_ARG, "bad act");
+  KW8_REQUIRE(out_dtype == KW8_DT_BF16 || out_dtype == KW8_DT_F32, KW8_ERR_INVALID_ARG,
+              "bad out dtype");
+  int rc = check_weight(gate, "gate");
+  if (!rc) rc = check_weight(up, "up");
+  if (!rc) rc = check_weight(down, "down");
+  if (rc) return rc;
+  if (T == 0) return KW8_OK;
+  KW8_REQUIRE(T < (1ll << 31), KW8_ERR_UNSUPPORTED, "too many tokens");
+  Carver c(workspace, workspace_bytes);
+  __nv_bfloat16* h = c.take<__nv_bfloat16>(T * H);
+  KW8_REQUIRE(workspace != nullptr && c.ok, KW8_ERR_WORKSPACE, "dense FFN workspace too small");
+  const bool simt = use_simt(T, 1);
+  const int nt = simt ? kSimtTN : pick_nt(T, 1);
+  GemmArgs g = base_args(gate, &up);
+  g.dense_rows = static_cast<int>(T);
+  g.nt = nt;
+  g.out = h;
+  g.ld_out = H;
+  rc = run_gemm(simt, act == KW8_ACT_GELU_TANH ? EPI_PAIR_GELU : EPI_PAIR_SILU, gate, &up, 1, H, D,
+                x, T, D, g, stream);
+  if (rc) return rc;
+  GemmArgs d = base_args(down, nullptr);
+  d.dense_rows = static_cast<int>(T);
+  d.nt = nt;
+  d.out = out;
+  d.ld_out = D;
+  return run_gemm(simt, out_dtype == KW8_DT_F32 ? EPI_PLAIN_F32 : EPI_PLAIN_BF16, down, nullptr, 1,
+                  D, H, h, T, H, d, stream);
+}
+
+int kw8_moe_route(const void* x, int64_t T, int64_t D, int64_t E, int32_t k, kw8_weight router,
+                  float* logits_out, int32_t* idx_out, void* w_out, kw8_stream_t stream) {
+  KW8_API_BEGIN
+  KW8_REQUIRE(x && logits_out && idx_out && w_out, KW8_ERR_INVALID_ARG, "null pointer");
+  int rc = check_weight(router, "router");
+  if (rc) return rc;
+  if (T == 0) return KW8_OK;
+  return kw8::route(x, T, D, E, k, router, logits_out, idx_out, w_out, stream);
+}
+
+int kw8_moe_topk(const float* logits, int64_t T, int64_t E, int32_t k, int32_t* idx_out,
+                 void* w_out, kw8_stream_t stream) {
+  KW8_API_BEGIN
+  KW8_REQUIRE(logits && idx_out && w_out, KW8_ERR_INVALID_ARG, "null pointer");
+  return launch_topk(logits, T, E, k, idx_out, w_out, stream);
+}
+
+int kw8_moe_permute(const int32_t* idx, int64_t T, int32_t k, int64_t E, int64_t capacity,
+                    int32_t* sorted_token, int32_t* inv_pos, int32_t* group_sizes,
+                    int32_t* group_offsets, kw8_stream_t stream) {
+  KW8_API_BEGIN
+  KW8_REQUIRE(idx && sorted_token && inv_pos && group_sizes && group_offsets, KW8_ERR_INVALID_ARG,
+              "null pointer");
+  return launch_permute(idx, T, k, E, capacity, sorted_token, inv_pos, group_sizes, group_offsets,
+                        stream);
+}
+
+size_t kw8_moe_expert_ffn_workspace_size(int64_t rows, int64_t D, int64_t I, int64_t E) {
+  (void)D;
+  Carver c(nullptr, SIZE_MAX);
+  carve_expert(c, rows, I, E);
+  return c.off;
+}
+
+int kw8_moe_expert_ffn(const void* xs, int64_t rows, int64_t D, int64_t I, int64_t E,
+                       const int32_t* group_offsets, kw8_weight gate, kw8_weight up,
+                       kw8_weight down, void* ys, void* workspace, size_t workspace_bytes,
+                       kw8_stream_t stream) {
+  KW8_API_BEGIN
+  KW8_REQUIRE(xs && ys && group_offsets, KW8_ERR_INVALID_ARG, "null pointer");
+  KW8_REQUIRE(rows >= 0 && D > 0 && I > 0 && E > 0, KW8_ERR_INVALID_ARG, "bad shape");
+  int rc = check_weight(gate, "gate");
+  if (!rc) rc = check_weight(up, "up");
+  if (!rc) rc = check_weight(down, "down");
+  if (rc) return rc;
+  if (rows == 0) return KW8_OK;
+  Carver c(workspace, workspace_bytes);
+  ExpertBuffers b = carve_expert(c, rows, I, E);
+  KW8_REQUIRE(workspace != nullptr && c.ok, KW8_ERR_WORKSPACE, "expert FFN workspace too small");
+  return expert_ffn(xs, rows, D, I, E, group_offsets, gate, up, down, ys, b, stream);
+}
+
+int kw8_moe_combine(const void* ys, const int32_t* inv_pos, const void* w, int64_t T, int32_t k,
+                    int64_t D, void* out, kw8_stream_t stream) {
+  KW8_API_BEGIN
+  KW8_REQUIRE(ys && inv_pos && w && out, KW8_ERR_INVALID_ARG, "null pointer");
+  return launch_combine(ys, inv_pos, w, T, k, D, out, stream);
+}
+
+size_t kw8_moe_ffn_workspace_size(int64_t T, int64_t D, int64_t I, int64_t E, int32_t k) {
+  Carver c(nullptr, SIZE_MAX);
+  carve_moe(c, T, D, I, E, k);
+  return c.off;
+}
+
+int kw8_moe_ffn(const void* x, int64_t T, int64_t D, int64_t I, int64_t E, int32_t k,
+                int64_t capacity, kw8_weight router, kw8_weight gate, kw8_weight up,
+                kw8_weight down, void* out, void* workspace, size_t workspace_bytes,
+                kw8_stream_t stream) {
+  KW8_API_BEGIN
+  KW8_REQUIRE(x && out, KW8_ERR_INVALID_ARG, "null x/out");
+  KW8_REQUIRE(T >= 0 && D > 0 && I > 0 && E > 0 && k >= 1 && k <= E, KW8_ERR_INVALID_ARG,
+              "bad shape (T=%lld D=%lld I=%lld E=%lld k=%d)", (long long)T, (long long)D,
+              (long long)I, (long long)E, k);
+  int rc = check_weight(router, "router");
+  if (!rc) rc = check_weight(gate, "gate");
+  if (!rc) rc = check_weight(up, "up");
+  if (!rc) rc = check_weight(down, "down");
+  if (rc) return rc;
+  if (T == 0) return KW8_OK;
+  KW8_REQUIRE(T * k < (1ll << 31), KW8_ERR_UNSUPPORTED, "too many routed rows");
+  Carver c(workspace, workspace_bytes);
+  MoeBuffers b = carve_moe(c, T, D, I, E, k);
+  KW8_REQUIRE(workspace != nullptr && c.ok, KW8_ERR_WORKSPACE,
+              "MoE workspace too small (%zu < %zu)", workspace_bytes, c.off);
+  const int64_t m = T * k;
+  rc = kw8::route(x, T, D, E, k, router, b.logits, b.idx, b.w, stream);
+  if (rc) return rc;
+  rc = launch_permute(b.idx, T, k, E, capacity, b.sorted_token, b.inv_pos, b.group_sizes,
+                      b.group_offsets, stream);
+  if (rc) return rc;
+  rc = launch_gather(x, b.sorted_token, b.group_offsets + E, m, D, b.xs, stream);
+  if (rc) return rc;
+  ExpertBuffers eb{b.tiles, b.num_tiles, b.h};
+  rc = expert_ffn(b.xs, m, D, I, E, b.group_offsets, gate, up, down, b.ys, eb, stream);
+  if (rc) return rc;
+  return launch_combine(b.ys, b.inv_pos, b.w, T, k, D, out, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,394 @@
+// tcgen05 grouped W8A16 GEMM: kernel and launcher.  Design notes are in
+// gemm_tc.cuh.
+#include "gemm_tc.cuh"
+
+namespace kw8 {
+
+namespace {
+
+struct TileInfo {
+  int group, row0, nrows, mt;
+};
+
+__device__ __forceinline__ TileInfo decode_tile(const GemmArgs& p, int t) {
+  TileInfo ti;
+  const int e = t / p.m_tiles;
+  ti.mt = t - e * p.m_tiles;
+  if (p.tiles == nullptr) {
+    ti.group = 0;
+    ti.row0 = e * p.nt;
+    ti.nrows = min(p.nt, p.dense_rows - ti.row0);
+  } else {
+    const TileEntry te = p.tiles[e];
+    ti.group = te.group;
+    ti.row0 = te.row0;
+    ti.nrows = te.nrows;
+  }
+  return ti;
+}
+
+__device__ __forceinline__ float scale_at(const void* s, int dtype, int pc,
+                                          int64_t idx) {
+  return load_scale(s, dtype, pc ? idx : 0);
+}
+
+template <int kMode>
+__device__ __forceinline__ void epilogue_tile(const GemmArgs& p,
+                                              const TileInfo& ti,
+                                              uint32_t tmem_lane_base, int q,
+                                              int lane) {
+  constexpr bool kPair = epi_is_pair(kMode);
+  const int nrows = ti.nrows;
+  const int nchunks = (nrows + 31) >> 5;
+  if constexpr (kPair) {
+    const int f = ti.mt * 64 + q * 16 + (lane & 15);
+    const bool fvalid = f < p.N_out;
+    const int64_t sidx = static_cast<int64_t>(ti.group) * p.N_out + (fvalid ? f : 0);
+    const float s = (lane < 16)
+                        ? scale_at(p.scale_a, p.scale_a_dtype, p.scale_a_pc, sidx)
+                        : scale_at(p.scale_b, p.scale_b_dtype, p.scale_b_pc, sidx);
+    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
+    for (int c = 0; c < nchunks; ++c) {
+      uint32_t r[32];
+      KW8_TMEM_LD_X32(tmem_lane_base + kTcAccCol + c * 32, r);
+      tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float lo = __uint_as_float(r[j]) * s;       // token c*32 + j
+        const float hi = __uint_as_float(r[16 + j]) * s;  // token c*32 + 16 + j
+        const float send = (lane < 16) ? hi : lo;
+        const float recv = __shfl_xor_sync(0xffffffffu, send, 16);
+        const float g = (lane < 16) ? lo : recv;
+        const float u = (lane < 16) ? recv : hi;
+        const int tok = c * 32 + j + ((lane < 16) ? 0 : 16);
+        float h;
+        if constexpr (kMode == EPI_PAIR_GELU)
+          h = gelu_tanh_f(g) * u;
+        else
+          h = silu_f(g) * u;
+        if (fvalid && tok < nrows)
+          out[static_cast<int64_t>(ti.row0 + tok) * p.ld_out + f] = __float2bfloat16_rn(h);
+      }
+    }
+  } else {
+    const int f = ti.mt * 128 + q * 32 + lane;
+    const bool fvalid = f < p.N_out;
+    const int64_t sidx = static_cast<int64_t>(ti.group) * p.N_out + (fvalid ? f : 0);
+    const float s = scale_at(p.scale_a, p.scale_a_dtype, p.scale_a_pc, sidx);
+    for (int c = 0; c < nchunks; ++c) {
+      uint32_t r[32];
+      KW8_TMEM_LD_X32(tmem_lane_base + kTcAccCol + c * 32, r);
+      tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int tok = c * 32 + j;
+        if (fvalid && tok < nrows) {
+          const float y = __uint_as_float(r[j]) * s;
+          const int64_t o = static_cast<int64_t>(ti.row0 + tok) * p.ld_out + f;
+          if constexpr (kMode == EPI_PLAIN_F32)
+            static_cast<float*>(p.out)[o] = y;
+          else
+            static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(y);
+        }
+      }
+    }
+  }
+}
+
+template <int kMode>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    w8_gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a0,
+                      const __grid_constant__ CUtensorMap map_a1,
+                      const __grid_constant__ CUtensorMap map_b,
+                      const GemmArgs p) {
+  constexpr bool kPair = epi_is_pair(kMode);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+
+  __shared__ uint64_t full_bar[kTcStages];
+  __shared__ uint64_t aready_bar[kTcStages];
+  __shared__ uint64_t empty_bar[kTcStages];
+  __shared__ uint64_t acc_full_bar;
+  __shared__ uint64_t acc_empty_bar;
+  __shared__ uint64_t drain_bar;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int abort_sh;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTcStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&aready_bar[s], 4);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(&acc_full_bar, 1);
+    mbar_init(&acc_empty_bar, 4);
+    mbar_init(&drain_bar, 1);
+    abort_sh = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_a0);
+    if (kPair) tma_prefetch_desc(&map_a1);
+    tma_prefetch_desc(&map_b);
+  }
+  if (warp == 1) tmem_alloc(&tmem_base_sh, kTcTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+  volatile int* abort_flag = &abort_sh;
+
+  const int n_entries =
+      (p.tiles == nullptr) ? (p.dense_rows + p.nt - 1) / p.nt : *p.num_tiles;
+  const int total_tiles = n_entries * p.m_tiles;
+  const int k_tiles = (p.K + kTcBK - 1) / kTcBK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------ TMA producer ----
+      const uint32_t tx_bytes = kTcATileBytes + static_cast<uint32_t>(p.nt) * kTcBK * 2;
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_parity = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
+        const TileInfo ti = decode_tile(p, t);
+        const int a_row = ti.group * p.N_out + ti.mt * (kPair ? 64 : 128);
+        for (int kt = 0; kt < k_tiles; ++kt) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* a_dst = smem + stage * kTcStageBytes;
+          uint8_t* b_dst = a_dst + kTcATileBytes;
+          mbar_arrive_expect_tx(&full_bar[stage], tx_bytes);
+          if (kPair) {
+            tma_load_2d(a_dst, &map_a0, &full_bar[stage], kt * kTcBK, a_row);
+            tma_load_2d(a_dst + kTcATileBytes / 2, &map_a1, &full_bar[stage], kt * kTcBK, a_row);
+          } else {
+            tma_load_2d(a_dst, &map_a0, &full_bar[stage], kt * kTcBK, a_row);
+          }
+          tma_load_2d(b_dst, &map_b, &full_bar[stage], kt * kTcBK, ti.row0);
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == kTcStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Never leave the CTA with a TMA write still in flight: wait (time
+      // bounded, abort ignored) for the last load issued into each stage.
+      for (int s = 0; s < kTcStages; ++s)
+        if (issued_mask & (1u << s))
+          mbar_wait(&full_bar[s], (issued_parity >> s) & 1u, nullptr);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // --------------------------------------------------- MMA issuer ----
+      int stage = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
+        const TileInfo ti = decode_tile(p, t);
+        const uint32_t n_mma = static_cast<uint32_t>(max(16, (ti.nrows + 15) & ~15));
+        const uint32_t idesc = idesc_bf16_f32(128, n_mma);
+        if (!mbar_wait(&acc_empty_bar, acc_phase ^ 1u, abort_flag)) break;
+        tc_fence_after();
+        for (int kt = 0; kt < k_tiles; ++kt) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag) ||
+              !mbar_wait(&aready_bar[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t b_addr = smem_u32(smem + stage * kTcStageBytes + kTcATileBytes);
+          const uint32_t a_tmem = tmem + kTcASlotCol + stage * 32;
+#pragma unroll
+          for (int kk = 0; kk < kTcBK / 16; ++kk) {
+            const uint64_t bdesc = smem_desc_kmajor_sw128(b_addr + kk * 32);
+            mma_ts_bf16(tmem + kTcAccCol, a_tmem + kk * 8, bdesc, idesc,
+                        (kt | kk) != 0 ? 1u : 0u);
+          }
+          mma_commit(&empty_bar[stage]);
+          if (++stage == kTcStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&acc_full_bar);
+        acc_phase ^= 1u;
+      }
+      // Drain: every MMA issued above has completed once this arrives.
+      mma_commit(&drain_bar);
+      mbar_wait(&drain_bar, 0, nullptr);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------ converters + epilogue ----
+    const int q = warp & 3;  // TMEM lane quarter of this warp
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    const int src_row = kPair ? ((lane < 16) ? (q * 16 + lane) : (64 + q * 16 + lane - 16))
+                              : (q * 32 + lane);
+    const int swz = (src_row >> 1) & 3;  // 64-byte TMA swizzle of this row
+    int stage = 0;
+    uint32_t phase = 0, acc_phase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
+      const TileInfo ti = decode_tile(p, t);
+      for (int kt = 0; kt < k_tiles; ++kt) {
+        // Warp-uniform outcome: the tcgen05.st below needs all 32 lanes.
+        if (!__all_sync(0xffffffffu, mbar_wait(&full_bar[stage], phase, abort_flag))) {
+          ok = false;
+          break;
+        }
+        const uint8_t* a_src = smem + stage * kTcStageBytes + src_row * kTcBK;
+        uint32_t v[32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint4 w = *reinterpret_cast<const uint4*>(a_src + ((c ^ swz) << 4));
+          i8x4_to_bf16x4(w.x, v[c * 8 + 0], v[c * 8 + 1]);
+          i8x4_to_bf16x4(w.y, v[c * 8 + 2], v[c * 8 + 3]);
+          i8x4_to_bf16x4(w.z, v[c * 8 + 4], v[c * 8 + 5]);
+          i8x4_to_bf16x4(w.w, v[c * 8 + 6], v[c * 8 + 7]);
+        }
+        KW8_TMEM_ST_X32(lane_base + kTcASlotCol + stage * 32, v);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&aready_bar[stage]);
+        if (++stage == kTcStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+      if (!__all_sync(0xffffffffu, mbar_wait(&acc_full_bar, acc_phase, abort_flag))) break;
+      tc_fence_after();
+      epilogue_tile<kMode>(p, ti, lane_base, q, lane);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty_bar);
+      acc_phase ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTcTmemCols);
+  }
+}
+
+int g_num_sms[64] = {0};
+
+int num_sms(int dev) {
+  if (dev < 0 || dev >= 64) return 148;
+  if (g_num_sms[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    g_num_sms[dev] = n;
+  }
+  return g_num_sms[dev];
+}
+
+template <int kMode>
+int launch_mode(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b,
+                const GemmArgs& args, int grid, cudaStream_t stream) {
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  KW8_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    KW8_CUDA_TRY(cudaFuncSetAttribute(w8_gemm_tc_kernel<kMode>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      kTcSmemBytes));
+    attr_set[dev] = true;
+  }
+  w8_gemm_tc_kernel<kMode><<<grid, kTcThreads, kTcSmemBytes, stream>>>(a0, a1, b, args);
+  KW8_CHECK_LAUNCH();
+  return KW8_OK;
+}
+
+}  // namespace
+
+// Launches the grouped GEMM.  `wa` (and `wb` in paired mode) are int8
+// [groups][N_out][K]; x is bf16 [x_rows][ldx].  `args_in` carries the tile
+// source, scales and output; the launcher fills in the shape fields.
+int launch_gemm_tc(int mode, const int8_t* wa, const int8_t* wb, int64_t groups,
+                   int64_t N_out, int64_t K, const void* x, int64_t x_rows,
+                   int64_t ldx, const GemmArgs& args_in, cudaStream_t stream) {
+  const bool pair = epi_is_pair(mode);
+  KW8_REQUIRE(K > 0 && K % 16 == 0, KW8_ERR_UNSUPPORTED, "K=%lld must be a positive multiple of 16",
+              (long long)K);
+  KW8_REQUIRE(ldx % 8 == 0 && ldx >= K, KW8_ERR_UNSUPPORTED, "token row pitch %lld invalid",
+              (long long)ldx);
+  KW8_REQUIRE(N_out > 0 && groups > 0 && groups * N_out < (1ll << 31), KW8_ERR_UNSUPPORTED,
+              "weight rows out of range");
+  KW8_REQUIRE(x_rows > 0 && x_rows < (1ll << 31), KW8_ERR_UNSUPPORTED, "token rows out of range");
+  KW8_REQUIRE(args_in.nt >= 16 && args_in.nt <= kTcMaxNT && args_in.nt % 16 == 0,
+              KW8_ERR_INVALID_ARG, "token tile %d invalid", args_in.nt);
+  KW8_REQUIRE(!pair || wb != nullptr, KW8_ERR_INVALID_ARG, "paired GEMM needs two weights");
+  KW8_REQUIRE((reinterpret_cast<uintptr_t>(wa) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(wb) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(x) & 15) == 0,
+              KW8_ERR_UNSUPPORTED, "operands must be 16-byte aligned");
+
+  GemmArgs args = args_in;
+  args.K = static_cast<int>(K);
+  args.N_out = static_cast<int>(N_out);
+  const int rows_per_mtile = pair ? 64 : 128;
+  args.m_tiles = static_cast<int>((N_out + rows_per_mtile - 1) / rows_per_mtile);
+
+  CUtensorMap map_a0, map_a1, map_b;
+  const uint32_t a_box_rows = pair ? 64 : 128;
+  int rc = make_tmap_2d(&map_a0, wa, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1,
+                        static_cast<uint64_t>(groups * N_out), static_cast<uint64_t>(K),
+                        static_cast<uint64_t>(K), kTcBK, a_box_rows,
+                        CU_TENSOR_MAP_SWIZZLE_64B);
+  if (rc) return rc;
+  if (pair) {
+    rc = make_tmap_2d(&map_a1, wb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1,
+                      static_cast<uint64_t>(groups * N_out), static_cast<uint64_t>(K),
+                      static_cast<uint64_t>(K), kTcBK, a_box_rows, CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc) return rc;
+  } else {
+    map_a1 = map_a0;
+  }
+  rc = make_tmap_2d(&map_b, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                    static_cast<uint64_t>(x_rows), static_cast<uint64_t>(K),
+                    static_cast<uint64_t>(ldx) * 2, kTcBK, static_cast<uint32_t>(args.nt),
+                    CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+
+  // Upper bound on the work: the table holds at most groups + rows/nt
+  // entries; a dense range holds ceil(rows/nt).
+  int64_t max_entries = args.tiles == nullptr
+                            ? (args.dense_rows + args.nt - 1) / args.nt
+                            : groups + (x_rows + args.nt - 1) / args.nt;
+  int64_t max_tiles = max_entries * args.m_tiles;
+  if (max_tiles <= 0) return KW8_OK;
+  int dev = 0;
+  KW8_CUDA_TRY(cudaGetDevice(&dev));
+  const int grid = static_cast<int>(std::min<int64_t>(max_tiles, num_sms(dev)));
+
+  switch (mode) {
+    case EPI_PAIR_GELU:
+      return launch_mode<EPI_PAIR_GELU>(map_a0, map_a1, map_b, args, grid, stream);
+    case EPI_PAIR_SILU:
+      return launch_mode<EPI_PAIR_SILU>(map_a0, map_a1, map_b, args, grid, stream);
+    case EPI_PLAIN_BF16:
+      return launch_mode<EPI_PLAIN_BF16>(map_a0, map_a1, map_b, args, grid, stream);
+    case EPI_PLAIN_F32:
+      return launch_mode<EPI_PLAIN_F32>(map_a0, map_a1, map_b, args, grid, stream);
+    default:
+      return fail(KW8_ERR_INVALID_ARG, "unknown epilogue mode %d", mode);
+  }
+}
+
+}  // namespace kw8

@@ -1,0 +1,9 @@
+// Single translation unit of libkappa_w8.so: the parts share one device
+// status word and are compiled together so no relocatable device code is
+// needed.
+#include "host.cu"
+#include "quant.cu"
+#include "gemm_tc.cu"
+#include "gemm_simt.cu"
+#include "moe.cu"
+#include "api.cu"

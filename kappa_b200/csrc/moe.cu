@@ -1,0 +1,354 @@
+// MoE routing kernels: top-k + softmax, stable expert permutation,
+// tile-table construction, row gather and the weighted combine.
+#include "moe.cuh"
+
+namespace kw8 {
+
+namespace {
+
+constexpr int kBlock = 1024;
+
+// Block-wide exclusive scan of one int per thread (blockDim.x == kBlock).
+// Returns the exclusive prefix; *total receives the block sum.
+__device__ int block_exclusive_scan(int v, int* total) {
+  __shared__ int warp_sums[32];
+  __shared__ int total_sh;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += n;
+  }
+  if (lane == 31) warp_sums[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int s = warp_sums[lane];
+    int si = s;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, si, o);
+      if (lane >= o) si += n;
+    }
+    warp_sums[lane] = si - s;
+    if (lane == 31) total_sh = si;
+  }
+  __syncthreads();
+  const int r = warp_sums[warp] + incl - v;
+  *total = total_sh;
+  __syncthreads();
+  return r;
+}
+
+// ------------------------------------------------------------- top-k ----
+// One warp per token.  Lane l holds logits l, l+32, ... (E <= 32*kMaxPerLane).
+// Round j picks the largest remaining logit, ties to the lower index, which
+// is jax.lax.top_k's order; lane j keeps round j's winner.  The softmax over
+// the k winners is fp32 exp(v - max) / sum, rounded to bf16.
+constexpr int kMaxPerLane = 8;
+
+__global__ void topk_softmax_kernel(const float* __restrict__ logits, int T, int E, int k,
+                                    int32_t* __restrict__ idx_out,
+                                    __nv_bfloat16* __restrict__ w_out) {
+  const int lane = threadIdx.x & 31;
+  const int tok = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (tok >= T) return;
+  const float* row = logits + static_cast<int64_t>(tok) * E;
+  float v[kMaxPerLane];
+  bool taken[kMaxPerLane];
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i) {
+    const int e = lane + 32 * i;
+    v[i] = (e < E) ? row[e] : 0.f;
+    taken[i] = !(e < E);
+  }
+  float my_v = -INFINITY;
+  int my_i = -1;
+  for (int j = 0; j < k; ++j) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) {
+      const int e = lane + 32 * i;
+      if (!taken[i] && (v[i] > bv || (v[i] == bv && e < bi))) {
+        bv = v[i];
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i)
+      if (lane + 32 * i == bi) taken[i] = true;
+    if (lane == j) {
+      my_v = bv;
+      my_i = bi;
+    }
+  }
+  const float m = __shfl_sync(0xffffffffu, my_v, 0);
+  const float ex = (lane < k) ? expf(my_v - m) : 0.f;
+  float s = ex;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane < k) {
+    idx_out[static_cast<int64_t>(tok) * k + lane] = my_i;
+    w_out[static_cast<int64_t>(tok) * k + lane] = __float2bfloat16_rn(__fdiv_rn(ex, s));
+  }
+}
+
+// ----------------------------------------------------------- permute ----
+// Stable counting sort of the T*k expert ids in one CTA of 32 warps.  Warp w
+// owns a contiguous chunk of entries and walks it 32 at a time; lanes with
+// the same expert find each other with __match_any_sync, so a lane's rank
+// among equal experts in the step is the number of lower lanes that match.
+// Pass 1 counts per (warp, expert); the counts become per-(warp, expert)
+// start slots; pass 2 assigns slots in the same order.  The result is the
+// order of a stable argsort by expert id (ties by flat index).
+__global__ void __launch_bounds__(kBlock, 1)
+    permute_kernel(const int32_t* __restrict__ idx, int m, int k, int E, int capacity,
+                   int32_t* __restrict__ sorted_token, int32_t* __restrict__ inv_pos,
+                   int32_t* __restrict__ group_sizes, int32_t* __restrict__ group_offsets) {
+  extern __shared__ int sm[];
+  int* cnt = sm;            // [32][E]
+  int* goff = sm + 32 * E;  // [E]
+  __shared__ int total_sh;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int i = threadIdx.x; i < 32 * E; i += kBlock) cnt[i] = 0;
+  __syncthreads();
+
+  const int chunk = ((m + 31) / 32 + 31) & ~31;
+  const int beg = warp * chunk;
+  const int end = min(m, beg + chunk);
+  for (int base = beg; base < end; base += 32) {
+    const int i = base + lane;
+    int e = (i < end) ? idx[i] : -1;
+    if (i < end && (e < 0 || e >= E)) {
+      report(KW8_ERR_INVALID_ARG);
+      e = -1;
+    }
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    if (e >= 0 && lane == __ffs(peers) - 1) cnt[warp * E + e] += __popc(peers);
+  }
+  __syncthreads();
+
+  for (int e0 = 0; e0 < E; e0 += kBlock) {
+    const int e = e0 + threadIdx.x;
+    int kept = 0;
+    if (e < E) {
+      int acc = 0;
+      for (int w = 0; w < 32; ++w) {
+        const int c = cnt[w * E + e];
+        cnt[w * E + e] = acc;
+        acc += c;
+      }
+      kept = capacity >= 0 ? min(acc, capacity) : acc;
+      group_sizes[e] = kept;
+    }
+    int tot;
+    const int off = block_exclusive_scan(kept, &tot);
+    const int carry = (e0 == 0) ? 0 : total_sh;
+    if (e < E) {
+      goff[e] = carry + off;
+      group_offsets[e] = carry + off;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) total_sh = carry + tot;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) group_offsets[E] = total_sh;
+  __syncthreads();
+
+  for (int base = beg; base < end; base += 32) {
+    const int i = base + lane;
+    int e = (i < end) ? idx[i] : -1;
+    if (e >= E || e < 0) e = -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    if (e >= 0) {
+      const int rank = __popc(peers & ((1u << lane) - 1u));
+      const int slot = cnt[warp * E + e] + rank;
+      if (capacity < 0 || slot < capacity) {
+        const int p = goff[e] + slot;
+        sorted_token[p] = i / k;
+        inv_pos[i] = p;
+      } else {
+        inv_pos[i] = -1;
+      }
+    } else if (i < end) {
+      inv_pos[i] = -1;
+    }
+    __syncwarp();
+    if (e >= 0 && lane == __ffs(peers) - 1) cnt[warp * E + e] += __popc(peers);
+    __syncwarp();
+  }
+}
+
+// Tile table: every group's rows cut into runs of at most `nt` rows.
+__global__ void __launch_bounds__(kBlock, 1)
+    build_tiles_kernel(const int32_t* __restrict__ group_offsets, int E, int nt,
+                       TileEntry* __restrict__ tiles, int32_t* __restrict__ num_tiles) {
+  __shared__ int carry_sh;
+  if (threadIdx.x == 0) carry_sh = 0;
+  __syncthreads();
+  for (int e0 = 0; e0 < E; e0 += kBlock) {
+    const int e = e0 + threadIdx.x;
+    int n = 0, start = 0;
+    if (e < E) {
+      start = group_offsets[e];
+      n = group_offsets[e + 1] - start;
+    }
+    const int cnt = (n + nt - 1) / nt;
+    int tot;
+    const int off = block_exclusive_scan(cnt, &tot) + carry_sh;
+    for (int j = 0; j < cnt; ++j) {
+      TileEntry te;
+      te.group = e;
+      te.row0 = start + j * nt;
+      te.nrows = min(nt, n - j * nt);
+      te.pad = 0;
+      tiles[off + j] = te;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) carry_sh += tot;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *num_tiles = carry_sh;
+}
+
+// ----------------------------------------------------------- gather ----
+// xs[p] = x[sorted_token[p]] for p < group_offsets[E]; 16-byte vectors.
+__global__ void gather_rows_kernel(const uint4* __restrict__ x, const int32_t* __restrict__ sorted_token,
+                                   const int32_t* __restrict__ total_rows, int64_t max_rows,
+                                   int vec_per_row, uint4* __restrict__ xs) {
+  const int64_t tr = *total_rows;
+  const int64_t rows = tr < max_rows ? tr : max_rows;
+  const int64_t n = rows * vec_per_row;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / vec_per_row;
+    const int c = static_cast<int>(i - r * vec_per_row);
+    xs[i] = x[static_cast<int64_t>(sorted_token[r]) * vec_per_row + c];
+  }
+}
+
+// ---------------------------------------------------------- combine ----
+// out[t][8c..8c+7] = bf16( Σ_j f32(w[t][j]) * f32(ys[inv_pos[t*k+j]][8c..]) ).
+__global__ void combine_kernel(const uint4* __restrict__ ys, const int32_t* __restrict__ inv_pos,
+                               const __nv_bfloat16* __restrict__ w, int64_t T, int k,
+                               int vec_per_row, uint4* __restrict__ out) {
+  const int64_t n = T * vec_per_row;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = i / vec_per_row;
+    const int c = static_cast<int>(i - t * vec_per_row);
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < k; ++j) {
+      const int p = inv_pos[t * k + j];
+      if (p < 0) continue;
+      const float wj = __bfloat162float(w[t * k + j]);
+      const uint4 v = ys[static_cast<int64_t>(p) * vec_per_row + c];
+      const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        acc[2 * q] = fmaf(wj, __uint_as_float(words[q] << 16), acc[2 * q]);
+        acc[2 * q + 1] = fmaf(wj, __uint_as_float(words[q] & 0xFFFF0000u), acc[2 * q + 1]);
+      }
+    }
+    uint4 o;
+    uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const __nv_bfloat162 b = __floats2bfloat162_rn(acc[2 * q], acc[2 * q + 1]);
+      ow[q] = *reinterpret_cast<const uint32_t*>(&b);
+    }
+    out[i] = o;
+  }
+}
+
+int grid_for(int64_t n, int threads, int cap) {
+  int64_t g = (n + threads - 1) / threads;
+  if (g < 1) g = 1;
+  if (g > cap) g = cap;
+  return static_cast<int>(g);
+}
+
+}  // namespace
+
+int launch_topk(const float* logits, int64_t T, int64_t E, int k, int32_t* idx, void* w,
+                cudaStream_t stream) {
+  KW8_REQUIRE(E >= 1 && E <= 32 * kMaxPerLane, KW8_ERR_UNSUPPORTED,
+              "top-k supports 1..%d experts (got %lld)", 32 * kMaxPerLane, (long long)E);
+  KW8_REQUIRE(k >= 1 && k <= 32 && k <= E, KW8_ERR_INVALID_ARG, "k=%d invalid for E=%lld", k,
+              (long long)E);
+  if (T <= 0) return KW8_OK;
+  const int warps = 8;
+  const int64_t blocks = (T + warps - 1) / warps;
+  KW8_REQUIRE(blocks < (1ll << 31), KW8_ERR_UNSUPPORTED, "too many tokens");
+  topk_softmax_kernel<<<static_cast<unsigned>(blocks), warps * 32, 0, stream>>>(
+      logits, static_cast<int>(T), static_cast<int>(E), k, idx, static_cast<__nv_bfloat16*>(w));
+  KW8_CHECK_LAUNCH();
+  return KW8_OK;
+}
+
+int launch_permute(const int32_t* idx, int64_t T, int k, int64_t E, int64_t capacity,
+                   int32_t* sorted_token, int32_t* inv_pos, int32_t* group_sizes,
+                   int32_t* group_offsets, cudaStream_t stream) {
+  KW8_REQUIRE(E >= 1 && E <= 1024, KW8_ERR_UNSUPPORTED, "permute supports 1..1024 experts");
+  KW8_REQUIRE(k >= 1 && T >= 0 && T * k < (1ll << 31), KW8_ERR_INVALID_ARG, "bad T/k");
+  const int m = static_cast<int>(T * k);
+  const int cap = capacity < 0 ? -1 : static_cast<int>(std::min<int64_t>(capacity, 1ll << 30));
+  const size_t smem = static_cast<size_t>(33) * E * sizeof(int);
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  KW8_CUDA_TRY(cudaGetDevice(&dev));
+  if (smem > 48 * 1024 && dev >= 0 && dev < 64 && !attr_set[dev]) {
+    KW8_CUDA_TRY(cudaFuncSetAttribute(permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(33 * 1024 * sizeof(int))));
+    attr_set[dev] = true;
+  }
+  permute_kernel<<<1, kBlock, smem, stream>>>(idx, m, k, static_cast<int>(E), cap, sorted_token,
+                                              inv_pos, group_sizes, group_offsets);
+  KW8_CHECK_LAUNCH();
+  return KW8_OK;
+}
+
+int launch_build_tiles(const int32_t* group_offsets, int64_t E, int nt, TileEntry* tiles,
+                       int32_t* num_tiles, cudaStream_t stream) {
+  KW8_REQUIRE(E >= 1 && E <= (1 << 20) && nt >= 1, KW8_ERR_INVALID_ARG, "bad tile table args");
+  build_tiles_kernel<<<1, kBlock, 0, stream>>>(group_offsets, static_cast<int>(E), nt, tiles,
+                                               num_tiles);
+  KW8_CHECK_LAUNCH();
+  return KW8_OK;
+}
+
+int launch_gather(const void* x, const int32_t* sorted_token, const int32_t* total_rows,
+                  int64_t max_rows, int64_t D, void* xs, cudaStream_t stream) {
+  KW8_REQUIRE(D % 8 == 0, KW8_ERR_UNSUPPORTED, "D must be a multiple of 8");
+  if (max_rows <= 0) return KW8_OK;
+  const int vec = static_cast<int>(D / 8);
+  gather_rows_kernel<<<grid_for(max_rows * vec, 256, 148 * 16), 256, 0, stream>>>(
+      static_cast<const uint4*>(x), sorted_token, total_rows, max_rows, vec,
+      static_cast<uint4*>(xs));
+  KW8_CHECK_LAUNCH();
+  return KW8_OK;
+}
+
+int launch_combine(const void* ys, const int32_t* inv_pos, const void* w, int64_t T, int k,
+                   int64_t D, void* out, cudaStream_t stream) {
+  KW8_REQUIRE(D % 8 == 0, KW8_ERR_UNSUPPORTED, "D must be a multiple of 8");
+  if (T <= 0) return KW8_OK;
+  const int vec = static_cast<int>(D / 8);
+  combine_kernel<<<grid_for(T * vec, 256, 148 * 16), 256, 0, stream>>>(
+      static_cast<const uint4*>(ys), inv_pos, static_cast<const __nv_bfloat16*>(w), T, k, vec,
+      static_cast<uint4*>(out));
+  KW8_CHECK_LAUNCH();
+  return KW8_OK;
+}
+
+}  // namespace kw8

@@ -1,0 +1,20 @@
+// MoE routing kernels (see moe.cu).
+#pragma once
+
+#include "gemm_tc.cuh"
+
+namespace kw8 {
+
+int launch_topk(const float* logits, int64_t T, int64_t E, int k, int32_t* idx, void* w,
+                cudaStream_t stream);
+int launch_permute(const int32_t* idx, int64_t T, int k, int64_t E, int64_t capacity,
+                   int32_t* sorted_token, int32_t* inv_pos, int32_t* group_sizes,
+                   int32_t* group_offsets, cudaStream_t stream);
+int launch_build_tiles(const int32_t* group_offsets, int64_t E, int nt, TileEntry* tiles,
+                       int32_t* num_tiles, cudaStream_t stream);
+int launch_gather(const void* x, const int32_t* sorted_token, const int32_t* total_rows,
+                  int64_t max_rows, int64_t D, void* xs, cudaStream_t stream);
+int launch_combine(const void* ys, const int32_t* inv_pos, const void* w, int64_t T, int k,
+                   int64_t D, void* out, cudaStream_t stream);
+
+}  // namespace kw8

@@ -1,0 +1,163 @@
+// W8 quantisation (kappa/qwen3/quant.py:41-48) and dequantisation
+// (quant.py:34-38) kernels.
+//
+// quantize: pass 1 takes the absmax of every output channel (one thread per
+// channel, walking K) and, for the per-tensor form, folds it into one word
+// with an integer atomicMax on the float's bits (valid for non-negative
+// floats; max is order independent, so the result is deterministic).
+// Pass 2 computes scale = max(amax / 127, FLT_MIN) with IEEE division,
+// q = clip(rint(w / scale), -128, 127) (rintf rounds half to even, like
+// jnp.round) and writes q K-major; the stored scale is the fp32 scale
+// rounded to nearest even in the requested dtype.
+#include "quant.cuh"
+
+namespace kw8 {
+
+namespace {
+
+__device__ __forceinline__ float load_w(const void* w, int dtype, int64_t i) {
+  if (dtype == KW8_DT_F32) return static_cast<const float*>(w)[i];
+  return bf16_bits_to_f32(static_cast<const uint16_t*>(w)[i]);
+}
+
+__global__ void amax_kernel(const void* __restrict__ w, int dtype, int64_t outer, int64_t K,
+                            int64_t N, int64_t so, int64_t sk, int64_t sn, int per_channel,
+                            float* __restrict__ ch_amax, unsigned* __restrict__ glob) {
+  const int64_t ch = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (ch >= outer * N) return;
+  const int64_t o = ch / N, n = ch - o * N;
+  const int64_t base = o * so + n * sn;
+  float m = 0.f;
+  for (int64_t k = 0; k < K; ++k) m = fmaxf(m, fabsf(load_w(w, dtype, base + k * sk)));
+  if (per_channel)
+    ch_amax[ch] = m;
+  else
+    atomicMax(glob, __float_as_uint(m));
+}
+
+__device__ __forceinline__ float scale_from_amax(float amax) {
+  return fmaxf(__fdiv_rn(amax, 127.0f), 1.17549435e-38f);  // FLT_MIN floor
+}
+
+__device__ __forceinline__ int8_t quant1(float w, float s) {
+  float r = rintf(__fdiv_rn(w, s));
+  r = fminf(fmaxf(r, -128.0f), 127.0f);
+  return static_cast<int8_t>(static_cast<int>(r));
+}
+
+// One thread per (outer, n, 16-wide k chunk); writes 16 bytes of q[o][n][k].
+// `k_fast` selects the thread order: consecutive threads take consecutive k
+// chunks (K-contiguous input) or consecutive channels (N-contiguous input).
+__global__ void quant_kernel(const void* __restrict__ w, int dtype, int64_t outer, int64_t K,
+                             int64_t N, int64_t so, int64_t sk, int64_t sn, int per_channel,
+                             const float* __restrict__ ch_amax, const unsigned* __restrict__ glob,
+                             int k_fast, int scale_dtype, int8_t* __restrict__ q,
+                             void* __restrict__ scale_out) {
+  const int64_t kc = (K + 15) / 16;
+  const int64_t tid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (tid >= outer * N * kc) return;
+  int64_t ch, c;
+  if (k_fast) {
+    ch = tid / kc;
+    c = tid - ch * kc;
+  } else {
+    const int64_t on = outer * N;
+    c = tid / on;
+    ch = tid - c * on;
+  }
+  const int64_t o = ch / N, n = ch - o * N;
+  const float amax = per_channel ? ch_amax[ch] : __uint_as_float(*glob);
+  const float s = scale_from_amax(amax);
+  const int64_t base = o * so + n * sn;
+  alignas(16) int8_t buf[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int64_t k = c * 16 + i;
+    buf[i] = (k < K) ? quant1(load_w(w, dtype, base + k * sk), s) : 0;
+  }
+  int8_t* dst = q + ch * K + c * 16;
+  if (K % 16 == 0) {
+    *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(buf);
+  } else {
+    for (int i = 0; i < 16 && c * 16 + i < K; ++i) dst[i] = buf[i];
+  }
+  const bool writer = per_channel ? (c == 0) : (tid == 0);
+  if (writer) {
+    const int64_t si = per_channel ? ch : 0;
+    if (scale_dtype == KW8_DT_F32)
+      static_cast<float*>(scale_out)[si] = s;
+    else
+      static_cast<__nv_bfloat16*>(scale_out)[si] = __float2bfloat16_rn(s);
+  }
+}
+
+__global__ void dequant_kernel(const int8_t* __restrict__ q, const void* __restrict__ scale,
+                               int scale_dtype, int per_channel, int64_t K, int64_t total,
+                               int out_dtype, void* __restrict__ out) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float s = load_scale(scale, scale_dtype, per_channel ? i / K : 0);
+    const float v = static_cast<float>(q[i]);
+    if (out_dtype == KW8_DT_F32) {
+      static_cast<float*>(out)[i] = v * s;  // exact: 8-bit x 8..24-bit mantissa
+    } else {
+      // bf16(q) * bf16(s) rounded once to bf16; q and bf16(s) are exact in
+      // fp32 and so is their product (<= 16 significant bits).
+      const float sb = __bfloat162float(__float2bfloat16_rn(s));
+      static_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(v * sb);
+    }
+  }
+}
+
+}  // namespace
+
+size_t quantize_workspace_size(int64_t outer, int64_t N) {
+  return static_cast<size_t>(outer * N + 4) * sizeof(float);
+}
+
+int launch_quantize(const void* w, int w_dtype, int64_t outer, int64_t K, int64_t N, int64_t so,
+                    int64_t sk, int64_t sn, int per_channel, int scale_dtype, int8_t* q,
+                    void* scale_out, void* ws, size_t ws_bytes, cudaStream_t stream) {
+  KW8_REQUIRE(w && q && scale_out, KW8_ERR_INVALID_ARG, "null pointer");
+  KW8_REQUIRE(outer >= 1 && K >= 1 && N >= 1, KW8_ERR_INVALID_ARG, "empty weight");
+  KW8_REQUIRE(w_dtype == KW8_DT_F32 || w_dtype == KW8_DT_BF16, KW8_ERR_INVALID_ARG,
+              "weight dtype must be f32 or bf16");
+  KW8_REQUIRE(scale_dtype == KW8_DT_F32 || scale_dtype == KW8_DT_BF16, KW8_ERR_INVALID_ARG,
+              "scale dtype must be f32 or bf16");
+  KW8_REQUIRE(ws != nullptr && ws_bytes >= quantize_workspace_size(outer, N), KW8_ERR_WORKSPACE,
+              "quantize workspace too small (%zu < %zu)", ws_bytes,
+              quantize_workspace_size(outer, N));
+  KW8_REQUIRE((reinterpret_cast<uintptr_t>(q) & 15) == 0 || K % 16 != 0, KW8_ERR_INVALID_ARG,
+              "q_out must be 16-byte aligned");
+  float* ch_amax = static_cast<float*>(ws);
+  unsigned* glob = reinterpret_cast<unsigned*>(ch_amax + outer * N);
+  KW8_CUDA_TRY(cudaMemsetAsync(glob, 0, sizeof(unsigned), stream));
+  const int64_t channels = outer * N;
+  amax_kernel<<<static_cast<unsigned>((channels + 255) / 256), 256, 0, stream>>>(
+      w, w_dtype, outer, K, N, so, sk, sn, per_channel, ch_amax, glob);
+  KW8_CHECK_LAUNCH();
+  const int64_t threads = channels * ((K + 15) / 16);
+  const int k_fast = (sk == 1) ? 1 : 0;
+  quant_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(
+      w, w_dtype, outer, K, N, so, sk, sn, per_channel, ch_amax, glob, k_fast, scale_dtype, q,
+      scale_out);
+  KW8_CHECK_LAUNCH();
+  return KW8_OK;
+}
+
+int launch_dequantize(const kw8_weight& w, int64_t groups, int64_t N, int64_t K, int out_dtype,
+                      void* out, cudaStream_t stream) {
+  KW8_REQUIRE(w.q && w.scale && out, KW8_ERR_INVALID_ARG, "null pointer");
+  KW8_REQUIRE(out_dtype == KW8_DT_F32 || out_dtype == KW8_DT_BF16, KW8_ERR_INVALID_ARG,
+              "out dtype must be f32 or bf16");
+  const int64_t total = groups * N * K;
+  if (total <= 0) return KW8_OK;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  dequant_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+      w.q, w.scale, w.scale_dtype, w.per_channel, K, total, out_dtype, out);
+  KW8_CHECK_LAUNCH();
+  return KW8_OK;
+}
+
+}  // namespace kw8
