@@ -1,0 +1,157 @@
+"""ctypes binding of ``libkappa_w8.so`` (the C ABI in ``include/kappa_w8.h``).
+
+The shared library is built in-tree (``kappa_b200/build.py``) and loaded
+from this package's directory.  There is no fallback: if the library is
+missing, or no CUDA device is present, calls raise.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+LIB_NAME = "libkappa_w8.so"
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), LIB_NAME)
+
+# kw8_status
+KW8_OK = 0
+KW8_ERR_INVALID_ARG = -1
+KW8_ERR_UNSUPPORTED = -2
+KW8_ERR_CUDA = -3
+KW8_ERR_WORKSPACE = -4
+KW8_ERR_DEVICE_TIMEOUT = -5
+
+# kw8_dtype
+DT_F32 = 0
+DT_BF16 = 1
+
+# kw8_act
+ACT_GELU_TANH = 0
+ACT_SILU = 1
+
+# kw8_set_option
+OPT_GEMM_PATH = 0  # 0 auto, 1 tensor core, 2 GEMV
+OPT_TOKEN_TILE = 1  # 0 auto, 16..256
+
+
+class KW8Error(RuntimeError):
+    """A libkappa_w8 call failed; ``code`` is the kw8_status."""
+
+    def __init__(self, code: int, message: str):
+        super().__init__(f"kappa_w8 error {code}: {message}")
+        self.code = code
+
+
+class KW8Weight(ctypes.Structure):
+    """``kw8_weight`` (include/kappa_w8.h)."""
+
+    _fields_ = [
+        ("q", ctypes.c_void_p),
+        ("scale", ctypes.c_void_p),
+        ("scale_dtype", ctypes.c_int32),
+        ("per_channel", ctypes.c_int32),
+    ]
+
+
+_i64 = ctypes.c_int64
+_i32 = ctypes.c_int32
+_vp = ctypes.c_void_p
+_sz = ctypes.c_size_t
+
+# name -> (restype, argtypes); exactly the functions include/kappa_w8.h declares.
+SIGNATURES: dict[str, tuple] = {
+    "kw8_last_error": (ctypes.c_char_p, []),
+    "kw8_abi_version": (_i32, []),
+    "kw8_device_status": (ctypes.c_int, [ctypes.POINTER(_i32), _vp]),
+    "kw8_set_option": (ctypes.c_int, [_i32, _i64]),
+    "kw8_quantize_workspace_size": (_sz, [_i64, _i64]),
+    "kw8_quantize": (
+        ctypes.c_int,
+        [_vp, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _vp, _vp, _vp, _sz, _vp],
+    ),
+    "kw8_dequantize": (ctypes.c_int, [KW8Weight, _i64, _i64, _i64, _i32, _vp, _vp]),
+    "kw8_dense_ffn_workspace_size": (_sz, [_i64, _i64, _i64]),
+    "kw8_dense_ffn": (
+        ctypes.c_int,
+        [_vp, _i64, _i64, _i64, KW8Weight, KW8Weight, KW8Weight, _i32, _i32, _vp, _vp, _sz, _vp],
+    ),
+    "kw8_moe_route": (ctypes.c_int, [_vp, _i64, _i64, _i64, _i32, KW8Weight, _vp, _vp, _vp, _vp]),
+    "kw8_moe_topk": (ctypes.c_int, [_vp, _i64, _i64, _i32, _vp, _vp, _vp]),
+    "kw8_moe_permute": (ctypes.c_int, [_vp, _i64, _i32, _i64, _i64, _vp, _vp, _vp, _vp, _vp]),
+    "kw8_moe_expert_ffn_workspace_size": (_sz, [_i64, _i64, _i64, _i64]),
+    "kw8_moe_expert_ffn": (
+        ctypes.c_int,
+        [_vp, _i64, _i64, _i64, _i64, _vp, KW8Weight, KW8Weight, KW8Weight, _vp, _vp, _sz, _vp],
+    ),
+    "kw8_moe_combine": (ctypes.c_int, [_vp, _vp, _vp, _i64, _i32, _i64, _vp, _vp]),
+    "kw8_moe_ffn_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i32]),
+    "kw8_moe_ffn": (
+        ctypes.c_int,
+        [
+            _vp, _i64, _i64, _i64, _i64, _i32, _i64,
+            KW8Weight, KW8Weight, KW8Weight, KW8Weight, _vp, _vp, _sz, _vp,
+        ],
+    ),
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+def load() -> ctypes.CDLL:
+    """Load (once) and return the library; raises if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise RuntimeError(
+                    f"{LIB_PATH} is missing: build it with `python -m kappa_b200.build`"
+                )
+            lib = ctypes.CDLL(LIB_PATH)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+    return _lib
+
+
+def last_error() -> str:
+    msg = load().kw8_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(rc: int) -> None:
+    """Raise for a non-zero kw8_status (ValueError for bad arguments)."""
+    if rc == KW8_OK:
+        return
+    msg = last_error()
+    if rc in (KW8_ERR_INVALID_ARG, KW8_ERR_UNSUPPORTED):
+        raise ValueError(f"kappa_w8: {msg}")
+    raise KW8Error(rc, msg)
+
+
+def stream_of(t: torch.Tensor) -> int:
+    """Handle of torch's current stream on ``t``'s device."""
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def device_status(t: torch.Tensor) -> int:
+    """Read and clear the device status word (synchronises the stream)."""
+    v = _i32(0)
+    check(load().kw8_device_status(ctypes.byref(v), stream_of(t)))
+    return int(v.value)
+
+
+def set_option(option: int, value: int) -> None:
+    check(load().kw8_set_option(option, value))
+
+
+def require_cuda(t: torch.Tensor, name: str) -> None:
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (kappa_b200 has no CPU path)")
