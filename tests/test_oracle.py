@@ -1,0 +1,154 @@
+"""The CPU oracle against kappa's semantics (no GPU).
+
+* known answers derived with exact rational arithmetic (tests/golden/*.json);
+* kappa's own checks restated on NumPy inputs:
+  scripts/verify_qwen3_quant.py:13-25 and scripts/verify_qwen3_moe_impls.py:49-117;
+* the committed regression vectors (tests/golden/oracle_small.npz).
+"""
+
+from __future__ import annotations
+
+import json
+import os
+from dataclasses import dataclass, replace
+
+import numpy as np
+import pytest
+
+import oracle as O
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def _load(name):
+    with open(os.path.join(GOLDEN, name)) as f:
+        return json.load(f)
+
+
+@pytest.mark.parametrize("case", _load("kat_quant.json"), ids=lambda c: c["name"])
+def test_quantize_known_answers(case):
+    w = np.asarray(case["w"], dtype=np.float32).reshape(case["shape"])
+    ax = case["per_channel_axis"]
+    qb = O.quantize_weight(w, per_channel_axis=ax)  # bf16 scale (kappa default)
+    qf = O.quantize_weight(w, per_channel_axis=ax, scale_dtype=np.float32)
+    np.testing.assert_array_equal(qb.values.reshape(-1), np.asarray(case["q"], dtype=np.int8))
+    np.testing.assert_array_equal(qf.values, qb.values)
+    if ax is not None:
+        sf = np.moveaxis(np.asarray(qf.scale, dtype=np.float32), ax, -1).reshape(-1)
+        sb = np.moveaxis(np.asarray(qb.scale).astype(np.float32), ax, -1).reshape(-1)
+    else:
+        sf = np.asarray(qf.scale, dtype=np.float32).reshape(-1)
+        sb = np.asarray(qb.scale).astype(np.float32).reshape(-1)
+    np.testing.assert_array_equal(sf, np.asarray(case["scale_f32"], dtype=np.float32))
+    np.testing.assert_array_equal(sb, np.asarray(case["scale_bf16"], dtype=np.float32))
+
+
+@pytest.mark.parametrize("case", _load("kat_topk.json"))
+def test_topk_known_answers(case):
+    idx, w = O.topk_softmax(np.asarray(case["logits"], dtype=np.float32), case["k"])
+    np.testing.assert_array_equal(idx, np.asarray(case["idx"]))
+    np.testing.assert_allclose(np.asarray(w, dtype=np.float32).sum(-1), 1.0, atol=1e-2)
+
+
+@pytest.mark.parametrize("case", _load("kat_permute.json"))
+def test_permute_known_answers(case):
+    order, sizes, slot = O.permute(np.asarray(case["idx"], dtype=np.int32), case["E"])
+    np.testing.assert_array_equal(order, case["order"])
+    np.testing.assert_array_equal(sizes, case["group_sizes"])
+    np.testing.assert_array_equal(slot, case["slot"])
+    # fixed capacity 1: only slot-0 rows survive, still in stable order
+    order1, sizes1, _ = O.permute(np.asarray(case["idx"], dtype=np.int32), case["E"], capacity=1)
+    keep = [i for i in case["order"] if case["slot"][i] < 1]
+    np.testing.assert_array_equal(order1, keep)
+    np.testing.assert_array_equal(sizes1, np.minimum(case["group_sizes"], 1))
+
+
+def test_verify_qwen3_quant_restated():
+    """scripts/verify_qwen3_quant.py:13-25: W8 projection rel L2 <= 0.02 (fp32)."""
+    rng = np.random.default_rng(0)
+    b, t, d, nh, hdim = 2, 5, 64, 4, 16
+    x = rng.standard_normal((b, t, d)).astype(np.float32)
+    w = rng.standard_normal((nh, d, hdim)).astype(np.float32)
+    wq = O.quantize_weight(w, scale_dtype=np.float32)
+    y0 = np.einsum("btd,ndh->btnh", x, w)
+    y1 = np.einsum("btd,ndh->btnh", x, O.to_compute_dtype(wq, np.float32))
+    rel = np.linalg.norm(y0 - y1) / (np.linalg.norm(y0) + np.finfo(np.float32).tiny)
+    assert rel <= 0.02, rel
+
+
+@dataclass(frozen=True)
+class _Cfg:
+    use_moe: bool = True
+    num_experts: int = 8
+    num_experts_per_tok: int = 2
+    moe_impl: str = "gather_einsum"
+    moe_capacity_factor: float = 1.25
+    moe_fixed_capacity_slots: int | None = None
+    moe_ragged_decode_token_threshold: int = 0
+
+
+def _moe_inputs(seed=0, b=2, t=3, d=16, e=8, i=32, dtype=np.float32):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((b, t, d)).astype(np.float32).astype(dtype)
+    router = (rng.standard_normal((d, e)) * 0.02).astype(np.float32)
+    gate = (rng.standard_normal((e, d, i)) * 0.02).astype(np.float32)
+    up = (rng.standard_normal((e, d, i)) * 0.02).astype(np.float32)
+    down = (rng.standard_normal((e, i, d)) * 0.02).astype(np.float32)
+    return x, router, gate, up, down
+
+
+def test_verify_qwen3_moe_impls_restated():
+    """scripts/verify_qwen3_moe_impls.py:49-117 on NumPy inputs (fp32, unquantized)."""
+    x, router, gate, up, down = _moe_inputs()
+    base = _Cfg()
+    y_ref = O.moe_swiglu_ffn(x, router, gate, up, down, cfg=base)
+    y_r = O.moe_swiglu_ffn(x, router, gate, up, down, cfg=replace(base, moe_impl="ragged_jax"))
+    assert np.max(np.abs(y_ref - y_r)) < 1e-4
+    y_c = O.moe_swiglu_ffn(
+        x, router, gate, up, down,
+        cfg=replace(base, moe_impl="fixed_capacity", moe_capacity_factor=1000.0, moe_fixed_capacity_slots=2048),
+    )
+    assert np.max(np.abs(y_ref - y_c)) < 1e-4
+
+
+def test_moe_formulations_agree_w8_bf16():
+    """The W8 bf16 formulations agree within the parity tolerance."""
+    x, router, gate, up, down = _moe_inputs(seed=3, b=1, t=40, d=64, e=8, i=48, dtype=O.BF16)
+    q = [O.quantize_weight(w, per_channel_axis=ax, scale_dtype=np.float32) for w, ax in
+         ((router, 0), (gate, 1), (up, 1), (down, 1))]
+    base = _Cfg(num_experts=8, num_experts_per_tok=2)
+    y_g = O.moe_swiglu_ffn(x, *q, cfg=base).astype(np.float32)
+    y_r = O.moe_swiglu_ffn(x, *q, cfg=replace(base, moe_impl="ragged_jax")).astype(np.float32)
+    err = np.max(np.abs(y_g - y_r)) / np.max(np.abs(y_r))
+    assert err < 1e-2, err
+    # the fp32 reference agrees with both to within kappa's bf16 rounding
+    y32, _, _ = O.moe_reference_f32(x, *q, num_experts=8, k=2)
+    assert np.max(np.abs(y32 - y_r)) / np.max(np.abs(y32)) < 1e-2
+
+
+def test_fixed_capacity_drops_rows():
+    x, router, gate, up, down = _moe_inputs(seed=5, b=1, t=32, d=16, e=4, i=16)
+    cfg = _Cfg(num_experts=4, num_experts_per_tok=2, moe_impl="fixed_capacity", moe_capacity_factor=0.5,
+               moe_fixed_capacity_slots=64)
+    y = O.moe_swiglu_ffn(x, router, gate, up, down, cfg=cfg)
+    y_full = O.moe_swiglu_ffn(x, router, gate, up, down, cfg=replace(cfg, moe_impl="gather_einsum"))
+    assert not np.allclose(y, y_full)  # capacity 8 of ~16 rows per expert drops some
+    # the ragged path with the same slot limit computes the same function
+    cap = O.fixed_capacity_value(0.5, 32, 2, 4, 64)
+    x_flat, idx, w, b, t, d = O.route(x, router, num_experts=4, num_experts_per_tok=2)
+    y_r = O.moe_ragged(x_flat, idx, w, gate, up, down, num_experts=4, b=b, t=t, d=d, capacity=cap)
+    assert np.max(np.abs(y_r - y)) < 1e-4
+
+
+def test_regression_vectors():
+    z = np.load(os.path.join(GOLDEN, "oracle_small.npz"))
+    T, D, I, E, k = (int(v) for v in z["moe_shape"])
+    x = z["moe_x"].view(O.BF16)
+    qr = O.quantize_weight(z["moe_router"], per_channel_axis=0, scale_dtype=np.float32)
+    qg = O.quantize_weight(z["moe_gate"], per_channel_axis=1, scale_dtype=np.float32)
+    qu = O.quantize_weight(z["moe_up"], per_channel_axis=1, scale_dtype=np.float32)
+    qd = O.quantize_weight(z["moe_down"], per_channel_axis=1, scale_dtype=np.float32)
+    x_flat, idx, w, b, t, d = O.route(x, qr, num_experts=E, num_experts_per_tok=k)
+    np.testing.assert_array_equal(idx, z["moe_idx"])
+    y = O.moe_ragged(x_flat, idx, w, qg, qu, qd, num_experts=E, b=b, t=t, d=d)
+    np.testing.assert_array_equal(y.view(np.uint16), z["moe_y"])
