@@ -108,13 +108,14 @@ struct MoeBuffers {
   __nv_bfloat16* w;
   int32_t* sorted_token;
   int32_t* inv_pos;
+  float* sorted_w;
   int32_t* group_sizes;
   int32_t* group_offsets;
   TileEntry* tiles;
   int32_t* num_tiles;
   __nv_bfloat16* xs;
   __nv_bfloat16* h;
-  __nv_bfloat16* ys;
+  float* acc;  // [T][D] fp32 accumulation of the fused combine
 };
 
 struct ExpertBuffers {
@@ -143,20 +144,25 @@ MoeBuffers carve_moe(Carver& c, int64_t T, int64_t D, int64_t I, int64_t E, int 
   b.w = c.take<__nv_bfloat16>(m);
   b.sorted_token = c.take<int32_t>(m);
   b.inv_pos = c.take<int32_t>(m);
+  b.sorted_w = c.take<float>(m);
   b.group_sizes = c.take<int32_t>(E);
   b.group_offsets = c.take<int32_t>(E + 1);
   b.tiles = c.take<TileEntry>(tile_capacity(m, E, 8));
   b.num_tiles = c.take<int32_t>(1);
   b.xs = c.take<__nv_bfloat16>(m * D);
   b.h = c.take<__nv_bfloat16>(m * I);
-  b.ys = c.take<__nv_bfloat16>(m * D);
+  b.acc = c.take<float>(T * D);
   return b;
 }
 
 // Expert FFN over rows already sorted by group (gate/up + SwiGLU, down).
+// With row_token / row_weight the down projection runs the fused combine
+// (EPI_COMBINE_F32) into `ys` = fp32 [T][D] accumulation buffer; otherwise
+// `ys` is bf16 [rows][D].
 int expert_ffn(const void* xs, int64_t rows, int64_t D, int64_t I, int64_t E,
                const int32_t* group_offsets, const kw8_weight& gate, const kw8_weight& up,
-               const kw8_weight& down, void* ys, const ExpertBuffers& b, cudaStream_t stream) {
+               const kw8_weight& down, void* ys, const ExpertBuffers& b, cudaStream_t stream,
+               const int32_t* row_token = nullptr, const float* row_weight = nullptr) {
   const bool simt = use_simt(rows, E);
   const int nt = simt ? kSimtTN : pick_nt(rows, E);
   int rc = launch_build_tiles(group_offsets, E, nt, b.tiles, b.num_tiles, stream);
@@ -175,7 +181,10 @@ int expert_ffn(const void* xs, int64_t rows, int64_t D, int64_t I, int64_t E,
   d.nt = nt;
   d.out = ys;
   d.ld_out = D;
-  return run_gemm(simt, EPI_PLAIN_BF16, down, nullptr, E, D, I, b.h, rows, I, d, stream);
+  d.row_token = row_token;
+  d.row_weight = row_weight;
+  const int mode = row_token != nullptr ? EPI_COMBINE_F32 : EPI_PLAIN_BF16;
+  return run_gemm(simt, mode, down, nullptr, E, D, I, b.h, rows, I, d, stream);
 }
 
 int route(const void* x, int64_t T, int64_t D, int64_t E, int k, const kw8_weight& router,
@@ -382,14 +391,19 @@ int kw8_moe_ffn(const void* x, int64_t T, int64_t D, int64_t I, int64_t E, int32
   rc = kw8::route(x, T, D, E, k, router, b.logits, b.idx, b.w, stream);
   if (rc) return rc;
   rc = launch_permute(b.idx, T, k, E, capacity, b.sorted_token, b.inv_pos, b.group_sizes,
-                      b.group_offsets, stream);
+                      b.group_offsets, stream, b.w, b.sorted_w);
   if (rc) return rc;
   rc = launch_gather(x, b.sorted_token, b.group_offsets + E, m, D, b.xs, stream);
   if (rc) return rc;
+  // The down projection adds w * y of every routed row straight into the
+  // fp32 token buffer (no bf16 rounding of the per-expert outputs, no
+  // [T*k][D] round trip); one conversion pass writes the bf16 output.
+  KW8_CUDA_TRY(cudaMemsetAsync(b.acc, 0, static_cast<size_t>(T * D) * sizeof(float), stream));
   ExpertBuffers eb{b.tiles, b.num_tiles, b.h};
-  rc = expert_ffn(b.xs, m, D, I, E, b.group_offsets, gate, up, down, b.ys, eb, stream);
+  rc = expert_ffn(b.xs, m, D, I, E, b.group_offsets, gate, up, down, b.acc, eb, stream,
+                  b.sorted_token, b.sorted_w);
   if (rc) return rc;
-  return launch_combine(b.ys, b.inv_pos, b.w, T, k, D, out, stream);
+  return launch_f32_to_bf16(b.acc, T * D, out, stream);
 }
 
 }  // extern "C"

@@ -116,6 +116,10 @@ __global__ void __launch_bounds__(256)
         const float g = acc_a[t] * s_a, u = acc_b[t] * s_b;
         const float h = (kMode == EPI_PAIR_GELU) ? gelu_tanh_f(g) * u : silu_f(g) * u;
         static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(h);
+      } else if constexpr (kMode == EPI_COMBINE_F32) {
+        const int r = row0 + t;
+        atomicAdd(static_cast<float*>(p.out) + static_cast<int64_t>(p.row_token[r]) * p.ld_out + f,
+                  acc_a[t] * s_a * p.row_weight[r]);
       } else if constexpr (kMode == EPI_PLAIN_F32) {
         static_cast<float*>(p.out)[o] = acc_a[t] * s_a;
       } else {
@@ -164,6 +168,9 @@ int launch_gemm_simt(int mode, const int8_t* wa, const int8_t* wb, int64_t group
       return launch_simt_mode<EPI_PLAIN_BF16>(wa, wb, x, ldx, args, max_entries, stream);
     case EPI_PLAIN_F32:
       return launch_simt_mode<EPI_PLAIN_F32>(wa, wb, x, ldx, args, max_entries, stream);
+    case EPI_COMBINE_F32:
+      KW8_REQUIRE(args.row_token && args.row_weight, KW8_ERR_INVALID_ARG, "combine needs row maps");
+      return launch_simt_mode<EPI_COMBINE_F32>(wa, wb, x, ldx, args, max_entries, stream);
     default:
       return fail(KW8_ERR_INVALID_ARG, "unknown epilogue mode %d", mode);
   }

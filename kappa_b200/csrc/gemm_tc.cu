@@ -70,6 +70,29 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& p,
           out[static_cast<int64_t>(ti.row0 + tok) * p.ld_out + f] = __float2bfloat16_rn(h);
       }
     }
+  } else if constexpr (kMode == EPI_COMBINE_F32) {
+    const int f = ti.mt * 128 + q * 32 + lane;
+    const bool fvalid = f < p.N_out;
+    const int64_t sidx = static_cast<int64_t>(ti.group) * p.N_out + (fvalid ? f : 0);
+    const float s = scale_at(p.scale_a, p.scale_a_dtype, p.scale_a_pc, sidx);
+    float* out = static_cast<float*>(p.out);
+    for (int c = 0; c < nchunks; ++c) {
+      uint32_t r[32];
+      KW8_TMEM_LD_X32(tmem_lane_base + kTcAccCol + c * 32, r);
+      // Lane l fetches the token and weight of row c*32 + l; shuffles hand
+      // them to the whole warp.
+      const int my_row = c * 32 + lane;
+      const int tok_l = (my_row < nrows) ? p.row_token[ti.row0 + my_row] : 0;
+      const float w_l = (my_row < nrows) ? p.row_weight[ti.row0 + my_row] * s : 0.f;
+      tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int tok = __shfl_sync(0xffffffffu, tok_l, j);
+        const float wj = __shfl_sync(0xffffffffu, w_l, j);
+        if (fvalid && c * 32 + j < nrows)
+          atomicAdd(out + static_cast<int64_t>(tok) * p.ld_out + f, __uint_as_float(r[j]) * wj);
+      }
+    }
   } else {
     const int f = ti.mt * 128 + q * 32 + lane;
     const bool fvalid = f < p.N_out;
@@ -386,6 +409,9 @@ int launch_gemm_tc(int mode, const int8_t* wa, const int8_t* wb, int64_t groups,
       return launch_mode<EPI_PLAIN_BF16>(map_a0, map_a1, map_b, args, grid, stream);
     case EPI_PLAIN_F32:
       return launch_mode<EPI_PLAIN_F32>(map_a0, map_a1, map_b, args, grid, stream);
+    case EPI_COMBINE_F32:
+      KW8_REQUIRE(args.row_token && args.row_weight, KW8_ERR_INVALID_ARG, "combine needs row maps");
+      return launch_mode<EPI_COMBINE_F32>(map_a0, map_a1, map_b, args, grid, stream);
     default:
       return fail(KW8_ERR_INVALID_ARG, "unknown epilogue mode %d", mode);
   }

@@ -41,6 +41,10 @@ enum EpiMode : int {
   EPI_PAIR_SILU = 1,   // h = silu(g) * u, bf16 out, 64 features per tile
   EPI_PLAIN_BF16 = 2,  // y = acc * s, bf16 out, 128 features per tile
   EPI_PLAIN_F32 = 3,   // y = acc * s, fp32 out, 128 features per tile
+  // MoE down projection with the combine fused in: for sorted row p,
+  // out[row_token[p]][f] += row_weight[p] * acc * s (fp32 red.add into an
+  // L2-resident [T][D] buffer), 128 features per tile.
+  EPI_COMBINE_F32 = 4,
 };
 
 __host__ __device__ constexpr bool epi_is_pair(int m) {
@@ -70,9 +74,12 @@ struct GemmArgs {
   const void* scale_b;
   int scale_a_dtype, scale_b_dtype;
   int scale_a_pc, scale_b_pc;
-  // Output [rows][ld_out].
+  // Output [rows][ld_out] ([tokens][ld_out] for EPI_COMBINE_F32).
   void* out;
   int64_t ld_out;
+  // EPI_COMBINE_F32 only: token and routing weight of every sorted row.
+  const int32_t* row_token;
+  const float* row_weight;
 };
 
 constexpr int kTcStages = 4;

@@ -114,7 +114,8 @@ __global__ void topk_softmax_kernel(const float* __restrict__ logits, int T, int
 __global__ void __launch_bounds__(kBlock, 1)
     permute_kernel(const int32_t* __restrict__ idx, int m, int k, int E, int capacity,
                    int32_t* __restrict__ sorted_token, int32_t* __restrict__ inv_pos,
-                   int32_t* __restrict__ group_sizes, int32_t* __restrict__ group_offsets) {
+                   int32_t* __restrict__ group_sizes, int32_t* __restrict__ group_offsets,
+                   const __nv_bfloat16* __restrict__ w, float* __restrict__ sorted_w) {
   extern __shared__ int sm[];
   int* cnt = sm;            // [32][E]
   int* goff = sm + 32 * E;  // [E]
@@ -177,6 +178,7 @@ __global__ void __launch_bounds__(kBlock, 1)
         const int p = goff[e] + slot;
         sorted_token[p] = i / k;
         inv_pos[i] = p;
+        if (sorted_w != nullptr) sorted_w[p] = __bfloat162float(w[i]);
       } else {
         inv_pos[i] = -1;
       }
@@ -271,6 +273,21 @@ __global__ void combine_kernel(const uint4* __restrict__ ys, const int32_t* __re
   }
 }
 
+// out[i] = bf16(acc[i]) for the fp32 accumulation of the fused combine.
+__global__ void f32_to_bf16_kernel(const float4* __restrict__ acc, int64_t n4,
+                                   uint2* __restrict__ out) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float4 v = acc[i];
+    const __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y);
+    const __nv_bfloat162 b = __floats2bfloat162_rn(v.z, v.w);
+    uint2 o;
+    o.x = *reinterpret_cast<const uint32_t*>(&a);
+    o.y = *reinterpret_cast<const uint32_t*>(&b);
+    out[i] = o;
+  }
+}
+
 int grid_for(int64_t n, int threads, int cap) {
   int64_t g = (n + threads - 1) / threads;
   if (g < 1) g = 1;
@@ -298,7 +315,8 @@ int launch_topk(const float* logits, int64_t T, int64_t E, int k, int32_t* idx, 
 
 int launch_permute(const int32_t* idx, int64_t T, int k, int64_t E, int64_t capacity,
                    int32_t* sorted_token, int32_t* inv_pos, int32_t* group_sizes,
-                   int32_t* group_offsets, cudaStream_t stream) {
+                   int32_t* group_offsets, cudaStream_t stream, const void* w,
+                   float* sorted_w) {
   KW8_REQUIRE(E >= 1 && E <= 1024, KW8_ERR_UNSUPPORTED, "permute supports 1..1024 experts");
   KW8_REQUIRE(k >= 1 && T >= 0 && T * k < (1ll << 31), KW8_ERR_INVALID_ARG, "bad T/k");
   const int m = static_cast<int>(T * k);
@@ -313,7 +331,8 @@ int launch_permute(const int32_t* idx, int64_t T, int k, int64_t E, int64_t capa
     attr_set[dev] = true;
   }
   permute_kernel<<<1, kBlock, smem, stream>>>(idx, m, k, static_cast<int>(E), cap, sorted_token,
-                                              inv_pos, group_sizes, group_offsets);
+                                              inv_pos, group_sizes, group_offsets,
+                                              static_cast<const __nv_bfloat16*>(w), sorted_w);
   KW8_CHECK_LAUNCH();
   return KW8_OK;
 }
@@ -347,6 +366,15 @@ int launch_combine(const void* ys, const int32_t* inv_pos, const void* w, int64_
   combine_kernel<<<grid_for(T * vec, 256, 148 * 16), 256, 0, stream>>>(
       static_cast<const uint4*>(ys), inv_pos, static_cast<const __nv_bfloat16*>(w), T, k, vec,
       static_cast<uint4*>(out));
+  KW8_CHECK_LAUNCH();
+  return KW8_OK;
+}
+
+int launch_f32_to_bf16(const float* acc, int64_t n, void* out, cudaStream_t stream) {
+  KW8_REQUIRE(n % 4 == 0, KW8_ERR_UNSUPPORTED, "element count must be a multiple of 4");
+  if (n <= 0) return KW8_OK;
+  f32_to_bf16_kernel<<<grid_for(n / 4, 256, 148 * 16), 256, 0, stream>>>(
+      reinterpret_cast<const float4*>(acc), n / 4, static_cast<uint2*>(out));
   KW8_CHECK_LAUNCH();
   return KW8_OK;
 }

@@ -7,9 +7,13 @@ namespace kw8 {
 
 int launch_topk(const float* logits, int64_t T, int64_t E, int k, int32_t* idx, void* w,
                 cudaStream_t stream);
+// `w` / `sorted_w` (both optional): routing weights [T*k] bf16 and their
+// fp32 copies in sorted-row order, for the fused down-projection combine.
 int launch_permute(const int32_t* idx, int64_t T, int k, int64_t E, int64_t capacity,
                    int32_t* sorted_token, int32_t* inv_pos, int32_t* group_sizes,
-                   int32_t* group_offsets, cudaStream_t stream);
+                   int32_t* group_offsets, cudaStream_t stream, const void* w = nullptr,
+                   float* sorted_w = nullptr);
+int launch_f32_to_bf16(const float* acc, int64_t n, void* out, cudaStream_t stream);
 int launch_build_tiles(const int32_t* group_offsets, int64_t E, int nt, TileEntry* tiles,
                        int32_t* num_tiles, cudaStream_t stream);
 int launch_gather(const void* x, const int32_t* sorted_token, const int32_t* total_rows,

@@ -230,9 +230,9 @@ def moe_ragged(
     buffer); here the k contributions of each token are added in flat order,
     each partial sum rounded, which is XLA-CPU's sequential scatter.
     ``combine_dtype=np.float32`` keeps the combine in fp32 and returns fp32:
-    the fp32 dequantise-then-dot reference of the parity bar.  The expert
-    outputs are cast to x's dtype before the combine either way, as kappa
-    does at ffn_moe.py:213 (``y_sorted[inv].astype(x_flat.dtype)``).  ``capacity``
+    the fp32 dequantise-then-dot reference of the parity bar (kappa's cast
+    of the expert outputs to x's dtype, ffn_moe.py:213, is then skipped
+    too).  ``capacity``
     drops rows whose slot within their expert is >= capacity
     (ffn_moe.py:130-141), for comparing the fixed-capacity path.
     """
@@ -249,10 +249,9 @@ def moe_ragged(
     u = _ragged_dot(sorted_x, wu, group_sizes)
     h = (silu(g) * u).astype(np.float32)
     y_sorted = _ragged_dot(h, wd, group_sizes)
-    xdt = np.asarray(x_flat).dtype
-    dt = np.dtype(combine_dtype) if combine_dtype is not None else xdt
+    dt = np.dtype(combine_dtype) if combine_dtype is not None else np.asarray(x_flat).dtype
     y_orig = np.zeros((bt * k, d), dtype=np.float32)
-    y_orig[order] = _as(y_sorted, xdt)
+    y_orig[order] = _as(y_sorted, dt)
     contrib = _as(y_orig * w_flat.astype(np.float32)[:, None], dt).reshape(bt, k, d)
     out = np.zeros((bt, d), dtype=np.float32)
     for j in range(k):
@@ -373,9 +372,8 @@ def moe_swiglu_ffn(x, router_w, ffn_gate, ffn_up, ffn_down, *, cfg):
 def moe_reference_f32(x, router_w, ffn_gate, ffn_up, ffn_down, *, num_experts: int, k: int,
                       capacity: int | None = None, idx=None, w=None):
     """The parity reference for a MoE layer: kappa's routing (fp32 logits,
-    top-k, bf16 softmax weights), kappa's fp32 dequantise-then-dot expert
-    compute with its cast of each expert output to bf16 (ffn_moe.py:213),
-    and an fp32 combine.  ``idx`` / ``w`` override the routing choice and
+    top-k, bf16 softmax weights) and fp32 dequantise-then-dot expert compute
+    with an fp32 combine.  ``idx`` / ``w`` override the routing choice and
     its weights (to compare expert compute on another implementation's
     routing, checked separately); returns (y fp32 [B, T, D], idx, w)."""
     x = np.asarray(x)
