@@ -54,6 +54,31 @@ int pick_nt(int64_t rows, int64_t groups) {
   return static_cast<int>(nt);
 }
 
+// Token tile for a dense (single-group) tensor-core GEMM with `m_tiles`
+// feature tiles: the fewest waves over the SMs, a tile costing about
+// max(128, nt) (below ~128 tokens a tile is bound by widening its 128x64
+// int8 weight slices, not by the MMAs); ties go to the larger tile.
+int pick_nt_dense(int64_t rows, int64_t m_tiles) {
+  const int forced = g_opt_token_tile.load();
+  if (forced >= 16 && forced <= kTcMaxNT && forced % 16 == 0) return forced;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+  const int64_t sms = num_sms(dev);
+  int best = 16;
+  int64_t best_cost = INT64_MAX;
+  for (int nt = 16; nt <= kTcMaxNT; nt += 16) {
+    const int64_t tiles = (rows + nt - 1) / nt * m_tiles;
+    const int64_t waves = (tiles + sms - 1) / sms;
+    const int64_t cost = waves * (nt > 128 ? nt : 128);
+    if (cost < best_cost || (cost == best_cost && nt > best)) {
+      best = nt;
+      best_cost = cost;
+    }
+    if (nt >= rows) break;
+  }
+  return best;
+}
+
 // GEMV (SIMT) path when groups hold about one GEMV tile of rows or fewer.
 bool use_simt(int64_t rows, int64_t groups) {
   const int p = g_opt_path.load();
@@ -194,7 +219,7 @@ int route(const void* x, int64_t T, int64_t D, int64_t E, int k, const kw8_weigh
   r.tiles = nullptr;
   r.num_tiles = nullptr;
   r.dense_rows = static_cast<int>(T);
-  r.nt = simt ? kSimtTN : pick_nt(T, 1);
+  r.nt = simt ? kSimtTN : pick_nt_dense(T, (E + 127) / 128);
   r.out = logits;
   r.ld_out = E;
   int rc = run_gemm(simt, EPI_PLAIN_F32, router, nullptr, 1, E, D, x, T, D, r, stream);
@@ -284,10 +309,9 @@ int kw8_dense_ffn(const void* x, int64_t T, int64_t D, int64_t H, kw8_weight gat
   __nv_bfloat16* h = c.take<__nv_bfloat16>(T * H);
   KW8_REQUIRE(workspace != nullptr && c.ok, KW8_ERR_WORKSPACE, "dense FFN workspace too small");
   const bool simt = use_simt(T, 1);
-  const int nt = simt ? kSimtTN : pick_nt(T, 1);
   GemmArgs g = base_args(gate, &up);
   g.dense_rows = static_cast<int>(T);
-  g.nt = nt;
+  g.nt = simt ? kSimtTN : pick_nt_dense(T, (H + 63) / 64);
   g.out = h;
   g.ld_out = H;
   rc = run_gemm(simt, act == KW8_ACT_GELU_TANH ? EPI_PAIR_GELU : EPI_PAIR_SILU, gate, &up, 1, H, D,
@@ -295,7 +319,7 @@ int kw8_dense_ffn(const void* x, int64_t T, int64_t D, int64_t H, kw8_weight gat
   if (rc) return rc;
   GemmArgs d = base_args(down, nullptr);
   d.dense_rows = static_cast<int>(T);
-  d.nt = nt;
+  d.nt = simt ? kSimtTN : pick_nt_dense(T, (D + 127) / 128);
   d.out = out;
   d.ld_out = D;
   return run_gemm(simt, out_dtype == KW8_DT_F32 ? EPI_PLAIN_F32 : EPI_PLAIN_BF16, down, nullptr, 1,

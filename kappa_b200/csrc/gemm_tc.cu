@@ -83,14 +83,15 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& p,
       // them to the whole warp.
       const int my_row = c * 32 + lane;
       const int tok_l = (my_row < nrows) ? p.row_token[ti.row0 + my_row] : 0;
-      const float w_l = (my_row < nrows) ? p.row_weight[ti.row0 + my_row] * s : 0.f;
+      const float w_l = (my_row < nrows) ? p.row_weight[ti.row0 + my_row] : 0.f;
       tmem_wait_ld();
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
+        // Row weights are shared by the warp; the scale is this lane's channel.
         const int tok = __shfl_sync(0xffffffffu, tok_l, j);
         const float wj = __shfl_sync(0xffffffffu, w_l, j);
         if (fvalid && c * 32 + j < nrows)
-          atomicAdd(out + static_cast<int64_t>(tok) * p.ld_out + f, __uint_as_float(r[j]) * wj);
+          atomicAdd(out + static_cast<int64_t>(tok) * p.ld_out + f, __uint_as_float(r[j]) * s * wj);
       }
     }
   } else {
@@ -251,19 +252,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mma_commit(&drain_bar);
       mbar_wait(&drain_bar, 0, nullptr);
     }
-  } else if (warp >= 4) {
-    // ------------------------------------------ converters + epilogue ----
+  } else if (warp >= kTcFirstConvWarp && warp < kTcFirstEpiWarp) {
+    // ------------------------------------------------------ converters ----
     const int q = warp & 3;  // TMEM lane quarter of this warp
+    const int grp = (warp - kTcFirstConvWarp) >> 2;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
     const int src_row = kPair ? ((lane < 16) ? (q * 16 + lane) : (64 + q * 16 + lane - 16))
                               : (q * 32 + lane);
     const int swz = (src_row >> 1) & 3;  // 64-byte TMA swizzle of this row
-    int stage = 0;
-    uint32_t phase = 0, acc_phase = 0;
+    uint32_t gs = 0;                     // global stage counter (all tiles)
     bool ok = true;
     for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
-      const TileInfo ti = decode_tile(p, t);
-      for (int kt = 0; kt < k_tiles; ++kt) {
+      for (int kt = 0; kt < k_tiles; ++kt, ++gs) {
+        if ((gs % kTcConvGroups) != static_cast<uint32_t>(grp)) continue;
+        const int stage = static_cast<int>(gs % kTcStages);
+        const uint32_t phase = (gs / kTcStages) & 1u;
         // Warp-uniform outcome: the tcgen05.st below needs all 32 lanes.
         if (!__all_sync(0xffffffffu, mbar_wait(&full_bar[stage], phase, abort_flag))) {
           ok = false;
@@ -284,12 +287,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&aready_bar[stage]);
-        if (++stage == kTcStages) {
-          stage = 0;
-          phase ^= 1u;
-        }
       }
-      if (!ok) break;
+    }
+  } else if (warp >= kTcFirstEpiWarp) {
+    // -------------------------------------------------------- epilogue ----
+    const int q = warp & 3;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+      const TileInfo ti = decode_tile(p, t);
       if (!__all_sync(0xffffffffu, mbar_wait(&acc_full_bar, acc_phase, abort_flag))) break;
       tc_fence_after();
       epilogue_tile<kMode>(p, ti, lane_base, q, lane);

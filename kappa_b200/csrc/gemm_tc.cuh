@@ -5,22 +5,25 @@
 // for every row of every group g (an expert, or the single group of a dense
 // layer).  W is int8 K-major ([groups][N_out][K]); X is bf16 [rows][K].
 //
-// Roles of the 8 warps of a CTA (one CTA per SM, persistent over tiles):
-//   warp 0      TMA producer: int8 weight tile (128 rows x 64 k, 64 B
-//               swizzle) and bf16 token tile (nt rows x 64 k, 128 B swizzle)
-//               per pipeline stage, completion on full[s].
-//   warp 1      TMEM allocator and MMA issuer (one thread): per stage,
-//               4 x tcgen05.mma kind::f16, M=128 (weight rows), N=nt (tokens),
-//               K=16, A read from TMEM, B from shared memory, accumulator in
-//               TMEM; tcgen05.commit frees the stage (empty[s]) and, after
-//               the last k tile, signals the epilogue (acc_full).
-//   warps 4-7   converters + epilogue.  Warp 4+q owns TMEM lanes 32q..32q+31.
-//               Each thread widens its weight row of the stage from int8 to
-//               bf16 (exact) and stores it into the stage's TMEM A slot
-//               (tcgen05.st), then arrives on a_ready[s].  After the last
-//               k tile it reads the fp32 accumulator (tcgen05.ld), applies
-//               the per-channel scale and the activation, and stores bf16 or
-//               fp32 results.
+// Roles of the 16 warps of a CTA (one CTA per SM, persistent over tiles):
+//   warp 0       TMA producer: int8 weight tile (128 rows x 64 k, 64 B
+//                swizzle) and bf16 token tile (nt rows x 64 k, 128 B swizzle)
+//                per pipeline stage, completion on full[s].
+//   warp 1       TMEM allocator and MMA issuer (one thread): per stage,
+//                4 x tcgen05.mma kind::f16, M=128 (weight rows), N=nt
+//                (tokens), K=16, A read from TMEM, B from shared memory,
+//                accumulator in TMEM; tcgen05.commit frees the stage
+//                (empty[s]) and, after the last k tile, signals the
+//                epilogue (acc_full).
+//   warps 4-11   converters, two groups of four that take alternate
+//                stages.  Warp w owns TMEM lanes 32(w%4)..+31; each thread
+//                widens its weight row of the stage from int8 to bf16
+//                (exact) into the stage's TMEM A slot (tcgen05.st), then
+//                the warp arrives on a_ready[s].
+//   warps 12-15  epilogue: read the fp32 accumulator (tcgen05.ld), apply
+//                the per-channel scale and the activation, store; while
+//                they drain a tile the converters already fill the next
+//                tile's stages.
 // Putting the widened weights in TMEM (the "A from TMEM" MMA form) keeps
 // the shared-memory traffic per stage at one int8 read plus the tensor
 // core's read of the token tile; a bf16 copy of the weights never touches
@@ -82,7 +85,7 @@ struct GemmArgs {
   const float* row_weight;
 };
 
-constexpr int kTcStages = 4;
+constexpr int kTcStages = 5;
 constexpr int kTcBK = 64;                          // k per stage
 constexpr int kTcARows = 128;                      // weight rows per tile (M)
 constexpr int kTcATileBytes = kTcARows * kTcBK;    // 8 KB int8
@@ -90,7 +93,10 @@ constexpr int kTcMaxNT = 256;
 constexpr int kTcBTileBytes = kTcMaxNT * kTcBK * 2;  // 32 KB bf16
 constexpr int kTcStageBytes = kTcATileBytes + kTcBTileBytes;
 constexpr int kTcSmemBytes = kTcStages * kTcStageBytes + 1024;  // + align slack
-constexpr int kTcThreads = 256;
+constexpr int kTcThreads = 512;
+constexpr int kTcConvGroups = 2;        // converter groups (4 warps each)
+constexpr int kTcFirstConvWarp = 4;
+constexpr int kTcFirstEpiWarp = 12;
 constexpr uint32_t kTcTmemCols = 512;
 constexpr uint32_t kTcAccCol = 0;      // accumulator: columns [0, 256)
 constexpr uint32_t kTcASlotCol = 256;  // A slot s: columns [256 + 32 s, +32)
