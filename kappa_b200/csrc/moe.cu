@@ -7,6 +7,7 @@ namespace kw8 {
 namespace {
 
 constexpr int kBlock = 1024;
+constexpr int kPermBatch = 16;  // 32-entry steps per lane fetched at once
 
 // Block-wide exclusive scan of one int per thread (blockDim.x == kBlock).
 // Returns the exclusive prefix; *total receives the block sum.
@@ -127,15 +128,26 @@ __global__ void __launch_bounds__(kBlock, 1)
   const int chunk = ((m + 31) / 32 + 31) & ~31;
   const int beg = warp * chunk;
   const int end = min(m, beg + chunk);
-  for (int base = beg; base < end; base += 32) {
-    const int i = base + lane;
-    int e = (i < end) ? idx[i] : -1;
-    if (i < end && (e < 0 || e >= E)) {
-      report(KW8_ERR_INVALID_ARG);
-      e = -1;
+  // Each lane's ids are fetched kPermBatch steps at a time (independent
+  // loads in flight) before the warp walks them.
+  for (int b0 = beg; b0 < end; b0 += 32 * kPermBatch) {
+    int ev[kPermBatch];
+#pragma unroll
+    for (int s = 0; s < kPermBatch; ++s) {
+      const int i = b0 + s * 32 + lane;
+      ev[s] = (i < end) ? idx[i] : -1;
     }
-    const unsigned peers = __match_any_sync(0xffffffffu, e);
-    if (e >= 0 && lane == __ffs(peers) - 1) cnt[warp * E + e] += __popc(peers);
+#pragma unroll
+    for (int s = 0; s < kPermBatch; ++s) {
+      const int i = b0 + s * 32 + lane;
+      int e = ev[s];
+      if (i < end && (e < 0 || e >= E)) {
+        report(KW8_ERR_INVALID_ARG);
+        e = -1;
+      }
+      const unsigned peers = __match_any_sync(0xffffffffu, e);
+      if (e >= 0 && lane == __ffs(peers) - 1) cnt[warp * E + e] += __popc(peers);
+    }
   }
   __syncthreads();
 
@@ -166,28 +178,39 @@ __global__ void __launch_bounds__(kBlock, 1)
   if (threadIdx.x == 0) group_offsets[E] = total_sh;
   __syncthreads();
 
-  for (int base = beg; base < end; base += 32) {
-    const int i = base + lane;
-    int e = (i < end) ? idx[i] : -1;
-    if (e >= E || e < 0) e = -1;
-    const unsigned peers = __match_any_sync(0xffffffffu, e);
-    if (e >= 0) {
-      const int rank = __popc(peers & ((1u << lane) - 1u));
-      const int slot = cnt[warp * E + e] + rank;
-      if (capacity < 0 || slot < capacity) {
-        const int p = goff[e] + slot;
-        sorted_token[p] = i / k;
-        inv_pos[i] = p;
-        if (sorted_w != nullptr) sorted_w[p] = __bfloat162float(w[i]);
-      } else {
+  for (int b0 = beg; b0 < end; b0 += 32 * kPermBatch) {
+    int ev[kPermBatch];
+    float wv[kPermBatch];
+#pragma unroll
+    for (int s = 0; s < kPermBatch; ++s) {
+      const int i = b0 + s * 32 + lane;
+      ev[s] = (i < end) ? idx[i] : -1;
+      wv[s] = (i < end && sorted_w != nullptr) ? __bfloat162float(w[i]) : 0.f;
+    }
+#pragma unroll
+    for (int s = 0; s < kPermBatch; ++s) {
+      const int i = b0 + s * 32 + lane;
+      int e = ev[s];
+      if (e >= E || e < 0) e = -1;
+      const unsigned peers = __match_any_sync(0xffffffffu, e);
+      if (e >= 0) {
+        const int rank = __popc(peers & ((1u << lane) - 1u));
+        const int slot = cnt[warp * E + e] + rank;
+        if (capacity < 0 || slot < capacity) {
+          const int p = goff[e] + slot;
+          sorted_token[p] = i / k;
+          inv_pos[i] = p;
+          if (sorted_w != nullptr) sorted_w[p] = wv[s];
+        } else {
+          inv_pos[i] = -1;
+        }
+      } else if (i < end) {
         inv_pos[i] = -1;
       }
-    } else if (i < end) {
-      inv_pos[i] = -1;
+      __syncwarp();
+      if (e >= 0 && lane == __ffs(peers) - 1) cnt[warp * E + e] += __popc(peers);
+      __syncwarp();
     }
-    __syncwarp();
-    if (e >= 0 && lane == __ffs(peers) - 1) cnt[warp * E + e] += __popc(peers);
-    __syncwarp();
   }
 }
 
