@@ -194,6 +194,30 @@ int kw8_moe_ffn(const void* x, int64_t T, int64_t D, int64_t I, int64_t E,
                 kw8_weight gate, kw8_weight up, kw8_weight down, void* out,
                 void* workspace, size_t workspace_bytes, kw8_stream_t stream);
 
+/* ---------------------------------------------------- no-allocation -- */
+
+/* kw8_moe_ffn with no workspace argument.  No counterpart in kappa (kappa
+ * leaves memory to XLA); it exists for callers that cannot allocate device
+ * memory where they call this library: e.g. a custom-call handler that is
+ * given only its input and output buffers and no scratch allocator, or a
+ * program whose device memory belongs to another allocator it cannot reach
+ * from the call site.
+ * The scratch is a fixed 16 MiB array inside the library; every GPU that
+ * loads the library holds it until the process exits.  Shapes whose
+ * kw8_moe_ffn_workspace_size() exceeds 16 MiB are rejected with
+ * KW8_ERR_WORKSPACE (at the Qwen3-30B-A3B layer shape, D=2048, I=768,
+ * E=128, k=8, that is above about 300 tokens).  The first call on each
+ * device looks up the array's device address (cudaGetSymbolAddress) and
+ * caches it; make that first call before any stream capture.  Every call
+ * on a device shares the one array, which keeps the last call's contents
+ * (nothing in it needs to start at zero; the call clears what must), so
+ * calls that overlap on the same GPU (other streams or threads) race and
+ * corrupt each other's results.  Allocates nothing.                        */
+int kw8_moe_ffn_noalloc(const void* x, int64_t T, int64_t D, int64_t I,
+                        int64_t E, int32_t k, int64_t capacity,
+                        kw8_weight router, kw8_weight gate, kw8_weight up,
+                        kw8_weight down, void* out, kw8_stream_t stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -95,6 +95,10 @@ SIGNATURES: dict[str, tuple] = {
             KW8Weight, KW8Weight, KW8Weight, KW8Weight, _vp, _vp, _sz, _vp,
         ],
     ),
+    "kw8_moe_ffn_noalloc": (
+        ctypes.c_int,
+        [_vp, _i64, _i64, _i64, _i64, _i32, _i64, KW8Weight, KW8Weight, KW8Weight, KW8Weight, _vp, _vp],
+    ),
 }
 
 _lock = threading.Lock()

@@ -7,3 +7,4 @@
 #include "gemm_simt.cu"
 #include "moe.cu"
 #include "api.cu"
+#include "noalloc.cu"
