@@ -41,23 +41,25 @@ struct Carver {
 
 int round16(int64_t v) { return static_cast<int>((v + 15) & ~int64_t(15)); }
 
-// Token tile for the tensor-core path: about 1.5x the mean rows per group,
-// 16..256.  Small tiles keep the token TMA box (loaded in full every
-// stage) from dwarfing the weight tile when groups are small.
+// Token tile for the grouped tensor-core path: about 1.5x the mean rows per
+// group, 16..160.  Small tiles keep the token TMA box (loaded in full every
+// stage) from dwarfing the weight tile when groups are small; the 160 cap
+// keeps two accumulators in TMEM (groups are split into near-equal tiles).
 int pick_nt(int64_t rows, int64_t groups) {
   const int forced = g_opt_token_tile.load();
   if (forced >= 16 && forced <= kTcMaxNT && forced % 16 == 0) return forced;
   const int64_t mean = (rows + groups - 1) / (groups > 0 ? groups : 1);
   int64_t nt = round16((mean * 3 + 1) / 2);
   if (nt < 16) nt = 16;
-  if (nt > kTcMaxNT) nt = kTcMaxNT;
+  if (nt > kTcMaxDoubleBufferNT) nt = kTcMaxDoubleBufferNT;
   return static_cast<int>(nt);
 }
 
 // Token tile for a dense (single-group) tensor-core GEMM with `m_tiles`
 // feature tiles: the fewest waves over the SMs, a tile costing about
 // max(128, nt) (below ~128 tokens a tile is bound by widening its 128x64
-// int8 weight slices, not by the MMAs); ties go to the larger tile.
+// int8 weight slices, not by the MMAs); ties go to the larger tile; at most
+// 160 so the accumulator is double buffered.
 int pick_nt_dense(int64_t rows, int64_t m_tiles) {
   const int forced = g_opt_token_tile.load();
   if (forced >= 16 && forced <= kTcMaxNT && forced % 16 == 0) return forced;
@@ -66,7 +68,7 @@ int pick_nt_dense(int64_t rows, int64_t m_tiles) {
   const int64_t sms = num_sms(dev);
   int best = 16;
   int64_t best_cost = INT64_MAX;
-  for (int nt = 16; nt <= kTcMaxNT; nt += 16) {
+  for (int nt = 16; nt <= kTcMaxDoubleBufferNT; nt += 16) {
     const int64_t tiles = (rows + nt - 1) / nt * m_tiles;
     const int64_t waves = (tiles + sms - 1) / sms;
     const int64_t cost = waves * (nt > 128 ? nt : 128);

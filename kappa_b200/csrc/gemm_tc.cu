@@ -32,11 +32,32 @@ __device__ __forceinline__ float scale_at(const void* s, int dtype, int pc,
   return load_scale(s, dtype, pc ? idx : 0);
 }
 
+// 4x4 transpose within each group of four lanes: lane 4g+p holds a[i] =
+// M[p][i] on entry and M[i][p] on exit (two xor-shuffle rounds, one shuffle
+// per element).
+__device__ __forceinline__ void transpose4x4(float (&a)[4], int lane) {
+  const bool b0 = (lane & 1) != 0, b1 = (lane & 2) != 0;
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {  // 2x2 blocks: exchange elements whose bit 0 differs from p's
+    const int j = 2 * k + (b0 ? 0 : 1);
+    const float send = b0 ? a[2 * k] : a[2 * k + 1];
+    const float got = __shfl_xor_sync(0xffffffffu, send, 1);
+    if (b0) a[2 * k] = got; else a[2 * k + 1] = got;
+    (void)j;
+  }
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {  // blocks of 2x2: exchange elements whose bit 1 differs
+    const float send = b1 ? a[k] : a[k + 2];
+    const float got = __shfl_xor_sync(0xffffffffu, send, 2);
+    if (b1) a[k] = got; else a[k + 2] = got;
+  }
+}
+
+// Epilogue of one tile for one warp: TMEM lane quarter q, 32-column chunks
+// c = sub, sub + 2, ... of the accumulator at column acc_col.
 template <int kMode>
-__device__ __forceinline__ void epilogue_tile(const GemmArgs& p,
-                                              const TileInfo& ti,
-                                              uint32_t tmem_lane_base, int q,
-                                              int lane) {
+__device__ __forceinline__ void epilogue_tile(const GemmArgs& p, const TileInfo& ti,
+                                              uint32_t acc_lane_base, int q, int sub, int lane) {
   constexpr bool kPair = epi_is_pair(kMode);
   const int nrows = ti.nrows;
   const int nchunks = (nrows + 31) >> 5;
@@ -48,9 +69,9 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& p,
                         ? scale_at(p.scale_a, p.scale_a_dtype, p.scale_a_pc, sidx)
                         : scale_at(p.scale_b, p.scale_b_dtype, p.scale_b_pc, sidx);
     __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
-    for (int c = 0; c < nchunks; ++c) {
+    for (int c = sub; c < nchunks; c += 2) {
       uint32_t r[32];
-      KW8_TMEM_LD_X32(tmem_lane_base + kTcAccCol + c * 32, r);
+      KW8_TMEM_LD_X32(acc_lane_base + c * 32, r);
       tmem_wait_ld();
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
@@ -71,27 +92,36 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& p,
       }
     }
   } else if constexpr (kMode == EPI_COMBINE_F32) {
-    const int f = ti.mt * 128 + q * 32 + lane;
+    const int fbase = ti.mt * 128 + q * 32;
+    const int f = fbase + lane;
     const bool fvalid = f < p.N_out;
     const int64_t sidx = static_cast<int64_t>(ti.group) * p.N_out + (fvalid ? f : 0);
     const float s = scale_at(p.scale_a, p.scale_a_dtype, p.scale_a_pc, sidx);
+    const int f4 = fbase + (lane & ~3);  // first of the 4 features this lane adds
+    const bool f4valid = f4 < p.N_out;   // N_out % 4 == 0 (checked by the launcher)
     float* out = static_cast<float*>(p.out);
-    for (int c = 0; c < nchunks; ++c) {
+    for (int c = sub; c < nchunks; c += 2) {
       uint32_t r[32];
-      KW8_TMEM_LD_X32(tmem_lane_base + kTcAccCol + c * 32, r);
-      // Lane l fetches the token and weight of row c*32 + l; shuffles hand
-      // them to the whole warp.
+      KW8_TMEM_LD_X32(acc_lane_base + c * 32, r);
+      // Lane l fetches the token and routing weight of row c*32 + l.
       const int my_row = c * 32 + lane;
       const int tok_l = (my_row < nrows) ? p.row_token[ti.row0 + my_row] : 0;
       const float w_l = (my_row < nrows) ? p.row_weight[ti.row0 + my_row] : 0.f;
       tmem_wait_ld();
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        // Row weights are shared by the warp; the scale is this lane's channel.
-        const int tok = __shfl_sync(0xffffffffu, tok_l, j);
-        const float wj = __shfl_sync(0xffffffffu, w_l, j);
-        if (fvalid && c * 32 + j < nrows)
-          atomicAdd(out + static_cast<int64_t>(tok) * p.ld_out + f, __uint_as_float(r[j]) * s * wj);
+      for (int b = 0; b < 8; ++b) {
+        // Rows 4b..4b+3 of the chunk; after the transpose lane 4g+pl holds
+        // features f4..f4+3 of row 4b+pl, added with one 16-byte atomic.
+        float a[4] = {__uint_as_float(r[4 * b]) * s, __uint_as_float(r[4 * b + 1]) * s,
+                      __uint_as_float(r[4 * b + 2]) * s, __uint_as_float(r[4 * b + 3]) * s};
+        transpose4x4(a, lane);
+        const int src = 4 * b + (lane & 3);
+        const int tok = __shfl_sync(0xffffffffu, tok_l, src);
+        const float wr = __shfl_sync(0xffffffffu, w_l, src);
+        if (f4valid && c * 32 + src < nrows) {
+          float4 v = make_float4(a[0] * wr, a[1] * wr, a[2] * wr, a[3] * wr);
+          atomicAdd(reinterpret_cast<float4*>(out + static_cast<int64_t>(tok) * p.ld_out + f4), v);
+        }
       }
     }
   } else {
@@ -99,9 +129,9 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& p,
     const bool fvalid = f < p.N_out;
     const int64_t sidx = static_cast<int64_t>(ti.group) * p.N_out + (fvalid ? f : 0);
     const float s = scale_at(p.scale_a, p.scale_a_dtype, p.scale_a_pc, sidx);
-    for (int c = 0; c < nchunks; ++c) {
+    for (int c = sub; c < nchunks; c += 2) {
       uint32_t r[32];
-      KW8_TMEM_LD_X32(tmem_lane_base + kTcAccCol + c * 32, r);
+      KW8_TMEM_LD_X32(acc_lane_base + c * 32, r);
       tmem_wait_ld();
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
@@ -133,8 +163,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __shared__ uint64_t full_bar[kTcStages];
   __shared__ uint64_t aready_bar[kTcStages];
   __shared__ uint64_t empty_bar[kTcStages];
-  __shared__ uint64_t acc_full_bar;
-  __shared__ uint64_t acc_empty_bar;
+  __shared__ uint64_t acc_full_bar[2];
+  __shared__ uint64_t acc_empty_bar[2];
   __shared__ uint64_t drain_bar;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_sh;
@@ -148,8 +178,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&aready_bar[s], 4);
       mbar_init(&empty_bar[s], 1);
     }
-    mbar_init(&acc_full_bar, 1);
-    mbar_init(&acc_empty_bar, 4);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full_bar[b], 1);
+      mbar_init(&acc_empty_bar[b], kTcEpiWarps);
+    }
     mbar_init(&drain_bar, 1);
     abort_sh = 0;
     fence_barrier_init();
@@ -165,6 +197,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   tc_fence_after();
   const uint32_t tmem = tmem_base_sh;
   volatile int* abort_flag = &abort_sh;
+
+  // TMEM plan: accumulator buffers of acc_cols columns, then the A slots.
+  // Two buffers only when both plus the A slots fit in the allocation, so
+  // every column used stays below kTcTmemCols (nt <= 256 keeps the
+  // single-buffer plan at 256 + 160 columns).
+  const uint32_t acc_cols = static_cast<uint32_t>((p.nt + 31) & ~31);
+  const int nbuf = (2 * acc_cols + kTcStages * 32 <= kTcTmemCols) ? 2 : 1;
+  const uint32_t a_col0 = static_cast<uint32_t>(nbuf) * acc_cols;
 
   const int n_entries =
       (p.tiles == nullptr) ? (p.dense_rows + p.nt - 1) / p.nt : *p.num_tiles;
@@ -214,15 +254,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // --------------------------------------------------- MMA issuer ----
-      int stage = 0;
-      uint32_t phase = 0, acc_phase = 0;
+      int stage = 0, nt_done = 0;
+      uint32_t phase = 0, acc_phase = 0;  // acc_phase bit b: phase of buffer b
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
+      for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x, ++nt_done) {
         const TileInfo ti = decode_tile(p, t);
+        const int ab = nt_done % nbuf;
         const uint32_t n_mma = static_cast<uint32_t>(max(16, (ti.nrows + 15) & ~15));
         const uint32_t idesc = idesc_bf16_f32(128, n_mma);
-        if (!mbar_wait(&acc_empty_bar, acc_phase ^ 1u, abort_flag)) break;
+        if (!mbar_wait(&acc_empty_bar[ab], ((acc_phase >> ab) & 1u) ^ 1u, abort_flag)) break;
         tc_fence_after();
+        const uint32_t d_tmem = tmem + static_cast<uint32_t>(ab) * acc_cols;
         for (int kt = 0; kt < k_tiles; ++kt) {
           if (!mbar_wait(&full_bar[stage], phase, abort_flag) ||
               !mbar_wait(&aready_bar[stage], phase, abort_flag)) {
@@ -231,12 +273,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
           tc_fence_after();
           const uint32_t b_addr = smem_u32(smem + stage * kTcStageBytes + kTcATileBytes);
-          const uint32_t a_tmem = tmem + kTcASlotCol + stage * 32;
+          const uint32_t a_tmem = tmem + a_col0 + stage * 32;
 #pragma unroll
           for (int kk = 0; kk < kTcBK / 16; ++kk) {
             const uint64_t bdesc = smem_desc_kmajor_sw128(b_addr + kk * 32);
-            mma_ts_bf16(tmem + kTcAccCol, a_tmem + kk * 8, bdesc, idesc,
-                        (kt | kk) != 0 ? 1u : 0u);
+            mma_ts_bf16(d_tmem, a_tmem + kk * 8, bdesc, idesc, (kt | kk) != 0 ? 1u : 0u);
           }
           mma_commit(&empty_bar[stage]);
           if (++stage == kTcStages) {
@@ -245,8 +286,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
         }
         if (!ok) break;
-        mma_commit(&acc_full_bar);
-        acc_phase ^= 1u;
+        mma_commit(&acc_full_bar[ab]);
+        acc_phase ^= 1u << ab;
       }
       // Drain: every MMA issued above has completed once this arrives.
       mma_commit(&drain_bar);
@@ -282,7 +323,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           i8x4_to_bf16x4(w.z, v[c * 8 + 4], v[c * 8 + 5]);
           i8x4_to_bf16x4(w.w, v[c * 8 + 6], v[c * 8 + 7]);
         }
-        KW8_TMEM_ST_X32(lane_base + kTcASlotCol + stage * 32, v);
+        KW8_TMEM_ST_X32(lane_base + a_col0 + stage * 32, v);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
@@ -292,17 +333,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   } else if (warp >= kTcFirstEpiWarp) {
     // -------------------------------------------------------- epilogue ----
     const int q = warp & 3;
+    const int sub = (warp - kTcFirstEpiWarp) >> 2;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
     uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+    int nt_done = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++nt_done) {
       const TileInfo ti = decode_tile(p, t);
-      if (!__all_sync(0xffffffffu, mbar_wait(&acc_full_bar, acc_phase, abort_flag))) break;
+      const int ab = nt_done % nbuf;
+      if (!__all_sync(0xffffffffu,
+                      mbar_wait(&acc_full_bar[ab], (acc_phase >> ab) & 1u, abort_flag)))
+        break;
       tc_fence_after();
-      epilogue_tile<kMode>(p, ti, lane_base, q, lane);
+      epilogue_tile<kMode>(p, ti, lane_base + static_cast<uint32_t>(ab) * acc_cols, q, sub, lane);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty_bar);
-      acc_phase ^= 1u;
+      if (lane == 0) mbar_arrive(&acc_empty_bar[ab]);
+      acc_phase ^= 1u << ab;
     }
   }
 
@@ -417,6 +463,9 @@ int launch_gemm_tc(int mode, const int8_t* wa, const int8_t* wb, int64_t groups,
       return launch_mode<EPI_PLAIN_F32>(map_a0, map_a1, map_b, args, grid, stream);
     case EPI_COMBINE_F32:
       KW8_REQUIRE(args.row_token && args.row_weight, KW8_ERR_INVALID_ARG, "combine needs row maps");
+      KW8_REQUIRE(N_out % 4 == 0 && args.ld_out % 4 == 0 &&
+                      (reinterpret_cast<uintptr_t>(args.out) & 15) == 0,
+                  KW8_ERR_UNSUPPORTED, "fused combine needs D %% 4 == 0 and a 16-byte aligned output");
       return launch_mode<EPI_COMBINE_F32>(map_a0, map_a1, map_b, args, grid, stream);
     default:
       return fail(KW8_ERR_INVALID_ARG, "unknown epilogue mode %d", mode);

@@ -5,25 +5,28 @@
 // for every row of every group g (an expert, or the single group of a dense
 // layer).  W is int8 K-major ([groups][N_out][K]); X is bf16 [rows][K].
 //
-// Roles of the 16 warps of a CTA (one CTA per SM, persistent over tiles):
+// Roles of the 20 warps of a CTA (one CTA per SM, persistent over tiles):
 //   warp 0       TMA producer: int8 weight tile (128 rows x 64 k, 64 B
 //                swizzle) and bf16 token tile (nt rows x 64 k, 128 B swizzle)
 //                per pipeline stage, completion on full[s].
 //   warp 1       TMEM allocator and MMA issuer (one thread): per stage,
-//                4 x tcgen05.mma kind::f16, M=128 (weight rows), N=nt
-//                (tokens), K=16, A read from TMEM, B from shared memory,
-//                accumulator in TMEM; tcgen05.commit frees the stage
-//                (empty[s]) and, after the last k tile, signals the
-//                epilogue (acc_full).
+//                4 x tcgen05.mma kind::f16, M=128 (weight rows), N=rows of
+//                the tile rounded to 16, K=16, A read from TMEM, B from
+//                shared memory, accumulator in TMEM; tcgen05.commit frees the
+//                stage (empty[s]) and, after the last k tile, hands the
+//                accumulator to the epilogue (acc_full[b]).
 //   warps 4-11   converters, two groups of four that take alternate
 //                stages.  Warp w owns TMEM lanes 32(w%4)..+31; each thread
 //                widens its weight row of the stage from int8 to bf16
 //                (exact) into the stage's TMEM A slot (tcgen05.st), then
 //                the warp arrives on a_ready[s].
-//   warps 12-15  epilogue: read the fp32 accumulator (tcgen05.ld), apply
-//                the per-channel scale and the activation, store; while
-//                they drain a tile the converters already fill the next
-//                tile's stages.
+//   warps 12-19  epilogue, two warps per TMEM lane quarter taking alternate
+//                32-column chunks: read the fp32 accumulator (tcgen05.ld),
+//                apply the per-channel scale and the activation, store.
+// When the token tile is at most 160 columns the accumulator is double
+// buffered in TMEM (2 x 160 + 5 A slots x 32 = 480 of 512 columns), so the
+// epilogue of one tile runs under the MMAs of the next; wider tiles use one
+// accumulator and the MMA waits for the epilogue.
 // Putting the widened weights in TMEM (the "A from TMEM" MMA form) keeps
 // the shared-memory traffic per stage at one int8 read plus the tensor
 // core's read of the token tile; a bf16 copy of the weights never touches
@@ -93,13 +96,18 @@ constexpr int kTcMaxNT = 256;
 constexpr int kTcBTileBytes = kTcMaxNT * kTcBK * 2;  // 32 KB bf16
 constexpr int kTcStageBytes = kTcATileBytes + kTcBTileBytes;
 constexpr int kTcSmemBytes = kTcStages * kTcStageBytes + 1024;  // + align slack
-constexpr int kTcThreads = 512;
+constexpr int kTcThreads = 640;
 constexpr int kTcConvGroups = 2;        // converter groups (4 warps each)
 constexpr int kTcFirstConvWarp = 4;
 constexpr int kTcFirstEpiWarp = 12;
+constexpr int kTcEpiWarps = 8;          // two per TMEM lane quarter
+constexpr int kTcMaxDoubleBufferNT = 160;  // widest tile with two accumulators
+static_assert(2 * ((kTcMaxDoubleBufferNT + 31) / 32 * 32) + kTcStages * 32 <= 512,
+              "two accumulators and the A slots must fit in 512 TMEM columns");
+static_assert(kTcMaxNT + kTcStages * 32 <= 512, "one accumulator and the A slots must fit");
 constexpr uint32_t kTcTmemCols = 512;
-constexpr uint32_t kTcAccCol = 0;      // accumulator: columns [0, 256)
-constexpr uint32_t kTcASlotCol = 256;  // A slot s: columns [256 + 32 s, +32)
+// TMEM columns: accumulator buffer b at [b * acc_cols, +acc_cols) with
+// acc_cols = nt rounded up to 32; A slot s at [nbuf * acc_cols + 32 s, +32).
 
 int launch_gemm_tc(int mode, const int8_t* wa, const int8_t* wb, int64_t groups,
                    int64_t N_out, int64_t K, const void* x, int64_t x_rows,

@@ -214,7 +214,8 @@ __global__ void __launch_bounds__(kBlock, 1)
   }
 }
 
-// Tile table: every group's rows cut into runs of at most `nt` rows.
+// Tile table: every group's rows cut into ceil(n / nt) runs of near-equal
+// length (at most `nt` rows each).
 __global__ void __launch_bounds__(kBlock, 1)
     build_tiles_kernel(const int32_t* __restrict__ group_offsets, int E, int nt,
                        TileEntry* __restrict__ tiles, int32_t* __restrict__ num_tiles) {
@@ -231,11 +232,14 @@ __global__ void __launch_bounds__(kBlock, 1)
     const int cnt = (n + nt - 1) / nt;
     int tot;
     const int off = block_exclusive_scan(cnt, &tot) + carry_sh;
+    // Balanced split: tile j covers rows [n*j/cnt, n*(j+1)/cnt), <= nt each.
     for (int j = 0; j < cnt; ++j) {
+      const int lo = static_cast<int>(static_cast<int64_t>(n) * j / cnt);
+      const int hi = static_cast<int>(static_cast<int64_t>(n) * (j + 1) / cnt);
       TileEntry te;
       te.group = e;
-      te.row0 = start + j * nt;
-      te.nrows = min(nt, n - j * nt);
+      te.row0 = start + lo;
+      te.nrows = hi - lo;
       te.pad = 0;
       tiles[off + j] = te;
     }
