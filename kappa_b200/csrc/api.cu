@@ -42,9 +42,9 @@ struct Carver {
 int round16(int64_t v) { return static_cast<int>((v + 15) & ~int64_t(15)); }
 
 // Token tile for the grouped tensor-core path: about 1.5x the mean rows per
-// group, 16..160.  Small tiles keep the token TMA box (loaded in full every
-// stage) from dwarfing the weight tile when groups are small; the 160 cap
-// keeps two accumulators in TMEM (groups are split into near-equal tiles).
+// group, 16..128.  Small tiles keep the token TMA box (loaded in full every
+// stage) from dwarfing the weight tile when groups are small; 128-token tiles
+// keep four pipeline stages per ring (groups are split into near-equal tiles).
 int pick_nt(int64_t rows, int64_t groups) {
   const int forced = g_opt_token_tile.load();
   if (forced >= 16 && forced <= kTcMaxNT && forced % 16 == 0) return forced;
@@ -59,7 +59,7 @@ int pick_nt(int64_t rows, int64_t groups) {
 // feature tiles: the fewest waves over the SMs, a tile costing about
 // max(128, nt) (below ~128 tokens a tile is bound by widening its 128x64
 // int8 weight slices, not by the MMAs); ties go to the larger tile; at most
-// 160 so the accumulator is double buffered.
+// 128.
 int pick_nt_dense(int64_t rows, int64_t m_tiles) {
   const int forced = g_opt_token_tile.load();
   if (forced >= 16 && forced <= kTcMaxNT && forced % 16 == 0) return forced;

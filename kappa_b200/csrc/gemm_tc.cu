@@ -53,11 +53,11 @@ __device__ __forceinline__ void transpose4x4(float (&a)[4], int lane) {
   }
 }
 
-// Epilogue of one tile for one warp: TMEM lane quarter q, 32-column chunks
-// c = sub, sub + 2, ... of the accumulator at column acc_col.
+// Epilogue of one tile for one warp: TMEM lane quarter q, every 32-column
+// chunk of the accumulator at acc_lane_base.
 template <int kMode>
 __device__ __forceinline__ void epilogue_tile(const GemmArgs& p, const TileInfo& ti,
-                                              uint32_t acc_lane_base, int q, int sub, int lane) {
+                                              uint32_t acc_lane_base, int q, int lane) {
   constexpr bool kPair = epi_is_pair(kMode);
   const int nrows = ti.nrows;
   const int nchunks = (nrows + 31) >> 5;
@@ -69,7 +69,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& p, const TileInfo&
                         ? scale_at(p.scale_a, p.scale_a_dtype, p.scale_a_pc, sidx)
                         : scale_at(p.scale_b, p.scale_b_dtype, p.scale_b_pc, sidx);
     __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
-    for (int c = sub; c < nchunks; c += 2) {
+    for (int c = 0; c < nchunks; ++c) {
       uint32_t r[32];
       KW8_TMEM_LD_X32(acc_lane_base + c * 32, r);
       tmem_wait_ld();
@@ -100,7 +100,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& p, const TileInfo&
     const int f4 = fbase + (lane & ~3);  // first of the 4 features this lane adds
     const bool f4valid = f4 < p.N_out;   // N_out % 4 == 0 (checked by the launcher)
     float* out = static_cast<float*>(p.out);
-    for (int c = sub; c < nchunks; c += 2) {
+    for (int c = 0; c < nchunks; ++c) {
       uint32_t r[32];
       KW8_TMEM_LD_X32(acc_lane_base + c * 32, r);
       // Lane l fetches the token and routing weight of row c*32 + l.
@@ -129,7 +129,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& p, const TileInfo&
     const bool fvalid = f < p.N_out;
     const int64_t sidx = static_cast<int64_t>(ti.group) * p.N_out + (fvalid ? f : 0);
     const float s = scale_at(p.scale_a, p.scale_a_dtype, p.scale_a_pc, sidx);
-    for (int c = sub; c < nchunks; c += 2) {
+    for (int c = 0; c < nchunks; ++c) {
       uint32_t r[32];
       KW8_TMEM_LD_X32(acc_lane_base + c * 32, r);
       tmem_wait_ld();
@@ -160,12 +160,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
 
-  __shared__ uint64_t full_bar[kTcStages];
-  __shared__ uint64_t aready_bar[kTcStages];
-  __shared__ uint64_t empty_bar[kTcStages];
-  __shared__ uint64_t acc_full_bar[2];
-  __shared__ uint64_t acc_empty_bar[2];
-  __shared__ uint64_t drain_bar;
+  __shared__ uint64_t full_bar[kTcRings][kTcMaxStages];
+  __shared__ uint64_t aready_bar[kTcRings][kTcMaxStages];
+  __shared__ uint64_t empty_bar[kTcRings][kTcMaxStages];
+  __shared__ uint64_t acc_full_bar[kTcRings][2];
+  __shared__ uint64_t acc_empty_bar[kTcRings][2];
+  __shared__ uint64_t drain_bar[kTcRings];
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_sh;
 
@@ -173,16 +173,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kTcStages; ++s) {
-      mbar_init(&full_bar[s], 1);
-      mbar_init(&aready_bar[s], 4);
-      mbar_init(&empty_bar[s], 1);
+    for (int r = 0; r < kTcRings; ++r) {
+      for (int s = 0; s < p.stages; ++s) {
+        mbar_init(&full_bar[r][s], 1);
+        mbar_init(&aready_bar[r][s], 4);
+        mbar_init(&empty_bar[r][s], 1);
+      }
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(&acc_full_bar[r][b], 1);
+        mbar_init(&acc_empty_bar[r][b], kTcEpiWarpsPerRing);
+      }
+      mbar_init(&drain_bar[r], 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&acc_full_bar[b], 1);
-      mbar_init(&acc_empty_bar[b], kTcEpiWarps);
-    }
-    mbar_init(&drain_bar, 1);
     abort_sh = 0;
     fence_barrier_init();
   }
@@ -191,27 +193,50 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (kPair) tma_prefetch_desc(&map_a1);
     tma_prefetch_desc(&map_b);
   }
-  if (warp == 1) tmem_alloc(&tmem_base_sh, kTcTmemCols);
+  if (warp == 2) tmem_alloc(&tmem_base_sh, kTcTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = tmem_base_sh;
   volatile int* abort_flag = &abort_sh;
 
-  // TMEM plan: accumulator buffers of acc_cols columns, then the A slots.
-  // Two buffers only when both plus the A slots fit in the allocation, so
-  // every column used stays below kTcTmemCols (nt <= 256 keeps the
-  // single-buffer plan at 256 + 160 columns).
-  const uint32_t acc_cols = static_cast<uint32_t>((p.nt + 31) & ~31);
-  const int nbuf = (2 * acc_cols + kTcStages * 32 <= kTcTmemCols) ? 2 : 1;
+  // Plan from the launcher (tc_plan), per ring.
+  const int kStages = p.stages;
+  const int stage_bytes = p.stage_bytes;
+  const uint32_t acc_cols = static_cast<uint32_t>(p.acc_cols);
+  const int nbuf = p.nbuf;
   const uint32_t a_col0 = static_cast<uint32_t>(nbuf) * acc_cols;
 
   const int n_entries =
       (p.tiles == nullptr) ? (p.dense_rows + p.nt - 1) / p.nt : *p.num_tiles;
   const int total_tiles = n_entries * p.m_tiles;
   const int k_tiles = (p.K + kTcBK - 1) / kTcBK;
+  const int tile_step = gridDim.x * kTcRings;
 
-  if (warp == 0) {
+  // Role and ring of this warp.
+  int ring, role;  // role: 0 producer, 1 MMA, 2 converter, 3 epilogue
+  if (warp < 2) {
+    role = 0;
+    ring = warp;
+  } else if (warp < 4) {
+    role = 1;
+    ring = warp - 2;
+  } else if (warp < kTcFirstEpiWarp) {
+    role = 2;
+    ring = (warp - kTcFirstConvWarp) >> 2;
+  } else {
+    role = 3;
+    ring = (warp - kTcFirstEpiWarp) >> 2;
+  }
+  uint8_t* rsmem = smem + ring * kStages * stage_bytes;
+  const uint32_t rtmem = tmem_base_sh + static_cast<uint32_t>(ring) * kTcRingTmemCols;
+  uint64_t* full = full_bar[ring];
+  uint64_t* aready = aready_bar[ring];
+  uint64_t* empty = empty_bar[ring];
+  uint64_t* acc_full = acc_full_bar[ring];
+  uint64_t* acc_empty = acc_empty_bar[ring];
+  const int t0 = blockIdx.x * kTcRings + ring;
+
+  if (role == 0) {
     if (lane == 0) {
       // ------------------------------------------------ TMA producer ----
       const uint32_t tx_bytes = kTcATileBytes + static_cast<uint32_t>(p.nt) * kTcBK * 2;
@@ -219,27 +244,27 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       uint32_t phase = 0;
       uint32_t issued_mask = 0, issued_parity = 0;
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
+      for (int t = t0; ok && t < total_tiles; t += tile_step) {
         const TileInfo ti = decode_tile(p, t);
         const int a_row = ti.group * p.N_out + ti.mt * (kPair ? 64 : 128);
         for (int kt = 0; kt < k_tiles; ++kt) {
-          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag)) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
             ok = false;
             break;
           }
-          uint8_t* a_dst = smem + stage * kTcStageBytes;
+          uint8_t* a_dst = rsmem + stage * stage_bytes;
           uint8_t* b_dst = a_dst + kTcATileBytes;
-          mbar_arrive_expect_tx(&full_bar[stage], tx_bytes);
+          mbar_arrive_expect_tx(&full[stage], tx_bytes);
           if (kPair) {
-            tma_load_2d(a_dst, &map_a0, &full_bar[stage], kt * kTcBK, a_row);
-            tma_load_2d(a_dst + kTcATileBytes / 2, &map_a1, &full_bar[stage], kt * kTcBK, a_row);
+            tma_load_2d(a_dst, &map_a0, &full[stage], kt * kTcBK, a_row);
+            tma_load_2d(a_dst + kTcATileBytes / 2, &map_a1, &full[stage], kt * kTcBK, a_row);
           } else {
-            tma_load_2d(a_dst, &map_a0, &full_bar[stage], kt * kTcBK, a_row);
+            tma_load_2d(a_dst, &map_a0, &full[stage], kt * kTcBK, a_row);
           }
-          tma_load_2d(b_dst, &map_b, &full_bar[stage], kt * kTcBK, ti.row0);
+          tma_load_2d(b_dst, &map_b, &full[stage], kt * kTcBK, ti.row0);
           issued_mask |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
-          if (++stage == kTcStages) {
+          if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
           }
@@ -247,73 +272,70 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       // Never leave the CTA with a TMA write still in flight: wait (time
       // bounded, abort ignored) for the last load issued into each stage.
-      for (int s = 0; s < kTcStages; ++s)
+      for (int s = 0; s < kStages; ++s)
         if (issued_mask & (1u << s))
-          mbar_wait(&full_bar[s], (issued_parity >> s) & 1u, nullptr);
+          mbar_wait(&full[s], (issued_parity >> s) & 1u, nullptr);
     }
-  } else if (warp == 1) {
+  } else if (role == 1) {
     if (lane == 0) {
       // --------------------------------------------------- MMA issuer ----
       int stage = 0, nt_done = 0;
       uint32_t phase = 0, acc_phase = 0;  // acc_phase bit b: phase of buffer b
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x, ++nt_done) {
+      for (int t = t0; ok && t < total_tiles; t += tile_step, ++nt_done) {
         const TileInfo ti = decode_tile(p, t);
         const int ab = nt_done % nbuf;
         const uint32_t n_mma = static_cast<uint32_t>(max(16, (ti.nrows + 15) & ~15));
         const uint32_t idesc = idesc_bf16_f32(128, n_mma);
-        if (!mbar_wait(&acc_empty_bar[ab], ((acc_phase >> ab) & 1u) ^ 1u, abort_flag)) break;
+        if (!mbar_wait(&acc_empty[ab], ((acc_phase >> ab) & 1u) ^ 1u, abort_flag)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem + static_cast<uint32_t>(ab) * acc_cols;
+        const uint32_t d_tmem = rtmem + static_cast<uint32_t>(ab) * acc_cols;
         for (int kt = 0; kt < k_tiles; ++kt) {
-          if (!mbar_wait(&full_bar[stage], phase, abort_flag) ||
-              !mbar_wait(&aready_bar[stage], phase, abort_flag)) {
+          if (!mbar_wait(&full[stage], phase, abort_flag) ||
+              !mbar_wait(&aready[stage], phase, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t b_addr = smem_u32(smem + stage * kTcStageBytes + kTcATileBytes);
-          const uint32_t a_tmem = tmem + a_col0 + stage * 32;
+          const uint32_t b_addr = smem_u32(rsmem + stage * stage_bytes + kTcATileBytes);
+          const uint32_t a_tmem = rtmem + a_col0 + stage * 32;
 #pragma unroll
           for (int kk = 0; kk < kTcBK / 16; ++kk) {
             const uint64_t bdesc = smem_desc_kmajor_sw128(b_addr + kk * 32);
             mma_ts_bf16(d_tmem, a_tmem + kk * 8, bdesc, idesc, (kt | kk) != 0 ? 1u : 0u);
           }
-          mma_commit(&empty_bar[stage]);
-          if (++stage == kTcStages) {
+          mma_commit(&empty[stage]);
+          if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        mma_commit(&acc_full_bar[ab]);
+        mma_commit(&acc_full[ab]);
         acc_phase ^= 1u << ab;
       }
       // Drain: every MMA issued above has completed once this arrives.
-      mma_commit(&drain_bar);
-      mbar_wait(&drain_bar, 0, nullptr);
+      mma_commit(&drain_bar[ring]);
+      mbar_wait(&drain_bar[ring], 0, nullptr);
     }
-  } else if (warp >= kTcFirstConvWarp && warp < kTcFirstEpiWarp) {
+  } else if (role == 2) {
     // ------------------------------------------------------ converters ----
     const int q = warp & 3;  // TMEM lane quarter of this warp
-    const int grp = (warp - kTcFirstConvWarp) >> 2;
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    const uint32_t lane_base = rtmem + (static_cast<uint32_t>(q * 32) << 16);
     const int src_row = kPair ? ((lane < 16) ? (q * 16 + lane) : (64 + q * 16 + lane - 16))
                               : (q * 32 + lane);
     const int swz = (src_row >> 1) & 3;  // 64-byte TMA swizzle of this row
-    uint32_t gs = 0;                     // global stage counter (all tiles)
+    int stage = 0;
+    uint32_t phase = 0;
     bool ok = true;
-    for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
-      for (int kt = 0; kt < k_tiles; ++kt, ++gs) {
-        if ((gs % kTcConvGroups) != static_cast<uint32_t>(grp)) continue;
-        const int stage = static_cast<int>(gs % kTcStages);
-        const uint32_t phase = (gs / kTcStages) & 1u;
+    for (int t = t0; ok && t < total_tiles; t += tile_step) {
+      for (int kt = 0; kt < k_tiles; ++kt) {
         // Warp-uniform outcome: the tcgen05.st below needs all 32 lanes.
-        if (!__all_sync(0xffffffffu, mbar_wait(&full_bar[stage], phase, abort_flag))) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], phase, abort_flag))) {
           ok = false;
           break;
         }
-        const uint8_t* a_src = smem + stage * kTcStageBytes + src_row * kTcBK;
+        const uint8_t* a_src = rsmem + stage * stage_bytes + src_row * kTcBK;
         uint32_t v[32];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -327,36 +349,39 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&aready_bar[stage]);
+        if (lane == 0) mbar_arrive(&aready[stage]);
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
       }
     }
-  } else if (warp >= kTcFirstEpiWarp) {
+  } else {
     // -------------------------------------------------------- epilogue ----
     const int q = warp & 3;
-    const int sub = (warp - kTcFirstEpiWarp) >> 2;
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    const uint32_t lane_base = rtmem + (static_cast<uint32_t>(q * 32) << 16);
     uint32_t acc_phase = 0;
     int nt_done = 0;
-    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++nt_done) {
+    for (int t = t0; t < total_tiles; t += tile_step, ++nt_done) {
       const TileInfo ti = decode_tile(p, t);
       const int ab = nt_done % nbuf;
       if (!__all_sync(0xffffffffu,
-                      mbar_wait(&acc_full_bar[ab], (acc_phase >> ab) & 1u, abort_flag)))
+                      mbar_wait(&acc_full[ab], (acc_phase >> ab) & 1u, abort_flag)))
         break;
       tc_fence_after();
-      epilogue_tile<kMode>(p, ti, lane_base + static_cast<uint32_t>(ab) * acc_cols, q, sub, lane);
+      epilogue_tile<kMode>(p, ti, lane_base + static_cast<uint32_t>(ab) * acc_cols, q, lane);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty_bar[ab]);
+      if (lane == 0) mbar_arrive(&acc_empty[ab]);
       acc_phase ^= 1u << ab;
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == 2) {
     tc_fence_after();
-    tmem_dealloc(tmem, kTcTmemCols);
+    tmem_dealloc(tmem_base_sh, kTcTmemCols);
   }
 }
 
@@ -382,10 +407,11 @@ int launch_mode(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap&
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
     KW8_CUDA_TRY(cudaFuncSetAttribute(w8_gemm_tc_kernel<kMode>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      kTcSmemBytes));
+                                      kTcDynSmemMax));
     attr_set[dev] = true;
   }
-  w8_gemm_tc_kernel<kMode><<<grid, kTcThreads, kTcSmemBytes, stream>>>(a0, a1, b, args);
+  const TcPlan pl = tc_plan(args.nt);
+  w8_gemm_tc_kernel<kMode><<<grid, kTcThreads, pl.smem_bytes, stream>>>(a0, a1, b, args);
   KW8_CHECK_LAUNCH();
   return KW8_OK;
 }
@@ -417,6 +443,15 @@ int launch_gemm_tc(int mode, const int8_t* wa, const int8_t* wb, int64_t groups,
   GemmArgs args = args_in;
   args.K = static_cast<int>(K);
   args.N_out = static_cast<int>(N_out);
+  const TcPlan pl = tc_plan(args.nt);
+  KW8_REQUIRE(pl.stages >= 2 && pl.stages <= kTcMaxStages &&
+                  pl.nbuf * pl.acc_cols + pl.stages * 32 <= static_cast<int>(kTcRingTmemCols) &&
+                  pl.smem_bytes <= kTcDynSmemMax,
+              KW8_ERR_INVALID_ARG, "no pipeline plan for token tile %d", args.nt);
+  args.stages = pl.stages;
+  args.stage_bytes = pl.stage_bytes;
+  args.acc_cols = pl.acc_cols;
+  args.nbuf = pl.nbuf;
   const int rows_per_mtile = pair ? 64 : 128;
   args.m_tiles = static_cast<int>((N_out + rows_per_mtile - 1) / rows_per_mtile);
 
@@ -450,7 +485,8 @@ int launch_gemm_tc(int mode, const int8_t* wa, const int8_t* wb, int64_t groups,
   if (max_tiles <= 0) return KW8_OK;
   int dev = 0;
   KW8_CUDA_TRY(cudaGetDevice(&dev));
-  const int grid = static_cast<int>(std::min<int64_t>(max_tiles, num_sms(dev)));
+  const int grid =
+      static_cast<int>(std::min<int64_t>((max_tiles + kTcRings - 1) / kTcRings, num_sms(dev)));
 
   switch (mode) {
     case EPI_PAIR_GELU:

@@ -5,28 +5,31 @@
 // for every row of every group g (an expert, or the single group of a dense
 // layer).  W is int8 K-major ([groups][N_out][K]); X is bf16 [rows][K].
 //
-// Roles of the 20 warps of a CTA (one CTA per SM, persistent over tiles):
-//   warp 0       TMA producer: int8 weight tile (128 rows x 64 k, 64 B
-//                swizzle) and bf16 token tile (nt rows x 64 k, 128 B swizzle)
-//                per pipeline stage, completion on full[s].
-//   warp 1       TMEM allocator and MMA issuer (one thread): per stage,
-//                4 x tcgen05.mma kind::f16, M=128 (weight rows), N=rows of
-//                the tile rounded to 16, K=16, A read from TMEM, B from
-//                shared memory, accumulator in TMEM; tcgen05.commit frees the
-//                stage (empty[s]) and, after the last k tile, hands the
-//                accumulator to the epilogue (acc_full[b]).
-//   warps 4-11   converters, two groups of four that take alternate
-//                stages.  Warp w owns TMEM lanes 32(w%4)..+31; each thread
-//                widens its weight row of the stage from int8 to bf16
-//                (exact) into the stage's TMEM A slot (tcgen05.st), then
-//                the warp arrives on a_ready[s].
-//   warps 12-19  epilogue, two warps per TMEM lane quarter taking alternate
-//                32-column chunks: read the fp32 accumulator (tcgen05.ld),
-//                apply the per-channel scale and the activation, store.
-// When the token tile is at most 160 columns the accumulator is double
-// buffered in TMEM (2 x 160 + 5 A slots x 32 = 480 of 512 columns), so the
-// epilogue of one tile runs under the MMAs of the next; wider tiles use one
-// accumulator and the MMA waits for the epilogue.
+// A CTA (one per SM, persistent over tiles) runs two independent pipelines
+// ("rings"), each with its own shared-memory stages, half of the 512 TMEM
+// columns, its own barriers and every other tile of the CTA's share.  One
+// thread can issue a tcgen05.mma only about every 100 cycles, so a single
+// issuer keeps the tensor core busy only for tiles of ~200+ tokens; two
+// issuers working on 128-token tiles keep it ~90% busy, and while one
+// ring drains its accumulator the other still feeds the tensor core.
+// Warps of ring r (20 warps in all):
+//   warp r         TMA producer: int8 weight tile (128 rows x 64 k, 64 B
+//                  swizzle) and bf16 token tile (nt rows x 64 k, 128 B
+//                  swizzle) per stage, completion on full[s].
+//   warp 2+r       MMA issuer (one thread; warp 2 also allocates TMEM): per
+//                  stage 4 x tcgen05.mma kind::f16, M=128 (weight rows),
+//                  N=rows of the tile rounded to 16, K=16, A read from TMEM,
+//                  B from shared memory, fp32 accumulator in TMEM;
+//                  tcgen05.commit frees the stage (empty[s]) and, after the
+//                  last k tile, hands the accumulator to the epilogue.
+//   warps 4+4r..7+4r   converters: warp w owns TMEM lanes 32(w%4)..+31; each
+//                  thread widens its weight row of the stage from int8 to
+//                  bf16 (exact) into the stage's TMEM A slot (tcgen05.st).
+//   warps 12+4r..15+4r epilogue: read the accumulator (tcgen05.ld), apply
+//                  the per-channel scale and the activation, store.
+// Each ring's 256 TMEM columns hold its accumulator(s) followed by one
+// 32-column A slot per stage (tc_plan); tiles of up to 64 tokens get two
+// accumulators per ring.
 // Putting the widened weights in TMEM (the "A from TMEM" MMA form) keeps
 // the shared-memory traffic per stage at one int8 read plus the tensor
 // core's read of the token tile; a bf16 copy of the weights never touches
@@ -86,28 +89,50 @@ struct GemmArgs {
   // EPI_COMBINE_F32 only: token and routing weight of every sorted row.
   const int32_t* row_token;
   const float* row_weight;
+  // Pipeline plan (tc_plan), filled in by the launcher.
+  int stages, stage_bytes, acc_cols, nbuf;
 };
 
-constexpr int kTcStages = 5;
+constexpr int kTcRings = 2;
+constexpr int kTcMaxStages = 8;                    // pipeline depth limit (barrier arrays)
+constexpr int kTcMinDoubleBufferStages = 3;        // fewer stages: one accumulator instead
 constexpr int kTcBK = 64;                          // k per stage
 constexpr int kTcARows = 128;                      // weight rows per tile (M)
 constexpr int kTcATileBytes = kTcARows * kTcBK;    // 8 KB int8
-constexpr int kTcMaxNT = 256;
-constexpr int kTcBTileBytes = kTcMaxNT * kTcBK * 2;  // 32 KB bf16
-constexpr int kTcStageBytes = kTcATileBytes + kTcBTileBytes;
-constexpr int kTcSmemBytes = kTcStages * kTcStageBytes + 1024;  // + align slack
-constexpr int kTcThreads = 640;
-constexpr int kTcConvGroups = 2;        // converter groups (4 warps each)
+constexpr int kTcMaxNT = 192;                      // one accumulator + 2 A slots per ring
+constexpr int kTcDynSmemMax = 232448 - 1024;       // opt-in dynamic smem minus static
+constexpr int kTcThreads = 640;                    // 20 warps
 constexpr int kTcFirstConvWarp = 4;
 constexpr int kTcFirstEpiWarp = 12;
-constexpr int kTcEpiWarps = 8;          // two per TMEM lane quarter
-constexpr int kTcMaxDoubleBufferNT = 160;  // widest tile with two accumulators
-static_assert(2 * ((kTcMaxDoubleBufferNT + 31) / 32 * 32) + kTcStages * 32 <= 512,
-              "two accumulators and the A slots must fit in 512 TMEM columns");
-static_assert(kTcMaxNT + kTcStages * 32 <= 512, "one accumulator and the A slots must fit");
-constexpr uint32_t kTcTmemCols = 512;
-// TMEM columns: accumulator buffer b at [b * acc_cols, +acc_cols) with
-// acc_cols = nt rounded up to 32; A slot s at [nbuf * acc_cols + 32 s, +32).
+constexpr int kTcEpiWarpsPerRing = 4;
+constexpr int kTcMaxDoubleBufferNT = 128;          // widest tile the MoE path asks for
+constexpr uint32_t kTcTmemCols = 512;              // allocation (both rings)
+constexpr uint32_t kTcRingTmemCols = 256;
+
+// Pipeline plan of one launch, from the token tile nt, per ring:
+// accumulator buffers of acc_cols TMEM columns (nbuf of them) followed by
+// `stages` A slots of 32 columns, within the ring's 256 columns; `stages`
+// shared-memory stages of stage_bytes (8 KB int8 weights + nt x 128 B
+// tokens).  Two accumulators when that still leaves
+// kTcMinDoubleBufferStages stages.
+struct TcPlan {
+  int acc_cols, nbuf, stages, stage_bytes, ring_bytes, smem_bytes;
+};
+
+inline TcPlan tc_plan(int nt) {
+  TcPlan pl;
+  pl.acc_cols = (nt + 31) & ~31;
+  pl.stage_bytes = kTcATileBytes + nt * kTcBK * 2;
+  const int smem_stages = ((kTcDynSmemMax - 1024) / kTcRings) / pl.stage_bytes;
+  for (pl.nbuf = 2; pl.nbuf >= 1; --pl.nbuf) {
+    const int tmem_stages = (static_cast<int>(kTcRingTmemCols) - pl.nbuf * pl.acc_cols) / 32;
+    pl.stages = std::min(kTcMaxStages, std::min(tmem_stages, smem_stages));
+    if (pl.nbuf == 1 || pl.stages >= kTcMinDoubleBufferStages) break;
+  }
+  pl.ring_bytes = pl.stages * pl.stage_bytes;  // multiple of 1024
+  pl.smem_bytes = kTcRings * pl.ring_bytes + 1024;  // + 1 KB alignment slack
+  return pl;
+}
 
 int launch_gemm_tc(int mode, const int8_t* wa, const int8_t* wb, int64_t groups,
                    int64_t N_out, int64_t K, const void* x, int64_t x_rows,

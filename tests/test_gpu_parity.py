@@ -361,7 +361,7 @@ def test_moe_token_tiles_agree():
     cfg = MoEConfig(use_moe=True, num_experts=E, num_experts_per_tok=k, moe_impl="ragged_jax",
                     moe_ragged_decode_token_threshold=0)
     _lib.set_option(_lib.OPT_GEMM_PATH, 1)
-    for nt in (16, 48, 128, 256):
+    for nt in (16, 48, 128, 192):
         _lib.set_option(_lib.OPT_TOKEN_TILE, nt)
         _moe_check(x, g, o, E, k, M.moe_swiglu_ffn(to_dev(x), *g, cfg=cfg))
 
