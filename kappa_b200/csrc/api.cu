@@ -1,6 +1,7 @@
 // extern "C" entry points of libkappa_w8 (declared in include/kappa_w8.h).
 #include <atomic>
 #include <climits>
+#include <cmath>
 
 #include "gemm_simt.cuh"
 #include "gemm_tc.cuh"
@@ -41,15 +42,19 @@ struct Carver {
 
 int round16(int64_t v) { return static_cast<int>((v + 15) & ~int64_t(15)); }
 
-// Token tile for the grouped tensor-core path: about 1.5x the mean rows per
-// group, 16..128.  Small tiles keep the token TMA box (loaded in full every
-// stage) from dwarfing the weight tile when groups are small; 128-token tiles
-// keep four pipeline stages per ring (groups are split into near-equal tiles).
+// Token tile for the grouped tensor-core path.  With routed rows per group
+// of mean m (spread about sqrt(m)), a group's rows up to m + 3 sqrt(m) are
+// split into j near-equal tiles of at most kTcMaxDoubleBufferNT rows (the
+// widest tile with two TMEM accumulators): nt = that bound / j, rounded up
+// to 16.  Fewer, wider tiles widen each int8 weight slice into bf16 fewer
+// times.
 int pick_nt(int64_t rows, int64_t groups) {
   const int forced = g_opt_token_tile.load();
   if (forced >= 16 && forced <= kTcMaxNT && forced % 16 == 0) return forced;
-  const int64_t mean = (rows + groups - 1) / (groups > 0 ? groups : 1);
-  int64_t nt = round16((mean * 3 + 1) / 2);
+  const double mean = static_cast<double>(rows) / static_cast<double>(groups > 0 ? groups : 1);
+  const double hi = mean + 3.0 * std::sqrt(mean);
+  const int64_t j = std::max<int64_t>(1, static_cast<int64_t>(std::ceil(hi / kTcMaxDoubleBufferNT)));
+  int64_t nt = round16(static_cast<int64_t>(std::ceil(hi / static_cast<double>(j))));
   if (nt < 16) nt = 16;
   if (nt > kTcMaxDoubleBufferNT) nt = kTcMaxDoubleBufferNT;
   return static_cast<int>(nt);
@@ -59,7 +64,7 @@ int pick_nt(int64_t rows, int64_t groups) {
 // feature tiles: the fewest waves over the SMs, a tile costing about
 // max(128, nt) (below ~128 tokens a tile is bound by widening its 128x64
 // int8 weight slices, not by the MMAs); ties go to the larger tile; at most
-// 128.
+// kTcMaxDoubleBufferNT.
 int pick_nt_dense(int64_t rows, int64_t m_tiles) {
   const int forced = g_opt_token_tile.load();
   if (forced >= 16 && forced <= kTcMaxNT && forced % 16 == 0) return forced;

@@ -76,21 +76,25 @@ __device__ __forceinline__ float load_scale(const void* p, int dtype, int64_t i)
   return bf16_bits_to_f32(__ldg(b + i));
 }
 
-// int8 x4 (one 32-bit word, byte 0 = lowest k) -> two bf16x2 words, exact.
-// Each byte q is biased to u = q + 128, placed in the mantissa of the fp32
-// 2^23 (bits 0x4B0000uu = 8388608 + u), and 8388608 + 128 is subtracted:
-// the result is q exactly.  A small integer's fp32 encoding has zero low
-// 16 bits, so its bf16 encoding is the high half, taken with one byte_perm.
+__device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// int8 x4 (one 32-bit word, byte 0 = lowest k) -> two bf16x2 words, exact,
+// in two instructions per element.  For a byte b (two's complement q) the
+// 16-bit lane t = 0x43:b is formed with one byte_perm; then
+//   x = t & 0xFF7F  is bf16 128 + (b & 0x7F)
+//   c = t & 0xFF80  is bf16 128 (b >= 0) or 256 (b < 0, 0x4380)
+// and x - c = q: 128 + q - 128 for q >= 0, 128 + (q + 128) - 256 for q < 0.
+// The bf16 subtraction is exact (c/2 <= x <= 2c and q is representable).
 __device__ __forceinline__ void i8x4_to_bf16x4(uint32_t w, uint32_t& lo,
                                                uint32_t& hi) {
-  const uint32_t u = w ^ 0x80808080u;
-  const float magic = 8388736.0f;  // 2^23 + 128
-  float f0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)) - magic;
-  float f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541)) - magic;
-  float f2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)) - magic;
-  float f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)) - magic;
-  lo = __byte_perm(__float_as_uint(f0), __float_as_uint(f1), 0x7632);
-  hi = __byte_perm(__float_as_uint(f2), __float_as_uint(f3), 0x7632);
+  const uint32_t t0 = __byte_perm(w, 0x43434343u, 0x4140);  // 43:b1:43:b0
+  const uint32_t t1 = __byte_perm(w, 0x43434343u, 0x4342);  // 43:b3:43:b2
+  lo = bf16x2_sub(t0 & 0xFF7FFF7Fu, t0 & 0xFF80FF80u);
+  hi = bf16x2_sub(t1 & 0xFF7FFF7Fu, t1 & 0xFF80FF80u);
 }
 
 __device__ __forceinline__ float tanh_approx(float x) {
@@ -272,6 +276,15 @@ __device__ __forceinline__ uint64_t smem_desc_kmajor_sw128(uint32_t saddr) {
       "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), \
       "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), \
       "r"(v[30]), "r"(v[31])                                                   \
+      : "memory")
+
+#define KW8_TMEM_ST_X16(taddr, v)                                              \
+  asm volatile(                                                                \
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, " \
+      "%7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),          \
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]),       \
+      "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]),     \
+      "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])                           \
       : "memory")
 
 #define KW8_TMEM_LD_X32(taddr, v)                                              \

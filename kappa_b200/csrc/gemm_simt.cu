@@ -21,7 +21,9 @@ __device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
   return r;
 }
 
-// 16 int8 -> 16 fp32 (exact; same bias trick as i8x4_to_bf16x4).
+// 16 int8 -> 16 fp32, exact: each byte q is biased to u = q + 128, placed
+// in the mantissa of the fp32 2^23 (bits 0x4B0000uu = 8388608 + u), and
+// 8388608 + 128 is subtracted.
 __device__ __forceinline__ void i8x16_to_f32(const uint4& w, float* f) {
   const uint32_t words[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll

@@ -53,11 +53,12 @@ __device__ __forceinline__ void transpose4x4(float (&a)[4], int lane) {
   }
 }
 
-// Epilogue of one tile for one warp: TMEM lane quarter q, every 32-column
-// chunk of the accumulator at acc_lane_base.
+// Epilogue of one tile for one warp: TMEM lane quarter q, 32-column chunks
+// c0, c0 + cstep, ... of the accumulator at acc_lane_base.
 template <int kMode>
 __device__ __forceinline__ void epilogue_tile(const GemmArgs& p, const TileInfo& ti,
-                                              uint32_t acc_lane_base, int q, int lane) {
+                                              uint32_t acc_lane_base, int q, int lane,
+                                              int c0, int cstep) {
   constexpr bool kPair = epi_is_pair(kMode);
   const int nrows = ti.nrows;
   const int nchunks = (nrows + 31) >> 5;
@@ -69,26 +70,33 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& p, const TileInfo&
                         ? scale_at(p.scale_a, p.scale_a_dtype, p.scale_a_pc, sidx)
                         : scale_at(p.scale_b, p.scale_b_dtype, p.scale_b_pc, sidx);
     __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
-    for (int c = 0; c < nchunks; ++c) {
+    const bool hi_half = lane >= 16;
+    __nv_bfloat16* col = out + static_cast<int64_t>(ti.row0 + (hi_half ? 16 : 0)) * p.ld_out + f;
+    for (int c = c0; c < nchunks; c += cstep) {
       uint32_t r[32];
       KW8_TMEM_LD_X32(acc_lane_base + c * 32, r);
       tmem_wait_ld();
+      // All shuffles and math first (no divergence inside), stores after.
+      __nv_bfloat16 h[16];
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const float lo = __uint_as_float(r[j]) * s;       // token c*32 + j
         const float hi = __uint_as_float(r[16 + j]) * s;  // token c*32 + 16 + j
-        const float send = (lane < 16) ? hi : lo;
-        const float recv = __shfl_xor_sync(0xffffffffu, send, 16);
-        const float g = (lane < 16) ? lo : recv;
-        const float u = (lane < 16) ? recv : hi;
-        const int tok = c * 32 + j + ((lane < 16) ? 0 : 16);
-        float h;
+        const float recv = __shfl_xor_sync(0xffffffffu, hi_half ? lo : hi, 16);
+        const float g = hi_half ? recv : lo;
+        const float u = hi_half ? hi : recv;
         if constexpr (kMode == EPI_PAIR_GELU)
-          h = gelu_tanh_f(g) * u;
+          h[j] = __float2bfloat16_rn(gelu_tanh_f(g) * u);
         else
-          h = silu_f(g) * u;
-        if (fvalid && tok < nrows)
-          out[static_cast<int64_t>(ti.row0 + tok) * p.ld_out + f] = __float2bfloat16_rn(h);
+          h[j] = __float2bfloat16_rn(silu_f(g) * u);
+      }
+      // Lane rows: c*32 + j (lanes 0-15) or c*32 + 16 + j (lanes 16-31).
+      const int left = nrows - c * 32 - (hi_half ? 16 : 0);
+      __nv_bfloat16* dst = col + static_cast<int64_t>(c * 32) * p.ld_out;
+      if (fvalid) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (j < left) dst[static_cast<int64_t>(j) * p.ld_out] = h[j];
       }
     }
   } else if constexpr (kMode == EPI_COMBINE_F32) {
@@ -100,7 +108,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& p, const TileInfo&
     const int f4 = fbase + (lane & ~3);  // first of the 4 features this lane adds
     const bool f4valid = f4 < p.N_out;   // N_out % 4 == 0 (checked by the launcher)
     float* out = static_cast<float*>(p.out);
-    for (int c = 0; c < nchunks; ++c) {
+    for (int c = c0; c < nchunks; c += cstep) {
       uint32_t r[32];
       KW8_TMEM_LD_X32(acc_lane_base + c * 32, r);
       // Lane l fetches the token and routing weight of row c*32 + l.
@@ -108,20 +116,28 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& p, const TileInfo&
       const int tok_l = (my_row < nrows) ? p.row_token[ti.row0 + my_row] : 0;
       const float w_l = (my_row < nrows) ? p.row_weight[ti.row0 + my_row] : 0.f;
       tmem_wait_ld();
+      // Rows 4b..4b+3 of the chunk; after the transpose lane 4g+pl holds
+      // features f4..f4+3 of row 4b+pl, added with one 16-byte atomic.  All
+      // shuffles first (no divergence inside), atomics after.
+      float4 v[8];
+      int tok[8];
 #pragma unroll
       for (int b = 0; b < 8; ++b) {
-        // Rows 4b..4b+3 of the chunk; after the transpose lane 4g+pl holds
-        // features f4..f4+3 of row 4b+pl, added with one 16-byte atomic.
         float a[4] = {__uint_as_float(r[4 * b]) * s, __uint_as_float(r[4 * b + 1]) * s,
                       __uint_as_float(r[4 * b + 2]) * s, __uint_as_float(r[4 * b + 3]) * s};
         transpose4x4(a, lane);
         const int src = 4 * b + (lane & 3);
-        const int tok = __shfl_sync(0xffffffffu, tok_l, src);
+        tok[b] = __shfl_sync(0xffffffffu, tok_l, src);
         const float wr = __shfl_sync(0xffffffffu, w_l, src);
-        if (f4valid && c * 32 + src < nrows) {
-          float4 v = make_float4(a[0] * wr, a[1] * wr, a[2] * wr, a[3] * wr);
-          atomicAdd(reinterpret_cast<float4*>(out + static_cast<int64_t>(tok) * p.ld_out + f4), v);
-        }
+        v[b] = make_float4(a[0] * wr, a[1] * wr, a[2] * wr, a[3] * wr);
+      }
+      const int left = nrows - c * 32 - (lane & 3);
+      if (f4valid) {
+#pragma unroll
+        for (int b = 0; b < 8; ++b)
+          if (4 * b < left)
+            atomicAdd(reinterpret_cast<float4*>(out + static_cast<int64_t>(tok[b]) * p.ld_out + f4),
+                      v[b]);
       }
     }
   } else {
@@ -129,7 +145,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& p, const TileInfo&
     const bool fvalid = f < p.N_out;
     const int64_t sidx = static_cast<int64_t>(ti.group) * p.N_out + (fvalid ? f : 0);
     const float s = scale_at(p.scale_a, p.scale_a_dtype, p.scale_a_pc, sidx);
-    for (int c = 0; c < nchunks; ++c) {
+    for (int c = c0; c < nchunks; c += cstep) {
       uint32_t r[32];
       KW8_TMEM_LD_X32(acc_lane_base + c * 32, r);
       tmem_wait_ld();
@@ -160,12 +176,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
 
-  __shared__ uint64_t full_bar[kTcRings][kTcMaxStages];
-  __shared__ uint64_t aready_bar[kTcRings][kTcMaxStages];
-  __shared__ uint64_t empty_bar[kTcRings][kTcMaxStages];
-  __shared__ uint64_t acc_full_bar[kTcRings][2];
-  __shared__ uint64_t acc_empty_bar[kTcRings][2];
-  __shared__ uint64_t drain_bar[kTcRings];
+  __shared__ uint64_t full[kTcMaxStages];
+  __shared__ uint64_t aready[kTcMaxStages];
+  __shared__ uint64_t empty[kTcMaxStages];
+  __shared__ uint64_t acc_full[2];
+  __shared__ uint64_t acc_empty[2];
+  __shared__ uint64_t drain_bar;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_sh;
 
@@ -173,18 +189,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int r = 0; r < kTcRings; ++r) {
-      for (int s = 0; s < p.stages; ++s) {
-        mbar_init(&full_bar[r][s], 1);
-        mbar_init(&aready_bar[r][s], 4);
-        mbar_init(&empty_bar[r][s], 1);
-      }
-      for (int b = 0; b < 2; ++b) {
-        mbar_init(&acc_full_bar[r][b], 1);
-        mbar_init(&acc_empty_bar[r][b], kTcEpiWarpsPerRing);
-      }
-      mbar_init(&drain_bar[r], 1);
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(&full[s], kTcProducers);
+      mbar_init(&aready[s], kTcConvWarps);
+      mbar_init(&empty[s], 1);
     }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], kTcEpiWarps);
+    }
+    mbar_init(&drain_bar, 1);
     abort_sh = 0;
     fence_barrier_init();
   }
@@ -193,58 +207,40 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (kPair) tma_prefetch_desc(&map_a1);
     tma_prefetch_desc(&map_b);
   }
-  if (warp == 2) tmem_alloc(&tmem_base_sh, kTcTmemCols);
+  if (warp == 1) tmem_alloc(&tmem_base_sh, kTcTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   volatile int* abort_flag = &abort_sh;
 
-  // Plan from the launcher (tc_plan), per ring.
+  // Plan from the launcher (tc_plan).
   const int kStages = p.stages;
   const int stage_bytes = p.stage_bytes;
   const uint32_t acc_cols = static_cast<uint32_t>(p.acc_cols);
   const int nbuf = p.nbuf;
+  const uint32_t tmem = tmem_base_sh;
   const uint32_t a_col0 = static_cast<uint32_t>(nbuf) * acc_cols;
 
   const int n_entries =
       (p.tiles == nullptr) ? (p.dense_rows + p.nt - 1) / p.nt : *p.num_tiles;
   const int total_tiles = n_entries * p.m_tiles;
   const int k_tiles = (p.K + kTcBK - 1) / kTcBK;
-  const int tile_step = gridDim.x * kTcRings;
 
-  // Role and ring of this warp.
-  int ring, role;  // role: 0 producer, 1 MMA, 2 converter, 3 epilogue
-  if (warp < 2) {
-    role = 0;
-    ring = warp;
-  } else if (warp < 4) {
-    role = 1;
-    ring = warp - 2;
-  } else if (warp < kTcFirstEpiWarp) {
-    role = 2;
-    ring = (warp - kTcFirstConvWarp) >> 2;
-  } else {
-    role = 3;
-    ring = (warp - kTcFirstEpiWarp) >> 2;
-  }
-  uint8_t* rsmem = smem + ring * kStages * stage_bytes;
-  const uint32_t rtmem = tmem_base_sh + static_cast<uint32_t>(ring) * kTcRingTmemCols;
-  uint64_t* full = full_bar[ring];
-  uint64_t* aready = aready_bar[ring];
-  uint64_t* empty = empty_bar[ring];
-  uint64_t* acc_full = acc_full_bar[ring];
-  uint64_t* acc_empty = acc_empty_bar[ring];
-  const int t0 = blockIdx.x * kTcRings + ring;
-
-  if (role == 0) {
+  if (warp == 0 || warp == 2 || warp == 3) {
     if (lane == 0) {
-      // ------------------------------------------------ TMA producer ----
-      const uint32_t tx_bytes = kTcATileBytes + static_cast<uint32_t>(p.nt) * kTcBK * 2;
+      // ----------------------------------------------- TMA producers ----
+      // Warp 0 loads the weight tile, warps 2 and 3 one 64-k half of the
+      // token tile each; each arms full[s] with its own bytes.
+      const int part = (warp == 0) ? 0 : warp - 1;  // 0: weights, 1/2: token halves
+      const uint32_t tx_bytes = (part == 0)
+                                    ? static_cast<uint32_t>(kTcATileBytes)
+                                    : static_cast<uint32_t>(p.nt) * kTcBHalfK * 2;
+      const uint32_t b_off = kTcATileBytes + (part == 2 ? p.nt * kTcBHalfK * 2 : 0);
       int stage = 0;
       uint32_t phase = 0;
       uint32_t issued_mask = 0, issued_parity = 0;
       bool ok = true;
-      for (int t = t0; ok && t < total_tiles; t += tile_step) {
+      for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
         const TileInfo ti = decode_tile(p, t);
         const int a_row = ti.group * p.N_out + ti.mt * (kPair ? 64 : 128);
         for (int kt = 0; kt < k_tiles; ++kt) {
@@ -252,16 +248,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             ok = false;
             break;
           }
-          uint8_t* a_dst = rsmem + stage * stage_bytes;
-          uint8_t* b_dst = a_dst + kTcATileBytes;
-          mbar_arrive_expect_tx(&full[stage], tx_bytes);
-          if (kPair) {
-            tma_load_2d(a_dst, &map_a0, &full[stage], kt * kTcBK, a_row);
-            tma_load_2d(a_dst + kTcATileBytes / 2, &map_a1, &full[stage], kt * kTcBK, a_row);
-          } else {
-            tma_load_2d(a_dst, &map_a0, &full[stage], kt * kTcBK, a_row);
+          uint8_t* dst = smem + stage * stage_bytes;
+          // A second token half past K is not loaded (its MMAs are skipped).
+          const bool load = part != 2 || kt * kTcBK + kTcBHalfK < p.K;
+          if (load)
+            mbar_arrive_expect_tx(&full[stage], tx_bytes);
+          else
+            mbar_arrive(&full[stage]);
+          if (part == 0) {
+            if (kPair) {
+              tma_load_2d(dst, &map_a0, &full[stage], kt * kTcBK, a_row);
+              tma_load_2d(dst + kTcATileBytes / 2, &map_a1, &full[stage], kt * kTcBK, a_row);
+            } else {
+              tma_load_2d(dst, &map_a0, &full[stage], kt * kTcBK, a_row);
+            }
+          } else if (load) {
+            tma_load_2d(dst + b_off, &map_b, &full[stage], kt * kTcBK + (part - 1) * kTcBHalfK,
+                        ti.row0);
           }
-          tma_load_2d(b_dst, &map_b, &full[stage], kt * kTcBK, ti.row0);
           issued_mask |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == kStages) {
@@ -271,38 +275,44 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       }
       // Never leave the CTA with a TMA write still in flight: wait (time
-      // bounded, abort ignored) for the last load issued into each stage.
+      // bounded, abort ignored) for the last phase armed on each stage.
       for (int s = 0; s < kStages; ++s)
         if (issued_mask & (1u << s))
           mbar_wait(&full[s], (issued_parity >> s) & 1u, nullptr);
     }
-  } else if (role == 1) {
+  } else if (warp == 1) {
     if (lane == 0) {
       // --------------------------------------------------- MMA issuer ----
       int stage = 0, nt_done = 0;
       uint32_t phase = 0, acc_phase = 0;  // acc_phase bit b: phase of buffer b
       bool ok = true;
-      for (int t = t0; ok && t < total_tiles; t += tile_step, ++nt_done) {
+      for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x, ++nt_done) {
         const TileInfo ti = decode_tile(p, t);
         const int ab = nt_done % nbuf;
         const uint32_t n_mma = static_cast<uint32_t>(max(16, (ti.nrows + 15) & ~15));
         const uint32_t idesc = idesc_bf16_f32(128, n_mma);
         if (!mbar_wait(&acc_empty[ab], ((acc_phase >> ab) & 1u) ^ 1u, abort_flag)) break;
         tc_fence_after();
-        const uint32_t d_tmem = rtmem + static_cast<uint32_t>(ab) * acc_cols;
+        const uint32_t d_tmem = tmem + static_cast<uint32_t>(ab) * acc_cols;
         for (int kt = 0; kt < k_tiles; ++kt) {
-          if (!mbar_wait(&full[stage], phase, abort_flag) ||
-              !mbar_wait(&aready[stage], phase, abort_flag)) {
+          // aready[s] completes after every converter saw full[s], so the
+          // token tile of the stage has landed as well.
+          if (!mbar_wait(&aready[stage], phase, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t b_addr = smem_u32(rsmem + stage * stage_bytes + kTcATileBytes);
-          const uint32_t a_tmem = rtmem + a_col0 + stage * 32;
+          const uint32_t b_addr = smem_u32(smem + stage * stage_bytes + kTcATileBytes);
+          const uint32_t b_half = static_cast<uint32_t>(p.nt) * kTcBHalfK * 2;
+          const uint32_t a_tmem = tmem + a_col0 + stage * kTcASlotCols;
+          const int kk_n = min(kTcBK / 16, (p.K - kt * kTcBK) / 16);  // K % 16 == 0
 #pragma unroll
           for (int kk = 0; kk < kTcBK / 16; ++kk) {
-            const uint64_t bdesc = smem_desc_kmajor_sw128(b_addr + kk * 32);
-            mma_ts_bf16(d_tmem, a_tmem + kk * 8, bdesc, idesc, (kt | kk) != 0 ? 1u : 0u);
+            if (kk < kk_n) {
+              const uint64_t bdesc =
+                  smem_desc_kmajor_sw128(b_addr + (kk >> 2) * b_half + (kk & 3) * 32);
+              mma_ts_bf16(d_tmem, a_tmem + kk * 8, bdesc, idesc, (kt | kk) != 0 ? 1u : 0u);
+            }
           }
           mma_commit(&empty[stage]);
           if (++stage == kStages) {
@@ -315,37 +325,39 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         acc_phase ^= 1u << ab;
       }
       // Drain: every MMA issued above has completed once this arrives.
-      mma_commit(&drain_bar[ring]);
-      mbar_wait(&drain_bar[ring], 0, nullptr);
+      mma_commit(&drain_bar);
+      mbar_wait(&drain_bar, 0, nullptr);
     }
-  } else if (role == 2) {
+  } else if (warp >= kTcFirstConvWarp && warp < kTcFirstConvWarp + kTcConvWarps) {
     // ------------------------------------------------------ converters ----
-    const int q = warp & 3;  // TMEM lane quarter of this warp
-    const uint32_t lane_base = rtmem + (static_cast<uint32_t>(q * 32) << 16);
+    const int q = warp & 3;                               // TMEM lane quarter
+    const int kh = (warp - kTcFirstConvWarp) >> 2;        // 64-k half of the stage
+    const uint32_t lane_base =
+        tmem + (static_cast<uint32_t>(q * 32) << 16) + a_col0 + kh * (kTcASlotCols / 2);
     const int src_row = kPair ? ((lane < 16) ? (q * 16 + lane) : (64 + q * 16 + lane - 16))
                               : (q * 32 + lane);
-    const int swz = (src_row >> 1) & 3;  // 64-byte TMA swizzle of this row
+    const int swz = src_row & 7;  // 128-byte TMA swizzle of this row
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
-    for (int t = t0; ok && t < total_tiles; t += tile_step) {
+    for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
       for (int kt = 0; kt < k_tiles; ++kt) {
         // Warp-uniform outcome: the tcgen05.st below needs all 32 lanes.
         if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], phase, abort_flag))) {
           ok = false;
           break;
         }
-        const uint8_t* a_src = rsmem + stage * stage_bytes + src_row * kTcBK;
+        const uint8_t* a_src = smem + stage * stage_bytes + src_row * kTcBK;
         uint32_t v[32];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          const uint4 w = *reinterpret_cast<const uint4*>(a_src + ((c ^ swz) << 4));
+          const uint4 w = *reinterpret_cast<const uint4*>(a_src + (((kh * 4 + c) ^ swz) << 4));
           i8x4_to_bf16x4(w.x, v[c * 8 + 0], v[c * 8 + 1]);
           i8x4_to_bf16x4(w.y, v[c * 8 + 2], v[c * 8 + 3]);
           i8x4_to_bf16x4(w.z, v[c * 8 + 4], v[c * 8 + 5]);
           i8x4_to_bf16x4(w.w, v[c * 8 + 6], v[c * 8 + 7]);
         }
-        KW8_TMEM_ST_X32(lane_base + a_col0 + stage * 32, v);
+        KW8_TMEM_ST_X32(lane_base + stage * kTcASlotCols, v);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
@@ -356,20 +368,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       }
     }
-  } else {
+  } else if (warp >= kTcFirstEpiWarp) {
     // -------------------------------------------------------- epilogue ----
     const int q = warp & 3;
-    const uint32_t lane_base = rtmem + (static_cast<uint32_t>(q * 32) << 16);
+    const int ch = (warp - kTcFirstEpiWarp) >> 2;  // chunks ch, ch + 2, ...
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
     uint32_t acc_phase = 0;
     int nt_done = 0;
-    for (int t = t0; t < total_tiles; t += tile_step, ++nt_done) {
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++nt_done) {
       const TileInfo ti = decode_tile(p, t);
       const int ab = nt_done % nbuf;
       if (!__all_sync(0xffffffffu,
                       mbar_wait(&acc_full[ab], (acc_phase >> ab) & 1u, abort_flag)))
         break;
       tc_fence_after();
-      epilogue_tile<kMode>(p, ti, lane_base + static_cast<uint32_t>(ab) * acc_cols, q, lane);
+      epilogue_tile<kMode>(p, ti, lane_base + static_cast<uint32_t>(ab) * acc_cols, q, lane, ch,
+                           kTcEpiWarps / 4);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[ab]);
@@ -379,7 +393,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 2) {
+  if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base_sh, kTcTmemCols);
   }
@@ -445,7 +459,7 @@ int launch_gemm_tc(int mode, const int8_t* wa, const int8_t* wb, int64_t groups,
   args.N_out = static_cast<int>(N_out);
   const TcPlan pl = tc_plan(args.nt);
   KW8_REQUIRE(pl.stages >= 2 && pl.stages <= kTcMaxStages &&
-                  pl.nbuf * pl.acc_cols + pl.stages * 32 <= static_cast<int>(kTcRingTmemCols) &&
+                  pl.nbuf * pl.acc_cols + pl.stages * kTcASlotCols <= static_cast<int>(kTcTmemCols) &&
                   pl.smem_bytes <= kTcDynSmemMax,
               KW8_ERR_INVALID_ARG, "no pipeline plan for token tile %d", args.nt);
   args.stages = pl.stages;
@@ -460,19 +474,19 @@ int launch_gemm_tc(int mode, const int8_t* wa, const int8_t* wb, int64_t groups,
   int rc = make_tmap_2d(&map_a0, wa, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1,
                         static_cast<uint64_t>(groups * N_out), static_cast<uint64_t>(K),
                         static_cast<uint64_t>(K), kTcBK, a_box_rows,
-                        CU_TENSOR_MAP_SWIZZLE_64B);
+                        CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   if (pair) {
     rc = make_tmap_2d(&map_a1, wb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1,
                       static_cast<uint64_t>(groups * N_out), static_cast<uint64_t>(K),
-                      static_cast<uint64_t>(K), kTcBK, a_box_rows, CU_TENSOR_MAP_SWIZZLE_64B);
+                      static_cast<uint64_t>(K), kTcBK, a_box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   } else {
     map_a1 = map_a0;
   }
   rc = make_tmap_2d(&map_b, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
                     static_cast<uint64_t>(x_rows), static_cast<uint64_t>(K),
-                    static_cast<uint64_t>(ldx) * 2, kTcBK, static_cast<uint32_t>(args.nt),
+                    static_cast<uint64_t>(ldx) * 2, kTcBHalfK, static_cast<uint32_t>(args.nt),
                     CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
 
@@ -485,8 +499,7 @@ int launch_gemm_tc(int mode, const int8_t* wa, const int8_t* wb, int64_t groups,
   if (max_tiles <= 0) return KW8_OK;
   int dev = 0;
   KW8_CUDA_TRY(cudaGetDevice(&dev));
-  const int grid =
-      static_cast<int>(std::min<int64_t>((max_tiles + kTcRings - 1) / kTcRings, num_sms(dev)));
+  const int grid = static_cast<int>(std::min<int64_t>(max_tiles, num_sms(dev)));
 
   switch (mode) {
     case EPI_PAIR_GELU:

@@ -5,31 +5,33 @@
 // for every row of every group g (an expert, or the single group of a dense
 // layer).  W is int8 K-major ([groups][N_out][K]); X is bf16 [rows][K].
 //
-// A CTA (one per SM, persistent over tiles) runs two independent pipelines
-// ("rings"), each with its own shared-memory stages, half of the 512 TMEM
-// columns, its own barriers and every other tile of the CTA's share.  One
-// thread can issue a tcgen05.mma only about every 100 cycles, so a single
-// issuer keeps the tensor core busy only for tiles of ~200+ tokens; two
-// issuers working on 128-token tiles keep it ~90% busy, and while one
-// ring drains its accumulator the other still feeds the tensor core.
-// Warps of ring r (20 warps in all):
-//   warp r         TMA producer: int8 weight tile (128 rows x 64 k, 64 B
-//                  swizzle) and bf16 token tile (nt rows x 64 k, 128 B
-//                  swizzle) per stage, completion on full[s].
-//   warp 2+r       MMA issuer (one thread; warp 2 also allocates TMEM): per
-//                  stage 4 x tcgen05.mma kind::f16, M=128 (weight rows),
+// A CTA (one per SM, persistent over tiles) runs one pipeline of stages of
+// 128 k.  On sm_100a one thread needs ~150 cycles to issue a TMA load and
+// ~165 to pass an mbarrier wait, so every per-stage duty is split so that no
+// thread's share exceeds the ~512 tensor-core cycles of a stage's 8 MMAs.
+// Warps (20 in all):
+//   warps 0, 2, 3  TMA producers of stage s (each arms full[s] with its own
+//                  bytes): warp 0 the int8 weight tile (128 rows x 128 k,
+//                  128 B swizzle), warps 2 and 3 the bf16 token tile's two
+//                  64-k halves (nt rows x 128 B, 128 B swizzle).
+//   warp 1         MMA issuer (one thread; the warp also allocates TMEM):
+//                  per stage 8 x tcgen05.mma kind::f16, M=128 (weight rows),
 //                  N=rows of the tile rounded to 16, K=16, A read from TMEM,
-//                  B from shared memory, fp32 accumulator in TMEM;
+//                  B from shared memory, fp32 accumulator in TMEM; it waits
+//                  only for aready[s] (the converters saw full[s] first);
 //                  tcgen05.commit frees the stage (empty[s]) and, after the
 //                  last k tile, hands the accumulator to the epilogue.
-//   warps 4+4r..7+4r   converters: warp w owns TMEM lanes 32(w%4)..+31; each
-//                  thread widens its weight row of the stage from int8 to
-//                  bf16 (exact) into the stage's TMEM A slot (tcgen05.st).
-//   warps 12+4r..15+4r epilogue: read the accumulator (tcgen05.ld), apply
-//                  the per-channel scale and the activation, store.
-// Each ring's 256 TMEM columns hold its accumulator(s) followed by one
-// 32-column A slot per stage (tc_plan); tiles of up to 64 tokens get two
-// accumulators per ring.
+//   warps 4..11    converters: warp w owns TMEM lanes 32(w%4)..+31 and one
+//                  64-k half of the stage; each thread widens its 64 weights
+//                  from int8 to bf16 (exact, two instructions per element)
+//                  into the stage's TMEM A slot (tcgen05.st).
+//   warps 12..19   epilogue: two warps per lane quarter, alternate 32-column
+//                  chunks: read the accumulator (tcgen05.ld), apply the
+//                  per-channel scale and the activation, store.
+// TMEM (512 columns) holds two accumulators of acc_cols columns (tiles of
+// up to 160 tokens; one accumulator above that) followed by one 64-column
+// A slot per stage (tc_plan), so the epilogue of one tile overlaps the
+// MMAs of the next.
 // Putting the widened weights in TMEM (the "A from TMEM" MMA form) keeps
 // the shared-memory traffic per stage at one int8 read plus the tensor
 // core's read of the token tile; a bf16 copy of the weights never touches
@@ -73,7 +75,7 @@ struct GemmArgs {
   int K;          // contraction length (multiple of 16)
   int N_out;      // output features per group
   int m_tiles;    // feature tiles per group
-  int nt;         // token rows per tile (multiple of 16, <= 256)
+  int nt;         // token rows per tile (multiple of 16, <= kTcMaxNT)
   // Tile source: a device table (grouped) or a dense row range.
   const TileEntry* tiles;  // nullptr => dense mode
   const int* num_tiles;    // device count of table entries
@@ -93,44 +95,44 @@ struct GemmArgs {
   int stages, stage_bytes, acc_cols, nbuf;
 };
 
-constexpr int kTcRings = 2;
 constexpr int kTcMaxStages = 8;                    // pipeline depth limit (barrier arrays)
 constexpr int kTcMinDoubleBufferStages = 3;        // fewer stages: one accumulator instead
-constexpr int kTcBK = 64;                          // k per stage
+constexpr int kTcBK = 128;                         // k per stage
+constexpr int kTcBHalfK = 64;                      // k per token TMA box (128 B rows)
 constexpr int kTcARows = 128;                      // weight rows per tile (M)
-constexpr int kTcATileBytes = kTcARows * kTcBK;    // 8 KB int8
-constexpr int kTcMaxNT = 192;                      // one accumulator + 2 A slots per ring
+constexpr int kTcATileBytes = kTcARows * kTcBK;    // 16 KB int8
+constexpr int kTcASlotCols = kTcBK / 2;            // TMEM columns of one stage's bf16 A
+constexpr int kTcMaxNT = 256;                      // MMA N limit
+constexpr int kTcMaxDoubleBufferNT = 160;          // widest tile with two accumulators
 constexpr int kTcDynSmemMax = 232448 - 1024;       // opt-in dynamic smem minus static
 constexpr int kTcThreads = 640;                    // 20 warps
 constexpr int kTcFirstConvWarp = 4;
+constexpr int kTcConvWarps = 8;                    // 2 per TMEM lane quarter (k halves)
+constexpr int kTcProducers = 3;                    // warps 0, 2, 3
 constexpr int kTcFirstEpiWarp = 12;
-constexpr int kTcEpiWarpsPerRing = 4;
-constexpr int kTcMaxDoubleBufferNT = 128;          // widest tile the MoE path asks for
-constexpr uint32_t kTcTmemCols = 512;              // allocation (both rings)
-constexpr uint32_t kTcRingTmemCols = 256;
+constexpr int kTcEpiWarps = 8;                     // 2 per TMEM lane quarter
+constexpr uint32_t kTcTmemCols = 512;
 
-// Pipeline plan of one launch, from the token tile nt, per ring:
-// accumulator buffers of acc_cols TMEM columns (nbuf of them) followed by
-// `stages` A slots of 32 columns, within the ring's 256 columns; `stages`
-// shared-memory stages of stage_bytes (8 KB int8 weights + nt x 128 B
-// tokens).  Two accumulators when that still leaves
-// kTcMinDoubleBufferStages stages.
+// Pipeline plan of one launch, from the token tile nt: accumulator buffers
+// of acc_cols TMEM columns (nbuf of them) followed by `stages` A slots of
+// 64 columns within the 512 columns; `stages` shared-memory stages of
+// stage_bytes (16 KB int8 weights + two 64-k halves of nt x 128 B tokens).
+// Two accumulators when that still leaves kTcMinDoubleBufferStages stages.
 struct TcPlan {
-  int acc_cols, nbuf, stages, stage_bytes, ring_bytes, smem_bytes;
+  int acc_cols, nbuf, stages, stage_bytes, smem_bytes;
 };
 
 inline TcPlan tc_plan(int nt) {
   TcPlan pl;
   pl.acc_cols = (nt + 31) & ~31;
   pl.stage_bytes = kTcATileBytes + nt * kTcBK * 2;
-  const int smem_stages = ((kTcDynSmemMax - 1024) / kTcRings) / pl.stage_bytes;
+  const int smem_stages = (kTcDynSmemMax - 1024) / pl.stage_bytes;
   for (pl.nbuf = 2; pl.nbuf >= 1; --pl.nbuf) {
-    const int tmem_stages = (static_cast<int>(kTcRingTmemCols) - pl.nbuf * pl.acc_cols) / 32;
+    const int tmem_stages = (static_cast<int>(kTcTmemCols) - pl.nbuf * pl.acc_cols) / kTcASlotCols;
     pl.stages = std::min(kTcMaxStages, std::min(tmem_stages, smem_stages));
     if (pl.nbuf == 1 || pl.stages >= kTcMinDoubleBufferStages) break;
   }
-  pl.ring_bytes = pl.stages * pl.stage_bytes;  // multiple of 1024
-  pl.smem_bytes = kTcRings * pl.ring_bytes + 1024;  // + 1 KB alignment slack
+  pl.smem_bytes = pl.stages * pl.stage_bytes + 1024;  // + 1 KB alignment slack
   return pl;
 }
 
