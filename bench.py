@@ -17,6 +17,11 @@ API with host buffers, the roofline of the grouped expert GEMMs, clocks
 sampled during the timed region, and the CPU baseline (the NumPy oracle's
 ragged formulation on a bounded sample, rank 0 at N=1 only).
 
+``--profile-small`` runs two calls of a reduced layer (32 experts, top-2,
+T=4096: the same ~256 routed rows per expert, 151 MB of expert weights) and
+exits; it is the workload the committed ncu summaries capture with the full
+metric set (the full layer is captured with single-pass metrics only).
+
 ``--impl reference`` times the reference arm instead: kappa itself is JAX,
 which is not installed here, so the arm runs the oracle restatement of
 kappa's ``_moe_ragged`` path on the host cores (rank 0 only).
@@ -213,6 +218,33 @@ def run_reference(args):
         "wall_s": elapsed,
     }
     print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_profile_small():
+    """Two calls of the reduced layer used for ncu captures."""
+    import torch
+
+    from kappa_b200.qwen3 import ffn_moe as M
+    from kappa_b200.qwen3.architecture import MoEConfig
+    from kappa_b200.qwen3.quant import quantize_weight
+
+    e_small, k_small = 32, 2
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(0)
+
+    def q8(shape):
+        w = torch.randn(shape, generator=gen, device=dev, dtype=torch.float32) * 0.02
+        return quantize_weight(w, per_channel=True, scale_dtype=torch.float32)
+
+    router, gate, up, down = q8((D, e_small)), q8((e_small, D, I)), q8((e_small, D, I)), q8((e_small, I, D))
+    x = torch.randn((1, T_TOK, D), generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    cfg = MoEConfig(use_moe=True, num_experts=e_small, num_experts_per_tok=k_small, moe_impl="ragged_jax")
+    for _ in range(2):
+        y = M.moe_swiglu_ffn(x, router, gate, up, down, cfg=cfg)
+    torch.cuda.synchronize(dev)
+    print(json.dumps({"profile_small": "ok", "mean_abs_out": float(y.float().abs().mean())}), flush=True)
     return 0
 
 
@@ -426,9 +458,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="kappa_b200", choices=["kappa_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-small", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.profile_small:
+        return run_profile_small()
     return run_gpu(args)
 
 
