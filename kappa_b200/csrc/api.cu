@@ -148,6 +148,7 @@ struct MoeBuffers {
   __nv_bfloat16* xs;
   __nv_bfloat16* h;
   float* acc;  // [T][D] fp32 accumulation of the fused combine
+  int32_t* perm_hist;  // per-block expert histograms of the permutation
 };
 
 struct ExpertBuffers {
@@ -184,6 +185,7 @@ MoeBuffers carve_moe(Carver& c, int64_t T, int64_t D, int64_t I, int64_t E, int 
   b.xs = c.take<__nv_bfloat16>(m * D);
   b.h = c.take<__nv_bfloat16>(m * I);
   b.acc = c.take<float>(T * D);
+  b.perm_hist = c.take<int32_t>(permute_hist_ints(E));
   return b;
 }
 
@@ -421,8 +423,8 @@ int kw8_moe_ffn(const void* x, int64_t T, int64_t D, int64_t I, int64_t E, int32
   const int64_t m = T * k;
   rc = kw8::route(x, T, D, E, k, router, b.logits, b.idx, b.w, stream);
   if (rc) return rc;
-  rc = launch_permute(b.idx, T, k, E, capacity, b.sorted_token, b.inv_pos, b.group_sizes,
-                      b.group_offsets, stream, b.w, b.sorted_w);
+  rc = launch_permute_multi(b.idx, T, k, E, capacity, b.perm_hist, b.sorted_token, b.inv_pos,
+                            b.group_sizes, b.group_offsets, stream, b.w, b.sorted_w);
   if (rc) return rc;
   rc = launch_gather(x, b.sorted_token, b.group_offsets + E, m, D, b.xs, stream);
   if (rc) return rc;

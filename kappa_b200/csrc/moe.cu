@@ -8,9 +8,10 @@ namespace {
 
 constexpr int kBlock = 1024;
 constexpr int kPermBatch = 16;  // 32-entry steps per lane fetched at once
+constexpr int kPermThreads = 256;
 
-// Block-wide exclusive scan of one int per thread (blockDim.x == kBlock).
-// Returns the exclusive prefix; *total receives the block sum.
+// Block-wide exclusive scan of one int per thread (blockDim.x a multiple of
+// 32).  Returns the exclusive prefix; *total receives the block sum.
 __device__ int block_exclusive_scan(int v, int* total) {
   __shared__ int warp_sums[32];
   __shared__ int total_sh;
@@ -24,7 +25,7 @@ __device__ int block_exclusive_scan(int v, int* total) {
   if (lane == 31) warp_sums[warp] = incl;
   __syncthreads();
   if (warp == 0) {
-    const int s = warp_sums[lane];
+    const int s = lane < static_cast<int>(blockDim.x >> 5) ? warp_sums[lane] : 0;
     int si = s;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -214,6 +215,123 @@ __global__ void __launch_bounds__(kBlock, 1)
   }
 }
 
+// ------------------------------------------- multi-block stable permute ----
+// The same permutation as permute_kernel, spread over up to kPermMaxBlocks
+// blocks of kPermThreads: block b owns the flat range [b*chunk, (b+1)*chunk).
+// Pass 1 writes each block's expert histogram; pass 2 gives every block its
+// first slot per expert (the counts of all lower blocks), the expert offsets
+// (scan of the capacity-clipped totals) and scatters its entries, ranking
+// equal experts within a 256-entry round by warp (ballot match) and lane.
+
+// Pass 1: hist[b][e] = entries of block b routed to expert e.
+__global__ void __launch_bounds__(kPermThreads)
+    permute_hist_kernel(const int32_t* __restrict__ idx, int m, int E, int chunk,
+                        int32_t* __restrict__ hist) {
+  extern __shared__ int cnt[];  // [E]
+  for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
+  const int beg = blockIdx.x * chunk;
+  const int end = min(m, beg + chunk);
+  for (int i = beg + threadIdx.x; i < end; i += blockDim.x) {
+    const int e = idx[i];
+    if (e >= 0 && e < E)
+      atomicAdd(&cnt[e], 1);
+    else
+      report(KW8_ERR_INVALID_ARG);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) hist[blockIdx.x * E + e] = cnt[e];
+}
+
+// Pass 2: offsets and stable scatter (see above).  Shared memory: base[E]
+// (this block's first slot per expert), goff[E] (expert offsets), run[E]
+// (entries of earlier rounds), wcnt[kPermThreads/32][E] (per-warp counts of
+// the current round, zero between rounds).
+__global__ void __launch_bounds__(kPermThreads)
+    permute_scatter_kernel(const int32_t* __restrict__ idx, int m, int k, int E, int capacity,
+                           int chunk, const int32_t* __restrict__ hist, int32_t* __restrict__ sorted_token,
+                           int32_t* __restrict__ inv_pos, int32_t* __restrict__ group_sizes,
+                           int32_t* __restrict__ group_offsets, const __nv_bfloat16* __restrict__ w,
+                           float* __restrict__ sorted_w) {
+  extern __shared__ int sm[];
+  constexpr int kWarps = kPermThreads / 32;
+  int* base = sm;
+  int* goff = sm + E;
+  int* run = sm + 2 * E;
+  int* wcnt = sm + 3 * E;
+  __shared__ int carry_sh;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int b = blockIdx.x, nblk = gridDim.x;
+
+  // Expert totals, this block's base, and the expert offsets.
+  if (threadIdx.x == 0) carry_sh = 0;
+  __syncthreads();
+  for (int e0 = 0; e0 < E; e0 += blockDim.x) {
+    const int e = e0 + threadIdx.x;
+    int kept = 0;
+    if (e < E) {
+      int pre = 0, tot = 0;
+      for (int bb = 0; bb < nblk; ++bb) {
+        const int h = hist[bb * E + e];
+        pre += (bb < b) ? h : 0;
+        tot += h;
+      }
+      base[e] = pre;
+      run[e] = 0;
+      kept = capacity >= 0 ? min(tot, capacity) : tot;
+      for (int ww = 0; ww < kWarps; ++ww) wcnt[ww * E + e] = 0;
+    }
+    int total;
+    const int off = block_exclusive_scan(kept, &total);
+    const int carry = carry_sh;
+    if (e < E) {
+      goff[e] = carry + off;
+      if (b == 0) {
+        group_sizes[e] = kept;
+        group_offsets[e] = carry + off;
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) carry_sh = carry + total;
+    __syncthreads();
+  }
+  if (b == 0 && threadIdx.x == 0) group_offsets[E] = carry_sh;
+
+  const int beg = b * chunk;
+  const int end = min(m, beg + chunk);
+  for (int r0 = beg; r0 < end; r0 += blockDim.x) {
+    const int i = r0 + threadIdx.x;
+    int e = (i < end) ? idx[i] : -1;
+    if (e >= E || e < 0) e = -1;
+    const float wv = (e >= 0 && sorted_w != nullptr) ? __bfloat162float(w[i]) : 0.f;
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int lrank = __popc(peers & ((1u << lane) - 1u));
+    const bool leader = lrank == 0;
+    if (e >= 0 && leader) wcnt[warp * E + e] = __popc(peers);
+    __syncthreads();
+    if (e >= 0) {
+      int slot = base[e] + run[e] + lrank;
+      for (int ww = 0; ww < warp; ++ww) slot += wcnt[ww * E + e];
+      if (capacity < 0 || slot < capacity) {
+        const int p = goff[e] + slot;
+        sorted_token[p] = i / k;
+        inv_pos[i] = p;
+        if (sorted_w != nullptr) sorted_w[p] = wv;
+      } else {
+        inv_pos[i] = -1;
+      }
+    } else if (i < end) {
+      inv_pos[i] = -1;
+    }
+    __syncthreads();
+    if (e >= 0 && leader) {
+      wcnt[warp * E + e] = 0;
+      atomicAdd(&run[e], __popc(peers));
+    }
+    __syncthreads();
+  }
+}
+
 // Tile table: every group's rows cut into ceil(n / nt) runs of near-equal
 // length (at most `nt` rows each).
 __global__ void __launch_bounds__(kBlock, 1)
@@ -360,6 +478,42 @@ int launch_permute(const int32_t* idx, int64_t T, int k, int64_t E, int64_t capa
   permute_kernel<<<1, kBlock, smem, stream>>>(idx, m, k, static_cast<int>(E), cap, sorted_token,
                                               inv_pos, group_sizes, group_offsets,
                                               static_cast<const __nv_bfloat16*>(w), sorted_w);
+  KW8_CHECK_LAUNCH();
+  return KW8_OK;
+}
+
+int64_t permute_hist_ints(int64_t E) { return static_cast<int64_t>(kPermMaxBlocks) * E; }
+
+int launch_permute_multi(const int32_t* idx, int64_t T, int k, int64_t E, int64_t capacity,
+                         int32_t* hist, int32_t* sorted_token, int32_t* inv_pos,
+                         int32_t* group_sizes, int32_t* group_offsets, cudaStream_t stream,
+                         const void* w, float* sorted_w) {
+  KW8_REQUIRE(E >= 1 && E <= 1024, KW8_ERR_UNSUPPORTED, "permute supports 1..1024 experts");
+  KW8_REQUIRE(k >= 1 && T >= 0 && T * k < (1ll << 31), KW8_ERR_INVALID_ARG, "bad T/k");
+  const int m = static_cast<int>(T * k);
+  const int cap = capacity < 0 ? -1 : static_cast<int>(std::min<int64_t>(capacity, 1ll << 30));
+  // Blocks of whole 256-entry rounds, at most kPermMaxBlocks of them.
+  int nblk = std::max(1, std::min(kPermMaxBlocks, (m + kPermThreads - 1) / kPermThreads));
+  int chunk = (m + nblk - 1) / nblk;
+  chunk = (chunk + kPermThreads - 1) / kPermThreads * kPermThreads;
+  if (chunk == 0) chunk = kPermThreads;
+  nblk = std::max(1, (m + chunk - 1) / chunk);
+  const size_t smem1 = static_cast<size_t>(E) * sizeof(int);
+  const size_t smem2 = static_cast<size_t>(3 + kPermThreads / 32) * E * sizeof(int);
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  KW8_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    KW8_CUDA_TRY(cudaFuncSetAttribute(permute_scatter_kernel,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>((3 + kPermThreads / 32) * 1024 * sizeof(int))));
+    attr_set[dev] = true;
+  }
+  permute_hist_kernel<<<nblk, kPermThreads, smem1, stream>>>(idx, m, static_cast<int>(E), chunk, hist);
+  KW8_CHECK_LAUNCH();
+  permute_scatter_kernel<<<nblk, kPermThreads, smem2, stream>>>(
+      idx, m, k, static_cast<int>(E), cap, chunk, hist, sorted_token, inv_pos, group_sizes,
+      group_offsets, static_cast<const __nv_bfloat16*>(w), sorted_w);
   KW8_CHECK_LAUNCH();
   return KW8_OK;
 }
