@@ -8,8 +8,10 @@ A step is one Qwen3-30B-A3B-shaped W8 MoE layer (D=2048, I=768, 128 experts,
 top-8, per-channel int8 weights with fp32 scales) over a T=4096-token
 prefill chunk, x ~ N(0,1) bf16, weights ~ N(0, 0.02) quantised on the GPU,
 seed 0 (+rank for x).  Synthetic data of BASELINE's shapes and
-distributions; no checkpoint.  With N>1 every rank runs its own 4096 tokens
-through its own copy of the layer (weak scaling, no data-path collective).
+distributions; no checkpoint.  With N>1 the layer runs expert-parallel
+rank r holds experts [r*128/N, (r+1)*128/N) and its own
+4096 tokens (weak scaling); routed rows go to their experts' ranks and back
+with NCCL all-to-alls (kappa_b200.qwen3.sharding.moe_swiglu_ffn_ep).
 
 Prints one JSON line (rank 0): whole-job tokens/s from CUDA events over K
 steps (max over ranks), the end-to-end number through the public Python
@@ -257,6 +259,7 @@ def run_gpu(args):
     from kappa_b200.qwen3.architecture import MoEConfig
     from kappa_b200.qwen3.ffn_moe import moe_swiglu_ffn
     from kappa_b200.qwen3.quant import kmajor, quantize_weight
+    from kappa_b200.qwen3.sharding import moe_swiglu_ffn_ep, shard_experts
 
     world, rank, local = _dist()
     if world != args.gpus:
@@ -291,11 +294,19 @@ def run_gpu(args):
     stream = torch.cuda.current_stream(dev)
     sptr = stream.cuda_stream
 
-    def step():
-        rc = lib.kw8_moe_ffn(x.data_ptr(), T_TOK, D, I, E, K_TOP, -1, sr, sg, su, sd, out.data_ptr(),
-                             ws.data_ptr(), ws_bytes, sptr)
-        if rc != 0:
-            raise RuntimeError(_lib.last_error())
+    cfg = MoEConfig(use_moe=True, num_experts=E, num_experts_per_tok=K_TOP, moe_impl="ragged_jax")
+    if world > 1:
+        g_loc, u_loc, d_loc = shard_experts(gate, up, down, rank, world)
+
+        def step():
+            moe_swiglu_ffn_ep(x, router, g_loc, u_loc, d_loc, cfg=cfg)
+    else:
+
+        def step():
+            rc = lib.kw8_moe_ffn(x.data_ptr(), T_TOK, D, I, E, K_TOP, -1, sr, sg, su, sd, out.data_ptr(),
+                                 ws.data_ptr(), ws_bytes, sptr)
+            if rc != 0:
+                raise RuntimeError(_lib.last_error())
 
     def barrier():
         if world > 1:
@@ -322,7 +333,11 @@ def run_gpu(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     value = world * T_TOK * args.steps / (ms / 1e3)
-    launches_per_step = 8  # router GEMM, top-k, permute, gather, tile table, gate/up, down, combine
+    # Our kernels per step.  1 GPU (kw8_moe_ffn): router GEMM, top-k, permute
+    # (2 passes), gather, tile table, gate/up, down + combine, f32->bf16.
+    # EP: router GEMM, top-k, permute (2), tile table, gate/up, down, combine
+    # (the row gather and the all-to-alls are torch / NCCL).
+    launches_per_step = 9 if world == 1 else 8
 
     # ---- roofline of the dominant kernels: grouped expert GEMMs ----
     # Same rows as the step (permuted x), timed alone with events on the
@@ -357,11 +372,13 @@ def run_gpu(args):
     # ---- end to end through the public API with host buffers ----
     x_host = x.cpu().pin_memory()
     y_host = torch.empty(x.shape, dtype=torch.bfloat16).pin_memory()
-    cfg = MoEConfig(use_moe=True, num_experts=E, num_experts_per_tok=K_TOP, moe_impl="ragged_jax")
 
     def e2e_step():
         xd = x_host.to(dev, non_blocking=True)
-        y = moe_swiglu_ffn(xd, router, gate, up, down, cfg=cfg)
+        if world > 1:
+            y = moe_swiglu_ffn_ep(xd, router, g_loc, u_loc, d_loc, cfg=cfg)
+        else:
+            y = moe_swiglu_ffn(xd, router, gate, up, down, cfg=cfg)
         y_host.copy_(y, non_blocking=True)
 
     for _ in range(3):
@@ -422,7 +439,7 @@ def run_gpu(args):
             "I": I,
             "experts": E,
             "top_k": K_TOP,
-            "parallelism": "replicas" if world > 1 else "single",
+            "parallelism": f"ep{world}" if world > 1 else "single",
             "l2": "inputs larger than L2 (604 MB int8 expert weights read every step)",
         },
         "roofline": {

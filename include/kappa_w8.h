@@ -162,6 +162,15 @@ int kw8_moe_permute(const int32_t* idx, int64_t T, int32_t k, int64_t E,
                     int32_t* group_sizes, int32_t* group_offsets,
                     kw8_stream_t stream);
 
+/* kw8_moe_permute with scratch (same outputs): the sort runs over up to 148
+ * blocks instead of one; workspace >= kw8_moe_permute_workspace_size(E)
+ * bytes.  No counterpart in kappa beyond the function above.               */
+size_t kw8_moe_permute_workspace_size(int64_t E);
+int kw8_moe_permute_ws(const int32_t* idx, int64_t T, int32_t k, int64_t E,
+                       int64_t capacity, int32_t* sorted_token, int32_t* inv_pos,
+                       int32_t* group_sizes, int32_t* group_offsets,
+                       void* workspace, size_t workspace_bytes, kw8_stream_t stream);
+
 /* Expert FFN over permuted rows: the three ragged_dot calls and the SwiGLU
  * of _moe_ragged (kappa/qwen3/ffn_moe.py:202-210), run as grouped W8A16
  * GEMMs.  xs [rows][D] bf16 sorted by expert; group_offsets [E+1] on device;

@@ -81,6 +81,8 @@ SIGNATURES: dict[str, tuple] = {
     "kw8_moe_route": (ctypes.c_int, [_vp, _i64, _i64, _i64, _i32, KW8Weight, _vp, _vp, _vp, _vp]),
     "kw8_moe_topk": (ctypes.c_int, [_vp, _i64, _i64, _i32, _vp, _vp, _vp]),
     "kw8_moe_permute": (ctypes.c_int, [_vp, _i64, _i32, _i64, _i64, _vp, _vp, _vp, _vp, _vp]),
+    "kw8_moe_permute_workspace_size": (ctypes.c_size_t, [_i64]),
+    "kw8_moe_permute_ws": (ctypes.c_int, [_vp, _i64, _i32, _i64, _i64, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
     "kw8_moe_expert_ffn_workspace_size": (_sz, [_i64, _i64, _i64, _i64]),
     "kw8_moe_expert_ffn": (
         ctypes.c_int,

@@ -362,6 +362,26 @@ int kw8_moe_permute(const int32_t* idx, int64_t T, int32_t k, int64_t E, int64_t
                         stream);
 }
 
+size_t kw8_moe_permute_workspace_size(int64_t E) {
+  return static_cast<size_t>(permute_hist_ints(E > 0 ? E : 0)) * sizeof(int32_t);
+}
+
+int kw8_moe_permute_ws(const int32_t* idx, int64_t T, int32_t k, int64_t E, int64_t capacity,
+                       int32_t* sorted_token, int32_t* inv_pos, int32_t* group_sizes,
+                       int32_t* group_offsets, void* workspace, size_t workspace_bytes,
+                       kw8_stream_t stream) {
+  KW8_API_BEGIN
+  KW8_REQUIRE(idx && sorted_token && inv_pos && group_sizes && group_offsets, KW8_ERR_INVALID_ARG,
+              "null pointer");
+  KW8_REQUIRE(E >= 1, KW8_ERR_INVALID_ARG, "E=%lld invalid", (long long)E);
+  KW8_REQUIRE(workspace != nullptr && workspace_bytes >= kw8_moe_permute_workspace_size(E) &&
+                  (reinterpret_cast<uintptr_t>(workspace) & 3) == 0,
+              KW8_ERR_WORKSPACE, "permute workspace too small (%zu < %zu)", workspace_bytes,
+              kw8_moe_permute_workspace_size(E));
+  return launch_permute_multi(idx, T, k, E, capacity, static_cast<int32_t*>(workspace), sorted_token,
+                              inv_pos, group_sizes, group_offsets, stream, nullptr, nullptr);
+}
+
 size_t kw8_moe_expert_ffn_workspace_size(int64_t rows, int64_t D, int64_t I, int64_t E) {
   (void)D;
   Carver c(nullptr, SIZE_MAX);

@@ -117,8 +117,12 @@ def topk_softmax(logits: torch.Tensor, k: int):
     return idx, w
 
 
-def permute(idx: torch.Tensor, num_experts: int, capacity: int | None = None):
-    """Stable expert sort (ffn_moe.py:196-200) -> (sorted_token, inv_pos, group_sizes, group_offsets)."""
+def permute(idx: torch.Tensor, num_experts: int, capacity: int | None = None, *, single_block: bool = False):
+    """Stable expert sort (ffn_moe.py:196-200) -> (sorted_token, inv_pos, group_sizes, group_offsets).
+
+    Runs the multi-block sort (``kw8_moe_permute_ws``); ``single_block=True``
+    runs the scratch-free one-block kernel (``kw8_moe_permute``) instead.
+    """
     _lib.require_cuda(idx, "idx")
     if idx.dtype != torch.int32 or idx.dim() != 2:
         raise ValueError("idx must be [T, k] int32")
@@ -130,13 +134,23 @@ def permute(idx: torch.Tensor, num_experts: int, capacity: int | None = None):
     inv_pos = torch.empty((m,), dtype=torch.int32, device=dev)
     sizes = torch.empty((num_experts,), dtype=torch.int32, device=dev)
     offsets = torch.empty((num_experts + 1,), dtype=torch.int32, device=dev)
-    _lib.check(
-        _lib.load().kw8_moe_permute(
-            ic.data_ptr(), T, k, num_experts, -1 if capacity is None else int(capacity),
-            sorted_token.data_ptr(), inv_pos.data_ptr(), sizes.data_ptr(), offsets.data_ptr(),
-            _lib.stream_of(ic),
+    cap = -1 if capacity is None else int(capacity)
+    lib = _lib.load()
+    if single_block:
+        _lib.check(
+            lib.kw8_moe_permute(
+                ic.data_ptr(), T, k, num_experts, cap, sorted_token.data_ptr(), inv_pos.data_ptr(),
+                sizes.data_ptr(), offsets.data_ptr(), _lib.stream_of(ic),
+            )
         )
-    )
+    else:
+        ws = torch.empty(int(lib.kw8_moe_permute_workspace_size(num_experts)), dtype=torch.uint8, device=dev)
+        _lib.check(
+            lib.kw8_moe_permute_ws(
+                ic.data_ptr(), T, k, num_experts, cap, sorted_token.data_ptr(), inv_pos.data_ptr(),
+                sizes.data_ptr(), offsets.data_ptr(), ws.data_ptr(), ws.numel(), _lib.stream_of(ic),
+            )
+        )
     return sorted_token, inv_pos, sizes, offsets
 
 

@@ -1,0 +1,293 @@
+"""Multi-GPU W8 FFN: tensor parallel dense MLP and expert parallel MoE.
+
+One process per GPU, ``torch.distributed`` (NCCL) for the exchanges; every
+rank runs the single-GPU kernels on its shard.
+
+Dense MLP (kappa/qwen3/sharding.py:127-132, GSPMD there): gate/up (Gemma's
+gating) split on the hidden axis H (column parallel), down (Gemma's linear)
+split on H (row parallel).  Per-channel scales follow their output channels:
+gate/up scales are split with H, down scales (per model-dim channel) are
+replicated, a per-tensor scale is replicated (sharding.py:109-112).  Each
+rank computes its fp32 partial of the layer output; one all-reduce (fp32,
+so the sum is not rounded per rank) and one cast give the bf16 output.
+
+MoE, expert parallel (not in kappa): rank r holds experts
+[r*E/R, (r+1)*E/R) and its own tokens; the router is replicated.
+* prefill (``moe_swiglu_ffn_ep``): route and stably sort the rank's routed
+  rows by expert (rows for one rank's experts are then contiguous), exchange
+  per-expert counts, all-to-allv the sorted rows to their experts' ranks,
+  regroup the received rows by local expert, run the grouped expert FFN,
+  send the outputs back the same way, and combine locally.  Each rank's
+  result equals the single-GPU layer on that rank's tokens.
+* decode (``moe_swiglu_ffn_ep_decode``): x is replicated (B x D is small);
+  every rank routes all tokens, runs only its local experts' rows and adds
+  their weighted outputs into an fp32 partial; one all-reduce sums them.
+
+The compute steps go through an ``ops`` object (default: the B200 kernels),
+so the exchange logic also runs on CPU ranks (gloo) in the tests.
+"""
+
+from __future__ import annotations
+
+from typing import Protocol
+
+import torch
+import torch.distributed as dist
+
+from kappa_b200.qwen3.quant import Q8Weight, Weight
+
+__all__ = [
+    "shard_output_channels",
+    "shard_input_channels",
+    "shard_dense_swiglu",
+    "shard_gemma_mlp",
+    "shard_experts",
+    "swiglu_ffn_tp",
+    "feed_forward_tp",
+    "moe_swiglu_ffn_ep",
+    "moe_swiglu_ffn_ep_decode",
+    "MoEOps",
+    "KernelMoEOps",
+    "regroup_index",
+]
+
+
+def _world(group) -> tuple[int, int]:
+    return dist.get_world_size(group), dist.get_rank(group)
+
+
+def _span(n: int, rank: int, world: int, what: str) -> slice:
+    if n % world:
+        raise ValueError(f"{what}={n} is not divisible by the {world} ranks")
+    c = n // world
+    return slice(rank * c, (rank + 1) * c)
+
+
+def _q8(w: Weight, name: str) -> Q8Weight:
+    if not isinstance(w, Q8Weight):
+        raise TypeError(f"{name}: expected a Q8Weight")
+    return w
+
+
+def shard_output_channels(w: Weight, rank: int, world: int, axis: int) -> Q8Weight:
+    """Column-parallel shard: output axis ``axis`` split, per-channel scales with it."""
+    q = _q8(w, "weight")
+    v = q.values
+    ax = axis % v.dim()
+    sl = [slice(None)] * v.dim()
+    sl[ax] = _span(int(v.shape[ax]), rank, world, "output channels")
+    values = v[tuple(sl)]
+    scale = q.scale
+    if scale.dim() == v.dim() and int(scale.shape[ax]) == int(v.shape[ax]):
+        scale = scale[tuple(sl)]
+    return Q8Weight(values=values, scale=scale)
+
+
+def shard_input_channels(w: Weight, rank: int, world: int, axis: int) -> Q8Weight:
+    """Row-parallel shard: contraction axis ``axis`` split, scales replicated."""
+    q = _q8(w, "weight")
+    v = q.values
+    ax = axis % v.dim()
+    sl = [slice(None)] * v.dim()
+    sl[ax] = _span(int(v.shape[ax]), rank, world, "input channels")
+    return Q8Weight(values=v[tuple(sl)], scale=q.scale)
+
+
+def shard_dense_swiglu(gate_w: Weight, up_w: Weight, down_w: Weight, rank: int, world: int):
+    """Qwen3 dense MLP shards: gate/up ``[D, I]`` split on I, down ``[I, D]`` split on I."""
+    return (
+        shard_output_channels(gate_w, rank, world, -1),
+        shard_output_channels(up_w, rank, world, -1),
+        shard_input_channels(down_w, rank, world, -2),
+    )
+
+
+def shard_gemma_mlp(gating_w: Weight, linear_w: Weight, rank: int, world: int, *, transpose_gating_einsum: bool):
+    """Gemma3 MLP shards: gating ``[2, H, D]`` (or ``[2, D, H]``) split on H, linear ``[H, D]`` on H."""
+    g = shard_output_channels(gating_w, rank, world, 1 if transpose_gating_einsum else 2)
+    return g, shard_input_channels(linear_w, rank, world, 0)
+
+
+def shard_experts(ffn_gate: Weight, ffn_up: Weight, ffn_down: Weight, rank: int, world: int):
+    """Expert-parallel shards: experts ``[r*E/R, (r+1)*E/R)`` of ``[E, ...]`` weights and scales."""
+    out = []
+    for w in (ffn_gate, ffn_up, ffn_down):
+        q = _q8(w, "expert weight")
+        sl = _span(int(q.values.shape[0]), rank, world, "experts")
+        scale = q.scale[sl] if q.scale.dim() == q.values.dim() else q.scale
+        out.append(Q8Weight(values=q.values[sl], scale=scale))
+    return tuple(out)
+
+
+def _allreduce_to_bf16(partial: torch.Tensor, group) -> torch.Tensor:
+    dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=group)
+    return partial.to(torch.bfloat16)
+
+
+def swiglu_ffn_tp(x: torch.Tensor, gate_shard: Weight, up_shard: Weight, down_shard: Weight, *, group=None):
+    """Tensor-parallel kappa/qwen3/ffn.py:swiglu_ffn over this rank's shards."""
+    from kappa_b200.qwen3.ffn import swiglu_ffn
+
+    partial = swiglu_ffn(x, gate_shard, up_shard, down_shard, out_dtype=torch.float32)
+    return _allreduce_to_bf16(partial, group)
+
+
+def feed_forward_tp(x: torch.Tensor, gating_shard: Weight, linear_shard: Weight, *, transpose_gating_einsum: bool,
+                    group=None):
+    """Tensor-parallel kappa/gemma3/ffn.py:feed_forward over this rank's shards."""
+    from kappa_b200.gemma3.ffn import feed_forward
+
+    partial = feed_forward(x, gating_shard, linear_shard, transpose_gating_einsum=transpose_gating_einsum,
+                           out_dtype=torch.float32)
+    return _allreduce_to_bf16(partial, group)
+
+
+class MoEOps(Protocol):
+    """The per-rank compute steps of the MoE layer (see module docstring)."""
+
+    def route(self, x_flat: torch.Tensor, router_w: Weight, num_experts: int, k: int): ...
+
+    def permute(self, idx: torch.Tensor, num_experts: int, capacity: int | None): ...
+
+    def gather(self, x_flat: torch.Tensor, sorted_token: torch.Tensor, rows: int) -> torch.Tensor: ...
+
+    def experts(self, xs: torch.Tensor, group_offsets: torch.Tensor, gate: Weight, up: Weight,
+                down: Weight) -> torch.Tensor: ...
+
+    def combine(self, ys: torch.Tensor, inv_pos: torch.Tensor, w: torch.Tensor, d: int) -> torch.Tensor: ...
+
+
+class KernelMoEOps:
+    """MoEOps on the B200 kernels (the staged C-ABI entry points)."""
+
+    def route(self, x_flat, router_w, num_experts, k):
+        from kappa_b200.qwen3 import ffn_moe
+
+        _, idx, w = ffn_moe.route_logits(x_flat.unsqueeze(0), router_w, num_experts=num_experts,
+                                         num_experts_per_tok=k)
+        return idx, w
+
+    def permute(self, idx, num_experts, capacity):
+        from kappa_b200.qwen3 import ffn_moe
+
+        return ffn_moe.permute(idx, num_experts, capacity)
+
+    def gather(self, x_flat, sorted_token, rows):
+        return x_flat.index_select(0, sorted_token[:rows].long())
+
+    def experts(self, xs, group_offsets, gate, up, down):
+        from kappa_b200.qwen3 import ffn_moe
+
+        if xs.shape[0] == 0:
+            return torch.empty_like(xs)
+        return ffn_moe.expert_ffn(xs, group_offsets, gate, up, down)
+
+    def combine(self, ys, inv_pos, w, d):
+        from kappa_b200.qwen3 import ffn_moe
+
+        return ffn_moe.combine(ys, inv_pos, w, d)
+
+
+def regroup_index(counts: torch.Tensor) -> torch.Tensor:
+    """Index that reorders rows received source-major into local-expert-major order.
+
+    ``counts[s][j]``: rows from source rank s for local expert j.  Received
+    rows are laid out ``for s: for j``; the result ``perm`` satisfies
+    ``regrouped = received[perm]`` with regrouped laid out ``for j: for s``.
+    """
+    c = counts.to(torch.int64)
+    world, e_loc = c.shape
+    flat_src = c.reshape(-1)
+    src_start = (torch.cumsum(flat_src, 0) - flat_src).reshape(world, e_loc)
+    lengths = c.t().reshape(-1)
+    dst_start = torch.cumsum(lengths, 0) - lengths
+    total = int(lengths.sum())
+    shift = src_start.t().reshape(-1) - dst_start
+    return torch.arange(total, device=c.device) + torch.repeat_interleave(shift, lengths, output_size=total)
+
+
+def _moe_args(cfg, x: torch.Tensor):
+    if not cfg.use_moe:
+        raise ValueError("moe_swiglu_ffn requires cfg.use_moe")
+    if x.dim() != 3:
+        raise ValueError(f"x must be [B, T, D], got shape {tuple(x.shape)}")
+    b, t, d = (int(s) for s in x.shape)
+    capacity = None
+    if cfg.moe_impl == "fixed_capacity":
+        from kappa_b200.qwen3.ffn_moe import fixed_capacity
+
+        if cfg.moe_capacity_factor <= 0:
+            raise ValueError("fixed_capacity requires cfg.moe_capacity_factor > 0")
+        capacity = fixed_capacity(cfg, b * t)
+    return b, t, d, capacity
+
+
+def moe_swiglu_ffn_ep(x: torch.Tensor, router_w: Weight, gate_local: Weight, up_local: Weight, down_local: Weight,
+                      *, cfg, group=None, ops: MoEOps | None = None) -> torch.Tensor:
+    """Expert-parallel MoE layer over this rank's tokens ``x`` ``[B, T, D]`` (prefill).
+
+    ``gate_local`` / ``up_local`` / ``down_local`` hold this rank's E/R experts
+    (``shard_experts``); ``router_w`` is the full router.  Returns the same
+    ``[B, T, D]`` bf16 as the single-GPU layer on ``x`` with every expert.
+    """
+    ops = ops or KernelMoEOps()
+    world, rank = _world(group)
+    e, k = cfg.num_experts, cfg.num_experts_per_tok
+    if e % world:
+        raise ValueError(f"{e} experts do not split over {world} ranks")
+    e_loc = e // world
+    b, t, d, capacity = _moe_args(cfg, x)
+    x_flat = x.reshape(b * t, d)
+    idx, w = ops.route(x_flat, router_w, e, k)
+    sorted_token, inv_pos, sizes, offsets = ops.permute(idx, e, capacity)
+    kept = int(offsets[e])
+    xs = ops.gather(x_flat, sorted_token, kept)
+    # Per-expert counts: rank r receives the counts of its experts from every source.
+    send_counts = sizes.to(torch.int64).contiguous()
+    recv_counts = torch.empty_like(send_counts)
+    dist.all_to_all_single(recv_counts, send_counts, group=group)
+    per_src = recv_counts.reshape(world, e_loc)
+    send_split = send_counts.reshape(world, e_loc).sum(1).tolist()
+    recv_split = per_src.sum(1).tolist()
+    recv_rows = xs.new_empty((sum(recv_split), d))
+    dist.all_to_all_single(recv_rows, xs, output_split_sizes=recv_split, input_split_sizes=send_split, group=group)
+    perm = regroup_index(per_src)
+    xs_loc = recv_rows.index_select(0, perm)
+    per_exp = per_src.sum(0)
+    loc_off = torch.zeros(e_loc + 1, dtype=torch.int32, device=x.device)
+    loc_off[1:] = torch.cumsum(per_exp, 0).to(torch.int32)
+    ys_loc = ops.experts(xs_loc, loc_off, gate_local, up_local, down_local)
+    recv_y = torch.empty_like(ys_loc)
+    recv_y.index_copy_(0, perm, ys_loc)
+    ys = xs.new_empty((kept, d))
+    dist.all_to_all_single(ys, recv_y, output_split_sizes=send_split, input_split_sizes=recv_split, group=group)
+    return ops.combine(ys, inv_pos, w, d).reshape(b, t, d)
+
+
+def moe_swiglu_ffn_ep_decode(x: torch.Tensor, router_w: Weight, gate_local: Weight, up_local: Weight,
+                             down_local: Weight, *, cfg, group=None, ops: MoEOps | None = None) -> torch.Tensor:
+    """Expert-parallel MoE layer for small, replicated batches (decode).
+
+    Every rank passes the same ``x``; each adds its local experts' weighted
+    outputs into an fp32 partial and one all-reduce sums them.
+    """
+    ops = ops or KernelMoEOps()
+    world, rank = _world(group)
+    e, k = cfg.num_experts, cfg.num_experts_per_tok
+    if e % world:
+        raise ValueError(f"{e} experts do not split over {world} ranks")
+    e_loc = e // world
+    b, t, d, capacity = _moe_args(cfg, x)
+    x_flat = x.reshape(b * t, d)
+    idx, w = ops.route(x_flat, router_w, e, k)
+    sorted_token, inv_pos, sizes, offsets = ops.permute(idx, e, capacity)
+    kept = int(offsets[e])
+    xs = ops.gather(x_flat, sorted_token, kept)
+    bounds = offsets[rank * e_loc: (rank + 1) * e_loc + 1].to(torch.int64)
+    lo, hi = (int(v) for v in bounds[[0, -1]].tolist())
+    ys = torch.zeros((kept, d), dtype=torch.bfloat16, device=x.device)
+    if hi > lo:
+        loc_off = (bounds - lo).to(torch.int32)
+        ys[lo:hi] = ops.experts(xs[lo:hi].contiguous(), loc_off, gate_local, up_local, down_local)
+    partial = ops.combine(ys, inv_pos, w, d).to(torch.float32)
+    return _allreduce_to_bf16(partial, group).reshape(b, t, d)

@@ -138,7 +138,8 @@ def test_topk_exact_on_given_logits(E, k):
 @pytest.mark.parametrize(
     "T,k,E,capacity,dist",
     [(1000, 8, 128, None, "uniform"), (513, 2, 8, None, "skewed"), (64, 8, 128, None, "one"),
-     (700, 4, 16, 100, "skewed"), (1, 8, 128, None, "uniform"), (4096, 8, 128, None, "uniform")],
+     (700, 4, 16, 100, "skewed"), (1, 8, 128, None, "uniform"), (4096, 8, 128, None, "uniform"),
+     (8192, 8, 256, None, "uniform"), (6000, 4, 64, 300, "skewed")],
 )
 def test_permute_exact(T, k, E, capacity, dist):
     rng = np.random.default_rng(T * 31 + E)
@@ -149,15 +150,16 @@ def test_permute_exact(T, k, E, capacity, dist):
         idx = np.stack([rng.choice(E, size=k, replace=False, p=p / p.sum()) for _ in range(T)]).astype(np.int32)
     else:
         idx = np.tile(np.arange(k, dtype=np.int32), (T, 1))
-    st, inv, sizes, offs = M.permute(to_dev(idx), E, capacity)
     order, o_sizes, _ = O.permute(idx, E, capacity)
-    np.testing.assert_array_equal(to_np(sizes), o_sizes)
-    np.testing.assert_array_equal(to_np(offs), np.concatenate([[0], np.cumsum(o_sizes)]))
     n = int(o_sizes.sum())
-    np.testing.assert_array_equal(to_np(st)[:n], order // k)
     inv_ref = np.full(T * k, -1, dtype=np.int32)
     inv_ref[order] = np.arange(n, dtype=np.int32)
-    np.testing.assert_array_equal(to_np(inv), inv_ref)
+    for single_block in (False, True):  # kw8_moe_permute_ws (multi-block) and kw8_moe_permute
+        st, inv, sizes, offs = M.permute(to_dev(idx), E, capacity, single_block=single_block)
+        np.testing.assert_array_equal(to_np(sizes), o_sizes)
+        np.testing.assert_array_equal(to_np(offs), np.concatenate([[0], np.cumsum(o_sizes)]))
+        np.testing.assert_array_equal(to_np(st)[:n], order // k)
+        np.testing.assert_array_equal(to_np(inv), inv_ref)
 
 
 @pytest.mark.parametrize("T,D,E,k,per_channel", [(300, 256, 16, 4, True), (64, 2048, 128, 8, False), (4096, 2048, 128, 8, True)])

@@ -1,0 +1,112 @@
+"""Multi-GPU paths on B200s (NCCL, 2 ranks): expert-parallel MoE (prefill and
+decode) and tensor-parallel dense MLPs, each checked against the fp32
+dequantise-then-dot reference.  Skipped with fewer than two GPUs."""
+
+from __future__ import annotations
+
+import os
+import socket
+import tempfile
+from datetime import timedelta
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import oracle as O
+from helpers import moe_weights, normal, parity, to_dev, to_np
+
+pytestmark = pytest.mark.gpu
+WORLD = 2
+
+
+def _gpu_q(w, in_axis=-2):
+    from kappa_b200.qwen3.quant import quantize_weight
+
+    return quantize_weight(to_dev(w), per_channel=True, scale_dtype=torch.float32, in_axis=in_axis)
+
+
+def _oracle_q(w, axis=-2):
+    return O.quantize_weight(w, per_channel_axis=axis, scale_dtype=np.float32)
+
+
+def _rank_main(rank: int, world: int, port: int, errfile: str):
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+        from kappa_b200.qwen3 import sharding as S
+        from kappa_b200.qwen3.architecture import MoEConfig
+
+        # ---------------------------------------------------- MoE, EP ----
+        D, I, E, K = 512, 256, 16, 4
+        rng = np.random.default_rng(0)
+        r, g, u, dn = moe_weights(rng, D, I, E)
+        router, gate, up, down = (_gpu_q(a) for a in (r, g, u, dn))
+        o_router, o_gate, o_up, o_down = (_oracle_q(a) for a in (r, g, u, dn))
+        gl, ul, dl = S.shard_experts(gate, up, down, rank, world)
+        cfg = MoEConfig(use_moe=True, num_experts=E, num_experts_per_tok=K, moe_impl="ragged_jax")
+        x = normal(np.random.default_rng(100 + rank), (1, 300 + 50 * rank, D)).astype(O.BF16)
+        y = S.moe_swiglu_ffn_ep(to_dev(x, dev), router, gl, ul, dl, cfg=cfg)
+        # reference on this rank's tokens with the routing the GPU chose
+        from kappa_b200.qwen3 import ffn_moe as M
+
+        _, idx, w = M.route_logits(to_dev(x, dev), router, num_experts=E, num_experts_per_tok=K)
+        ref, _, _ = O.moe_reference_f32(x, o_router, o_gate, o_up, o_down, num_experts=E, k=K,
+                                        idx=to_np(idx), w=to_np(w))
+        parity(to_np(y), ref, tol=2e-2)
+        # decode: the same x on both ranks
+        xd = normal(np.random.default_rng(7), (1, 8, D)).astype(O.BF16)
+        yd = S.moe_swiglu_ffn_ep_decode(to_dev(xd, dev), router, gl, ul, dl, cfg=cfg)
+        _, idx, w = M.route_logits(to_dev(xd, dev), router, num_experts=E, num_experts_per_tok=K)
+        ref_d, _, _ = O.moe_reference_f32(xd, o_router, o_gate, o_up, o_down, num_experts=E, k=K,
+                                          idx=to_np(idx), w=to_np(w))
+        parity(to_np(yd), ref_d, tol=2e-2)
+
+        # ------------------------------------------------ dense MLP, TP ----
+        Dd, H = 512, 1024
+        rng2 = np.random.default_rng(3)
+        gw, uw, dw = normal(rng2, (Dd, H), 0.02), normal(rng2, (Dd, H), 0.02), normal(rng2, (H, Dd), 0.02)
+        xm = normal(np.random.default_rng(11), (1, 200, Dd)).astype(O.BF16)
+        gs, us, ds = S.shard_dense_swiglu(_gpu_q(gw), _gpu_q(uw), _gpu_q(dw), rank, world)
+        y = S.swiglu_ffn_tp(to_dev(xm, dev), gs, us, ds)
+        ref = O.swiglu_ffn(xm, _oracle_q(gw), _oracle_q(uw), _oracle_q(dw), compute_dtype=np.float32)
+        parity(to_np(y), ref)
+        gg = normal(rng2, (2, H, Dd), 0.02)
+        ll = normal(rng2, (H, Dd), 0.02)
+        gsh, lsh = S.shard_gemma_mlp(_gpu_q(gg, in_axis=-1), _gpu_q(ll), rank, world, transpose_gating_einsum=True)
+        y = S.feed_forward_tp(to_dev(xm, dev), gsh, lsh, transpose_gating_einsum=True)
+        ref = O.feed_forward(xm, _oracle_q(gg, -1), _oracle_q(ll), transpose_gating_einsum=True,
+                             compute_dtype=np.float32)
+        parity(to_np(y), ref)
+        torch.cuda.synchronize()
+        dist.barrier(device_ids=[rank])
+        dist.destroy_process_group()
+    except BaseException as exc:
+        with open(errfile, "a") as f:
+            f.write(f"rank {rank}: {type(exc).__name__}: {exc}\n")
+        raise
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+def test_ep_tp_two_gpus():
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    with tempfile.NamedTemporaryFile("w+", suffix=".log", delete=False) as f:
+        errfile = f.name
+    try:
+        mp.start_processes(_rank_main, args=(WORLD, _free_port(), errfile), nprocs=WORLD, start_method="spawn")
+    except Exception:
+        with open(errfile) as f:
+            pytest.fail(f.read() or "a rank failed")
+    finally:
+        os.unlink(errfile)
