@@ -11,7 +11,8 @@ seed 0 (+rank for x).  Synthetic data of BASELINE's shapes and
 distributions; no checkpoint.  With N>1 the layer runs expert-parallel
 rank r holds experts [r*128/N, (r+1)*128/N) and its own
 4096 tokens (weak scaling); routed rows go to their experts' ranks and back
-with NCCL all-to-alls (kappa_b200.qwen3.sharding.moe_swiglu_ffn_ep).
+over NVLink with peer-to-peer kernels (kappa_b200.qwen3.sharding
+.moe_swiglu_ffn_ep with an EPContext).
 
 Prints one JSON line (rank 0): whole-job tokens/s from CUDA events over K
 steps (max over ranks), the end-to-end number through the public Python
@@ -259,7 +260,7 @@ def run_gpu(args):
     from kappa_b200.qwen3.architecture import MoEConfig
     from kappa_b200.qwen3.ffn_moe import moe_swiglu_ffn
     from kappa_b200.qwen3.quant import kmajor, quantize_weight
-    from kappa_b200.qwen3.sharding import moe_swiglu_ffn_ep, shard_experts
+    from kappa_b200.qwen3.sharding import EPContext, moe_swiglu_ffn_ep, shard_experts
 
     world, rank, local = _dist()
     if world != args.gpus:
@@ -295,11 +296,13 @@ def run_gpu(args):
     sptr = stream.cuda_stream
 
     cfg = MoEConfig(use_moe=True, num_experts=E, num_experts_per_tok=K_TOP, moe_impl="ragged_jax")
+    ep_ctx = None
     if world > 1:
         g_loc, u_loc, d_loc = shard_experts(gate, up, down, rank, world)
+        ep_ctx = EPContext(max_tokens=T_TOK, d=D, k=K_TOP, hidden=I, num_experts=E)
 
         def step():
-            moe_swiglu_ffn_ep(x, router, g_loc, u_loc, d_loc, cfg=cfg)
+            moe_swiglu_ffn_ep(x, router, g_loc, u_loc, d_loc, cfg=cfg, ctx=ep_ctx)
     else:
 
         def step():
@@ -335,9 +338,9 @@ def run_gpu(args):
     value = world * T_TOK * args.steps / (ms / 1e3)
     # Our kernels per step.  1 GPU (kw8_moe_ffn): router GEMM, top-k, permute
     # (2 passes), gather, tile table, gate/up, down + combine, f32->bf16.
-    # EP: router GEMM, top-k, permute (2), tile table, gate/up, down, combine
-    # (the row gather and the all-to-alls are torch / NCCL).
-    launches_per_step = 9 if world == 1 else 8
+    # EP: router GEMM, top-k, permute (2), dispatch, local offsets, tile
+    # table, gate/up, down, return, combine (+ NCCL all-gather / all-reduces).
+    launches_per_step = 9 if world == 1 else 11
 
     # ---- roofline of the dominant kernels: grouped expert GEMMs ----
     # Same rows as the step (permuted x), timed alone with events on the
@@ -376,7 +379,7 @@ def run_gpu(args):
     def e2e_step():
         xd = x_host.to(dev, non_blocking=True)
         if world > 1:
-            y = moe_swiglu_ffn_ep(xd, router, g_loc, u_loc, d_loc, cfg=cfg)
+            y = moe_swiglu_ffn_ep(xd, router, g_loc, u_loc, d_loc, cfg=cfg, ctx=ep_ctx)
         else:
             y = moe_swiglu_ffn(xd, router, gate, up, down, cfg=cfg)
         y_host.copy_(y, non_blocking=True)
@@ -415,6 +418,7 @@ def run_gpu(args):
         }
 
     if world > 1:
+        ep_ctx.close()
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
     if rank != 0:

@@ -227,6 +227,48 @@ int kw8_moe_ffn_noalloc(const void* x, int64_t T, int64_t D, int64_t I,
                         kw8_weight router, kw8_weight gate, kw8_weight up,
                         kw8_weight down, void* out, kw8_stream_t stream);
 
+/* ------------------------------------------------------ expert parallel -- */
+
+/* Expert-parallel MoE row movement (no counterpart in kappa, which never
+ * shards experts).  Rank r of `world` owns experts [r*E/world,
+ * (r+1)*E/world).  counts [world][E] int32 (device): every rank's kept rows
+ * per expert (an all-gather of group_sizes).  Every placement follows from
+ * counts: rank r's receive buffer is expert-major, source-major within an
+ * expert; a source's return buffer is in its permutation's (expert) order.
+ * Rows move with plain peer-to-peer stores over NVLink into buffers mapped
+ * with CUDA IPC; peer_recv / peer_out are device arrays of `world` mapped
+ * addresses.  The caller orders the phases across ranks (a collective
+ * between dispatch and the expert FFN, and between return and combine).
+ *
+ * kw8_ipc_*: device buffers shareable between the ranks' processes
+ * (cudaMalloc + cudaIpcGetMemHandle; handles of kw8_ipc_handle_size()
+ * bytes are exchanged by the caller).                                       */
+size_t kw8_ipc_handle_size(void);
+int kw8_ipc_alloc(size_t bytes, void** ptr_out, void* handle_out);
+int kw8_ipc_free(void* ptr);
+int kw8_ipc_open(const void* handle, void** ptr_out);
+int kw8_ipc_close(void* ptr);
+
+/* Row p of this rank's sorted order (sorted_token / group_offsets from the
+ * permutation, p < group_offsets[E] <= max_rows) -> x[sorted_token[p]]
+ * written into its expert owner's receive buffer.  x [T][D] bf16.          */
+int kw8_ep_dispatch(const void* x, int64_t max_rows, int64_t D,
+                    const int32_t* sorted_token, const int32_t* group_offsets,
+                    const int32_t* counts, int32_t world, int32_t rank,
+                    int64_t E, const uint64_t* peer_recv, kw8_stream_t stream);
+
+/* Rows of this rank's receive layout (expert outputs ys [rows][D] bf16,
+ * rows <= max_rows) -> each written back to its source's return buffer at
+ * the row's position in the source's sorted order.                        */
+int kw8_ep_return(const void* ys, int64_t max_rows, int64_t D,
+                  const int32_t* counts, int32_t world, int32_t rank, int64_t E,
+                  const uint64_t* peer_out, kw8_stream_t stream);
+
+/* Group offsets [E/world + 1] of this rank's receive layout (for
+ * kw8_moe_expert_ffn on the received rows).                                */
+int kw8_ep_local_offsets(const int32_t* counts, int32_t world, int32_t rank,
+                         int64_t E, int32_t* local_offsets, kw8_stream_t stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

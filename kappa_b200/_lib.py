@@ -82,6 +82,14 @@ SIGNATURES: dict[str, tuple] = {
     "kw8_moe_topk": (ctypes.c_int, [_vp, _i64, _i64, _i32, _vp, _vp, _vp]),
     "kw8_moe_permute": (ctypes.c_int, [_vp, _i64, _i32, _i64, _i64, _vp, _vp, _vp, _vp, _vp]),
     "kw8_moe_permute_workspace_size": (ctypes.c_size_t, [_i64]),
+    "kw8_ipc_handle_size": (ctypes.c_size_t, []),
+    "kw8_ipc_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), _vp]),
+    "kw8_ipc_free": (ctypes.c_int, [_vp]),
+    "kw8_ipc_open": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_void_p)]),
+    "kw8_ipc_close": (ctypes.c_int, [_vp]),
+    "kw8_ep_dispatch": (ctypes.c_int, [_vp, _i64, _i64, _vp, _vp, _vp, _i32, _i32, _i64, _vp, _vp]),
+    "kw8_ep_return": (ctypes.c_int, [_vp, _i64, _i64, _vp, _i32, _i32, _i64, _vp, _vp]),
+    "kw8_ep_local_offsets": (ctypes.c_int, [_vp, _i32, _i32, _i64, _vp, _vp]),
     "kw8_moe_permute_ws": (ctypes.c_int, [_vp, _i64, _i32, _i64, _i64, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
     "kw8_moe_expert_ffn_workspace_size": (_sz, [_i64, _i64, _i64, _i64]),
     "kw8_moe_expert_ffn": (

@@ -1,0 +1,171 @@
+// Expert-parallel MoE data movement over NVLink: peer-to-peer row copies
+// into CUDA-IPC-mapped buffers of the other ranks (plain 16-byte stores;
+// no TMA, no multicast).
+//
+// counts[s][e] (all ranks' kept rows per expert, from an all-gather) fixes
+// every placement, so no host round trip is needed:
+//   rank r owns experts [r*El, (r+1)*El);
+//   its receive buffer is expert-major, source-major within an expert:
+//     recv_pos(s, e, i) = Σ_{e' in r's experts, e' < e} Σ_s' counts[s'][e']
+//                         + Σ_{s' < s} counts[s'][e] + i;
+//   source s keeps its rows sorted by expert (the permutation's order):
+//     src_pos(s, e, i) = Σ_{e' < e} counts[s][e'] + i.
+#include "ep.cuh"
+
+namespace kw8 {
+
+namespace {
+
+constexpr int kEpThreads = 256;
+
+// dest_base[e] = recv_pos(src, e, 0) on e's owner for this source `src`.
+__device__ void recv_bases(const int32_t* __restrict__ counts, int world, int E, int El, int src,
+                           int* dest_base) {
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    const int r0 = (e / El) * El;
+    int base = 0;
+    for (int e2 = r0; e2 < e; ++e2)
+      for (int s = 0; s < world; ++s) base += counts[s * E + e2];
+    for (int s = 0; s < src; ++s) base += counts[s * E + e];
+    dest_base[e] = base;
+  }
+}
+
+// Last index i in [0, n) with a[i] <= v (a non-decreasing, a[0] <= v).
+__device__ __forceinline__ int upper_index(const int* a, int n, int v) {
+  int lo = 0, hi = n - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (a[mid] <= v) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+// Row p of this rank's sorted order (expert e, i-th row of e) -> x[token]
+// copied to recv_pos(rank, e, i) on e's owner.  A warp per row.
+__global__ void __launch_bounds__(kEpThreads)
+    ep_dispatch_kernel(const uint4* __restrict__ x, int vec, const int32_t* __restrict__ sorted_token,
+                       const int32_t* __restrict__ offsets, const int32_t* __restrict__ counts, int world,
+                       int rank, int E, int El, const uint64_t* __restrict__ peer_recv) {
+  extern __shared__ int sh[];
+  int* off = sh;            // [E+1] this rank's offsets
+  int* dest = sh + E + 1;   // [E]
+  for (int e = threadIdx.x; e <= E; e += blockDim.x) off[e] = offsets[e];
+  recv_bases(counts, world, E, El, rank, dest);
+  __syncthreads();
+  const int rows = off[E];
+  const int lane = threadIdx.x & 31;
+  const int wpb = blockDim.x >> 5;
+  for (int p = blockIdx.x * wpb + (threadIdx.x >> 5); p < rows; p += gridDim.x * wpb) {
+    const int e = upper_index(off, E + 1, p);
+    const int pos = dest[e] + (p - off[e]);
+    const uint4* src = x + static_cast<int64_t>(sorted_token[p]) * vec;
+    uint4* dst = reinterpret_cast<uint4*>(peer_recv[e / El]) + static_cast<int64_t>(pos) * vec;
+    for (int c = lane; c < vec; c += 32) dst[c] = src[c];
+  }
+  __threadfence_system();
+}
+
+// Local row q of this rank's receive layout (expert e, source s, i-th row)
+// -> ys row copied to src_pos(s, e, i) on rank s.
+__global__ void __launch_bounds__(kEpThreads)
+    ep_return_kernel(const uint4* __restrict__ ys, int vec, const int32_t* __restrict__ counts, int world,
+                     int rank, int E, int El, const uint64_t* __restrict__ peer_out) {
+  extern __shared__ int sh[];
+  int* start = sh;                 // [El*world + 1] local block starts, (expert, source) order
+  int* dpos = sh + El * world + 1;  // [El*world]     src_pos(s, e, 0) on rank s
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int j = 0; j < El; ++j)
+      for (int s = 0; s < world; ++s) {
+        start[j * world + s] = acc;
+        acc += counts[s * E + rank * El + j];
+      }
+    start[El * world] = acc;
+  }
+  for (int b = threadIdx.x; b < El * world; b += blockDim.x) {
+    const int j = b / world, s = b % world, e = rank * El + j;
+    int pos = 0;
+    for (int e2 = 0; e2 < e; ++e2) pos += counts[s * E + e2];
+    dpos[b] = pos;
+  }
+  __syncthreads();
+  const int rows = start[El * world];
+  const int lane = threadIdx.x & 31;
+  const int wpb = blockDim.x >> 5;
+  for (int q = blockIdx.x * wpb + (threadIdx.x >> 5); q < rows; q += gridDim.x * wpb) {
+    const int b = upper_index(start, El * world + 1, q);
+    const int s = b % world;
+    const uint4* src = ys + static_cast<int64_t>(q) * vec;
+    uint4* dst = reinterpret_cast<uint4*>(peer_out[s]) + static_cast<int64_t>(dpos[b] + (q - start[b])) * vec;
+    for (int c = lane; c < vec; c += 32) dst[c] = src[c];
+  }
+  __threadfence_system();
+}
+
+// Local experts' group offsets [El+1] of the receive layout.
+__global__ void ep_local_offsets_kernel(const int32_t* __restrict__ counts, int world, int rank, int E,
+                                        int El, int32_t* __restrict__ loc_off) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    int acc = 0;
+    loc_off[0] = 0;
+    for (int j = 0; j < El; ++j) {
+      for (int s = 0; s < world; ++s) acc += counts[s * E + rank * El + j];
+      loc_off[j + 1] = acc;
+    }
+  }
+}
+
+int check_ep(int64_t D, int world, int rank, int64_t E) {
+  KW8_REQUIRE(world >= 1 && world <= kEpMaxRanks && rank >= 0 && rank < world, KW8_ERR_INVALID_ARG,
+              "bad rank %d of %d", rank, world);
+  KW8_REQUIRE(E >= 1 && E <= 4096 && E % world == 0, KW8_ERR_INVALID_ARG,
+              "%lld experts do not split over %d ranks", (long long)E, world);
+  KW8_REQUIRE(D > 0 && D % 8 == 0, KW8_ERR_UNSUPPORTED, "D must be a multiple of 8");
+  return KW8_OK;
+}
+
+}  // namespace
+
+int launch_ep_dispatch(const void* x, int64_t max_rows, int64_t D, const int32_t* sorted_token,
+                       const int32_t* offsets, const int32_t* counts, int world, int rank, int64_t E,
+                       const uint64_t* peer_recv, cudaStream_t stream) {
+  int rc = check_ep(D, world, rank, E);
+  if (rc) return rc;
+  if (max_rows <= 0) return KW8_OK;
+  const int El = static_cast<int>(E / world);
+  const size_t smem = (2 * E + 1) * sizeof(int);
+  const int64_t blocks = std::min<int64_t>((max_rows + 7) / 8, 148 * 8);
+  ep_dispatch_kernel<<<static_cast<int>(blocks), kEpThreads, smem, stream>>>(
+      static_cast<const uint4*>(x), static_cast<int>(D / 8), sorted_token, offsets, counts, world, rank,
+      static_cast<int>(E), El, peer_recv);
+  KW8_CHECK_LAUNCH();
+  return KW8_OK;
+}
+
+int launch_ep_return(const void* ys, int64_t max_rows, int64_t D, const int32_t* counts, int world,
+                     int rank, int64_t E, const uint64_t* peer_out, cudaStream_t stream) {
+  int rc = check_ep(D, world, rank, E);
+  if (rc) return rc;
+  if (max_rows <= 0) return KW8_OK;
+  const int El = static_cast<int>(E / world);
+  const size_t smem = (2 * static_cast<size_t>(El) * world + 1) * sizeof(int);
+  const int64_t blocks = std::min<int64_t>((max_rows + 7) / 8, 148 * 8);
+  ep_return_kernel<<<static_cast<int>(blocks), kEpThreads, smem, stream>>>(
+      static_cast<const uint4*>(ys), static_cast<int>(D / 8), counts, world, rank, static_cast<int>(E), El,
+      peer_out);
+  KW8_CHECK_LAUNCH();
+  return KW8_OK;
+}
+
+int launch_ep_local_offsets(const int32_t* counts, int world, int rank, int64_t E, int32_t* loc_off,
+                            cudaStream_t stream) {
+  int rc = check_ep(8, world, rank, E);
+  if (rc) return rc;
+  ep_local_offsets_kernel<<<1, 32, 0, stream>>>(counts, world, rank, static_cast<int>(E),
+                                                static_cast<int>(E / world), loc_off);
+  KW8_CHECK_LAUNCH();
+  return KW8_OK;
+}
+
+}  // namespace kw8

@@ -8,3 +8,5 @@
 #include "moe.cu"
 #include "api.cu"
 #include "noalloc.cu"
+#include "ep.cu"
+#include "ep_api.cu"

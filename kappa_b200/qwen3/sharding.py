@@ -14,11 +14,17 @@ so the sum is not rounded per rank) and one cast give the bf16 output.
 MoE, expert parallel (not in kappa): rank r holds experts
 [r*E/R, (r+1)*E/R) and its own tokens; the router is replicated.
 * prefill (``moe_swiglu_ffn_ep``): route and stably sort the rank's routed
-  rows by expert (rows for one rank's experts are then contiguous), exchange
-  per-expert counts, all-to-allv the sorted rows to their experts' ranks,
-  regroup the received rows by local expert, run the grouped expert FFN,
-  send the outputs back the same way, and combine locally.  Each rank's
-  result equals the single-GPU layer on that rank's tokens.
+  rows by expert, all-gather the per-expert counts, and move every routed
+  row of x straight into its expert owner's receive buffer over NVLink
+  (``kw8_ep_dispatch``: peer-to-peer stores into CUDA-IPC-mapped buffers
+  held by an :class:`EPContext`, laid out expert-major, so the grouped
+  expert FFN runs on it directly); the outputs go back the same way
+  (``kw8_ep_return``) and each rank combines locally.  Every placement is
+  computed on the GPU from the counts: no host round trip.  Two one-element
+  all-reduces order the phases across ranks.  Without a context (or with
+  custom ``ops``) the rows move with NCCL all-to-allv instead (counts to the
+  host, regroup by local expert).  Each rank's result equals the single-GPU
+  layer on that rank's tokens.
 * decode (``moe_swiglu_ffn_ep_decode``): x is replicated (B x D is small);
   every rank routes all tokens, runs only its local experts' rows and adds
   their weighted outputs into an fp32 partial; one all-reduce sums them.
@@ -29,12 +35,14 @@ so the exchange logic also runs on CPU ranks (gloo) in the tests.
 
 from __future__ import annotations
 
+import ctypes
 from typing import Protocol
 
 import torch
 import torch.distributed as dist
 
-from kappa_b200.qwen3.quant import Q8Weight, Weight
+from kappa_b200 import _lib
+from kappa_b200.qwen3.quant import Q8Weight, Weight, kmajor
 
 __all__ = [
     "shard_output_channels",
@@ -45,6 +53,7 @@ __all__ = [
     "swiglu_ffn_tp",
     "feed_forward_tp",
     "moe_swiglu_ffn_ep",
+    "EPContext",
     "moe_swiglu_ffn_ep_decode",
     "MoEOps",
     "KernelMoEOps",
@@ -222,14 +231,134 @@ def _moe_args(cfg, x: torch.Tensor):
     return b, t, d, capacity
 
 
+class EPContext:
+    """Buffers of the NVLink expert-parallel path for one process group.
+
+    Each rank allocates a receive buffer for every row the other ranks could
+    send it (``world * max_tokens * k`` rows of ``d``) and a return buffer
+    for its own routed rows, shares both with CUDA IPC and maps the other
+    ranks' buffers.  Collective: every rank constructs it with the same
+    arguments and calls :meth:`close` (also collective) when done.
+    """
+
+    def __init__(self, *, max_tokens: int, d: int, k: int, hidden: int, num_experts: int, group=None):
+        self.group = group
+        self.world, self.rank = _world(group)
+        if num_experts % self.world:
+            raise ValueError(f"{num_experts} experts do not split over {self.world} ranks")
+        self.max_tokens, self.d, self.k, self.hidden, self.num_experts = max_tokens, d, k, hidden, num_experts
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        lib = _lib.load()
+        hsize = int(lib.kw8_ipc_handle_size())
+        self.recv_rows = self.world * max_tokens * k
+        self.out_rows = max_tokens * k
+        self._own = []
+        handles = []
+        for rows in (self.recv_rows, self.out_rows):
+            ptr = ctypes.c_void_p()
+            h = ctypes.create_string_buffer(hsize)
+            _lib.check(lib.kw8_ipc_alloc(rows * d * 2, ctypes.byref(ptr), h))
+            self._own.append(ptr.value)
+            handles.append(h.raw)
+        allh = [None] * self.world
+        dist.all_gather_object(allh, handles, group=group)
+        self._opened = []
+        peers = [[], []]
+        for r, hs in enumerate(allh):
+            for b in range(2):
+                if r == self.rank:
+                    peers[b].append(self._own[b])
+                else:
+                    ptr = ctypes.c_void_p()
+                    _lib.check(lib.kw8_ipc_open(ctypes.create_string_buffer(hs[b], hsize), ctypes.byref(ptr)))
+                    self._opened.append(ptr.value)
+                    peers[b].append(ptr.value)
+
+        def as_i64(v):
+            return [int(a) - (1 << 64) if int(a) >= (1 << 63) else int(a) for a in v]
+
+        self.peer_recv = torch.tensor(as_i64(peers[0]), dtype=torch.int64, device=self.device)
+        self.peer_out = torch.tensor(as_i64(peers[1]), dtype=torch.int64, device=self.device)
+        self.recv_ptr, self.out_ptr = self._own
+        self.ys_loc = torch.empty((self.recv_rows, d), dtype=torch.bfloat16, device=self.device)
+        e_loc = num_experts // self.world
+        self.ws = torch.empty(int(lib.kw8_moe_expert_ffn_workspace_size(self.recv_rows, d, hidden, e_loc)),
+                              dtype=torch.uint8, device=self.device)
+        self.loc_off = torch.empty(e_loc + 1, dtype=torch.int32, device=self.device)
+        self.counts = torch.empty((self.world, num_experts), dtype=torch.int32, device=self.device)
+        self.flag = torch.zeros(1, dtype=torch.float32, device=self.device)
+        self.closed = False
+
+    def sync(self):
+        """Orders the phases across ranks on the current stream (a one-element all-reduce)."""
+        dist.all_reduce(self.flag, group=self.group)
+
+    def close(self):
+        """Collective: unmaps the other ranks' buffers, then frees this rank's."""
+        if self.closed:
+            return
+        lib = _lib.load()
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for p in self._opened:
+            lib.kw8_ipc_close(ctypes.c_void_p(p))
+        dist.barrier(group=self.group)
+        for p in self._own:
+            lib.kw8_ipc_free(ctypes.c_void_p(p))
+        self.closed = True
+
+
+def _moe_ep_p2p(x, router_w, gate_local, up_local, down_local, *, cfg, ctx: EPContext, capacity):
+    from kappa_b200.qwen3 import ffn_moe
+
+    lib = _lib.load()
+    b, t, d = (int(s) for s in x.shape)
+    T = b * t
+    e, k = cfg.num_experts, cfg.num_experts_per_tok
+    if T > ctx.max_tokens or d != ctx.d or k != ctx.k or e != ctx.num_experts:
+        raise ValueError("EPContext was made for other shapes")
+    e_loc = e // ctx.world
+    g, u, dn = (kmajor(w, -2, n) for w, n in ((gate_local, "ffn_gate"), (up_local, "ffn_up"),
+                                               (down_local, "ffn_down")))
+    i = int(g.q.shape[-2])
+    if int(g.q.shape[0]) != e_loc or i != ctx.hidden:
+        raise ValueError("local expert weights do not match the EPContext")
+    xc = x.contiguous()
+    stream = _lib.stream_of(x)
+    _, idx, w = ffn_moe.route_logits(xc, router_w, num_experts=e, num_experts_per_tok=k)
+    st, inv, sizes, offs = ffn_moe.permute(idx, e, capacity)
+    dist.all_gather_into_tensor(ctx.counts, sizes, group=ctx.group)
+    _lib.check(lib.kw8_ep_dispatch(xc.data_ptr(), T * k, d, st.data_ptr(), offs.data_ptr(), ctx.counts.data_ptr(),
+                                   ctx.world, ctx.rank, e, ctx.peer_recv.data_ptr(), stream))
+    ctx.sync()
+    _lib.check(lib.kw8_ep_local_offsets(ctx.counts.data_ptr(), ctx.world, ctx.rank, e, ctx.loc_off.data_ptr(),
+                                        stream))
+    _lib.check(lib.kw8_moe_expert_ffn(ctx.recv_ptr, ctx.recv_rows, d, i, e_loc, ctx.loc_off.data_ptr(), g.struct(),
+                                      u.struct(), dn.struct(), ctx.ys_loc.data_ptr(), ctx.ws.data_ptr(),
+                                      ctx.ws.numel(), stream))
+    _lib.check(lib.kw8_ep_return(ctx.ys_loc.data_ptr(), ctx.recv_rows, d, ctx.counts.data_ptr(), ctx.world,
+                                 ctx.rank, e, ctx.peer_out.data_ptr(), stream))
+    ctx.sync()
+    out = torch.empty((b, t, d), dtype=torch.bfloat16, device=x.device)
+    _lib.check(lib.kw8_moe_combine(ctx.out_ptr, inv.data_ptr(), w.contiguous().data_ptr(), T, k, d,
+                                   out.data_ptr(), stream))
+    del g, u, dn
+    return out
+
+
 def moe_swiglu_ffn_ep(x: torch.Tensor, router_w: Weight, gate_local: Weight, up_local: Weight, down_local: Weight,
-                      *, cfg, group=None, ops: MoEOps | None = None) -> torch.Tensor:
+                      *, cfg, group=None, ops: MoEOps | None = None, ctx: EPContext | None = None) -> torch.Tensor:
     """Expert-parallel MoE layer over this rank's tokens ``x`` ``[B, T, D]`` (prefill).
 
     ``gate_local`` / ``up_local`` / ``down_local`` hold this rank's E/R experts
     (``shard_experts``); ``router_w`` is the full router.  Returns the same
     ``[B, T, D]`` bf16 as the single-GPU layer on ``x`` with every expert.
+    With ``ctx`` (an :class:`EPContext` of this group) the rows move over
+    NVLink with the B200 kernels; otherwise with NCCL all-to-allv.
     """
+    if ctx is not None and ops is None:
+        _, _, _, capacity = _moe_args(cfg, x)
+        return _moe_ep_p2p(x, router_w, gate_local, up_local, down_local, cfg=cfg, ctx=ctx, capacity=capacity)
     ops = ops or KernelMoEOps()
     world, rank = _world(group)
     e, k = cfg.num_experts, cfg.num_experts_per_tok

@@ -51,7 +51,10 @@ def _rank_main(rank: int, world: int, port: int, errfile: str):
         gl, ul, dl = S.shard_experts(gate, up, down, rank, world)
         cfg = MoEConfig(use_moe=True, num_experts=E, num_experts_per_tok=K, moe_impl="ragged_jax")
         x = normal(np.random.default_rng(100 + rank), (1, 300 + 50 * rank, D)).astype(O.BF16)
-        y = S.moe_swiglu_ffn_ep(to_dev(x, dev), router, gl, ul, dl, cfg=cfg)
+        y = S.moe_swiglu_ffn_ep(to_dev(x, dev), router, gl, ul, dl, cfg=cfg)  # NCCL all-to-allv
+        ctx = S.EPContext(max_tokens=400, d=D, k=K, hidden=I, num_experts=E)
+        y2 = S.moe_swiglu_ffn_ep(to_dev(x, dev), router, gl, ul, dl, cfg=cfg, ctx=ctx)  # NVLink P2P
+        y3 = S.moe_swiglu_ffn_ep(to_dev(x, dev), router, gl, ul, dl, cfg=cfg, ctx=ctx)  # buffers reused
         # reference on this rank's tokens with the routing the GPU chose
         from kappa_b200.qwen3 import ffn_moe as M
 
@@ -59,6 +62,12 @@ def _rank_main(rank: int, world: int, port: int, errfile: str):
         ref, _, _ = O.moe_reference_f32(x, o_router, o_gate, o_up, o_down, num_experts=E, k=K,
                                         idx=to_np(idx), w=to_np(w))
         parity(to_np(y), ref, tol=2e-2)
+        parity(to_np(y2), ref, tol=2e-2)
+        assert torch.equal(y2, y3)
+        # the single-GPU layer with every expert on the same tokens
+        y1 = M.moe_swiglu_ffn(to_dev(x, dev), router, gate, up, down, cfg=cfg)
+        parity(to_np(y2), to_np(y1), tol=2e-2)
+        ctx.close()
         # decode: the same x on both ranks
         xd = normal(np.random.default_rng(7), (1, 8, D)).astype(O.BF16)
         yd = S.moe_swiglu_ffn_ep_decode(to_dev(xd, dev), router, gl, ul, dl, cfg=cfg)
