@@ -251,6 +251,74 @@ def run_profile_small():
     return 0
 
 
+def _extra_configs(lib, dev, stream, router, gate, up, down, sr, sg, su, sd):
+    """BASELINE configs[2] (MoE decode, HBM-bound) and configs[0] (Gemma3-4B MLP, T=256).
+
+    Decode bytes per call: the int8 bytes of the experts the seeded routing
+    actually activates (3*D*I each) + their fp32 scales + the router;
+    fraction of the measured HBM copy bandwidth.  The MLP: 6*T*D*H FLOPs.
+    """
+    import torch
+
+    from kappa_b200 import _lib
+    from kappa_b200.gemma3.ffn import feed_forward
+    from kappa_b200.qwen3 import ffn_moe as M
+    from kappa_b200.qwen3.quant import quantize_weight
+
+    peak_tf, peak_gbs, kind = _peaks()
+    sptr = stream.cuda_stream
+
+    def timed(fn, reps=20):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / reps / 1e3
+
+    decode = []
+    gx = torch.Generator(device=dev)
+    gx.manual_seed(7)
+    for b in (1, 8, 64, 256):
+        x = torch.randn((1, b, D), generator=gx, device=dev, dtype=torch.float32).to(torch.bfloat16)
+        out = torch.empty_like(x)
+        ws = torch.empty(int(lib.kw8_moe_ffn_workspace_size(b, D, I, E, K_TOP)), dtype=torch.uint8, device=dev)
+
+        def call():
+            rc = lib.kw8_moe_ffn(x.data_ptr(), b, D, I, E, K_TOP, -1, sr, sg, su, sd, out.data_ptr(), ws.data_ptr(),
+                                 ws.numel(), sptr)
+            if rc != 0:
+                raise RuntimeError(_lib.last_error())
+
+        sec = timed(call)
+        _, idx, _ = M.route_logits(x, router, num_experts=E, num_experts_per_tok=K_TOP)
+        active = int(torch.unique(idx).numel())
+        nbytes = active * (3 * D * I + (2 * I + D) * 4) + D * E + E * 4 + 2 * 2 * b * D
+        decode.append({"tokens": b, "active_experts": active, "us_per_call": sec * 1e6,
+                       "tokens_per_s": b / sec, "bytes_per_call": nbytes, "achieved_gbs": nbytes / sec / 1e9,
+                       "frac_hbm": nbytes / sec / 1e9 / peak_gbs})
+
+    # configs[0]: Gemma3-4B gated-GELU MLP, T=256, per-channel int8 + fp32 scales
+    dg, hg, tg = 2560, 10240, 256
+    gg = torch.Generator(device=dev)
+    gg.manual_seed(0)
+    gating = quantize_weight(torch.randn((2, hg, dg), generator=gg, device=dev) * 0.02, per_channel=True,
+                             scale_dtype=torch.float32, in_axis=-1)
+    linear = quantize_weight(torch.randn((hg, dg), generator=gg, device=dev) * 0.02, per_channel=True,
+                             scale_dtype=torch.float32)
+    xg = torch.randn((1, tg, dg), generator=gg, device=dev).to(torch.bfloat16)
+    sec = timed(lambda: feed_forward(xg, gating, linear, transpose_gating_einsum=True))
+    flops = 6.0 * tg * dg * hg
+    mlp = {"workload": "gemma3-4b W8 MLP, T=256 (BASELINE configs[0])", "us_per_call": sec * 1e6,
+           "tokens_per_s": tg / sec, "tflops": flops / sec / 1e12, "frac_tc": flops / sec / 1e12 / peak_tf,
+           "int8_weight_gbs": 3 * dg * hg / sec / 1e9}
+    return {"moe_decode": decode, "gemma_mlp": mlp, "peaks": f"{kind}: {peak_tf} TFLOP/s, {peak_gbs} GB/s"}
+
+
 def run_gpu(args):
     import torch
     import torch.distributed as dist
@@ -405,6 +473,8 @@ def run_gpu(args):
     if status != 0:
         raise RuntimeError(f"device status {status}")
 
+    extra = _extra_configs(lib, dev, stream, router, gate, up, down, sr, sg, su, sd) if world == 1 else None
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         tps, sec = cpu_reference_sample(256, 2)
@@ -468,6 +538,8 @@ def run_gpu(args):
         "clocks": clocks.summary(),
         "cpu_baseline": cpu,
     }
+    if extra is not None:
+        line["other_configs"] = extra
     print(json.dumps(line), flush=True)
     return 0
 
