@@ -80,7 +80,8 @@ int kw8_device_status(int32_t* status_out, kw8_stream_t stream);
 
 /* Tuning and testing knobs, process wide; no kappa counterpart (kappa
  * leaves kernel choice to XLA).
- *   option 0 (GEMM path): 0 automatic, 1 tensor-core GEMM, 2 GEMV;
+ *   option 0 (GEMM path): 0 automatic, 1 tensor-core GEMM, 2 weight-
+ *            streaming GEMM (the decode kernel: few rows per group);
  *   option 1 (token tile of the tensor-core GEMM): 0 automatic, or a
  *            multiple of 16 in [16, 256].                                   */
 int kw8_set_option(int32_t option, int64_t value);

@@ -33,7 +33,7 @@ ACT_GELU_TANH = 0
 ACT_SILU = 1
 
 # kw8_set_option
-OPT_GEMM_PATH = 0  # 0 auto, 1 tensor core, 2 GEMV
+OPT_GEMM_PATH = 0  # 0 auto, 1 tensor core, 2 weight streaming (decode kernel)
 OPT_TOKEN_TILE = 1  # 0 auto, 16..256
 
 

@@ -3,7 +3,7 @@
 #include <climits>
 #include <cmath>
 
-#include "gemm_simt.cuh"
+#include "gemm_stream.cuh"
 #include "gemm_tc.cuh"
 #include "moe.cuh"
 #include "quant.cuh"
@@ -15,7 +15,7 @@ int read_device_status(int32_t* out, cudaStream_t stream);
 
 namespace {
 
-std::atomic<int> g_opt_path{0};        // 0 auto, 1 tensor core, 2 GEMV
+std::atomic<int> g_opt_path{0};        // 0 auto, 1 tensor core, 2 weight streaming
 std::atomic<int> g_opt_token_tile{0};  // 0 auto, else 16..256 (multiple of 16)
 
 // Carves 256-byte aligned sub-buffers out of the caller's workspace.  With
@@ -86,17 +86,31 @@ int pick_nt_dense(int64_t rows, int64_t m_tiles) {
   return best;
 }
 
-// GEMV (SIMT) path only for a single GEMV tile of rows (<= 8: one decode
-// token's k routed rows, or a dense call of <= 8 tokens).  Measured at the
-// Qwen3-30B-A3B shape: the tensor-core path is faster from 2 tokens up
-// (e.g. 64 tokens: 237 vs 598 us), the GEMV ~5% faster at 1 token.
-bool use_simt(int64_t rows, int64_t groups) {
+// Routed rows per group up to m + 3 sqrt(m) for groups of mean m rows.
+double rows_hint(int64_t rows, int64_t groups) {
+  const double mean = static_cast<double>(rows) / static_cast<double>(groups > 0 ? groups : 1);
+  return mean + 3.0 * std::sqrt(mean);
+}
+
+// Weight-streaming kernel (gemm_stream) instead of the tensor-core pipeline
+// when a group's rows fit a pass of at most 16 rows: the work is then bound
+// by weight bytes, and the tensor-core pipeline's per-stage cost (one
+// mbarrier round trip and eight MMAs of N <= 32 per 16 KB of weights) caps
+// it well below HBM bandwidth.  Measured on the Qwen3-30B-A3B layer: the
+// streaming kernel is faster up to 64 decode tokens (<= 16 rows per expert;
+// 173 vs 221 us at 64), the tensor-core pipeline from 128 (224 vs 297 us).
+constexpr double kStreamMaxRowsHint = 16.0;
+
+bool use_stream(double hint) {
   const int p = g_opt_path.load();
   if (p == 1) return false;
   if (p == 2) return true;
-  (void)groups;
-  return rows <= kSimtTN;
+  return hint <= kStreamMaxRowsHint;
 }
+
+// Router logits: dense rows of the router GEMM up to this many go to the
+// weight-streaming kernel.
+constexpr int64_t kStreamRouterMaxRows = 256;
 
 int check_weight(const kw8_weight& w, const char* name) {
   KW8_REQUIRE(w.q != nullptr && w.scale != nullptr, KW8_ERR_INVALID_ARG, "%s: null pointer", name);
@@ -124,15 +138,23 @@ GemmArgs base_args(const kw8_weight& a, const kw8_weight* b) {
   return g;
 }
 
-// One grouped GEMM through the chosen path.
-int run_gemm(bool simt, int mode, const kw8_weight& a, const kw8_weight* b, int64_t groups,
-             int64_t N_out, int64_t K, const void* x, int64_t x_rows, int64_t ldx,
-             GemmArgs args, cudaStream_t stream) {
-  if (simt) {
-    args.nt = kSimtTN;
-    return launch_gemm_simt(mode, a.q, b ? b->q : nullptr, groups, N_out, K, x, x_rows, ldx, args,
-                            stream);
+StreamArgs stream_args(const kw8_weight& a, const kw8_weight* b) {
+  StreamArgs g{};
+  g.scale_a = a.scale;
+  g.scale_a_dtype = a.scale_dtype;
+  g.scale_a_pc = a.per_channel;
+  if (b) {
+    g.scale_b = b->scale;
+    g.scale_b_dtype = b->scale_dtype;
+    g.scale_b_pc = b->per_channel;
   }
+  return g;
+}
+
+// One grouped GEMM on the tensor-core pipeline.
+int run_gemm(int mode, const kw8_weight& a, const kw8_weight* b, int64_t groups, int64_t N_out,
+             int64_t K, const void* x, int64_t x_rows, int64_t ldx, const GemmArgs& args,
+             cudaStream_t stream) {
   return launch_gemm_tc(mode, a.q, b ? b->q : nullptr, groups, N_out, K, x, x_rows, ldx, args,
                         stream);
 }
@@ -192,16 +214,37 @@ MoeBuffers carve_moe(Carver& c, int64_t T, int64_t D, int64_t I, int64_t E, int 
   return b;
 }
 
-// Expert FFN over rows already sorted by group (gate/up + SwiGLU, down).
-// With row_token / row_weight the down projection runs the fused combine
-// (EPI_COMBINE_F32) into `ys` = fp32 [T][D] accumulation buffer; otherwise
-// `ys` is bf16 [rows][D].
-int expert_ffn(const void* xs, int64_t rows, int64_t D, int64_t I, int64_t E,
-               const int32_t* group_offsets, const kw8_weight& gate, const kw8_weight& up,
-               const kw8_weight& down, void* ys, const ExpertBuffers& b, cudaStream_t stream,
-               const int32_t* row_token = nullptr, const float* row_weight = nullptr) {
-  const bool simt = use_simt(rows, E);
-  const int nt = simt ? kSimtTN : pick_nt(rows, E);
+// Expert FFN over rows sorted by group (gate/up + SwiGLU, down).  Row r of
+// the sorted order is x row `row_index[r]` (weight-streaming path only: the
+// gather is fused into its operand load) or, with row_index == nullptr, x
+// row r.  With row_token / row_weight the down projection runs the fused
+// combine (EPI_COMBINE_F32) into `ys` = fp32 [T][D] accumulation buffer;
+// otherwise `ys` is bf16 [rows][D].
+int expert_ffn(bool streamed, const void* x, const int32_t* row_index, int64_t rows, int64_t D,
+               int64_t I, int64_t E, const int32_t* group_offsets, const kw8_weight& gate,
+               const kw8_weight& up, const kw8_weight& down, void* ys, const ExpertBuffers& b,
+               cudaStream_t stream, const int32_t* row_token = nullptr,
+               const float* row_weight = nullptr) {
+  const int mode = row_token != nullptr ? EPI_COMBINE_F32 : EPI_PLAIN_BF16;
+  if (streamed) {
+    const int nt = stream_nt(rows_hint(rows, E));
+    StreamArgs g = stream_args(gate, &up);
+    g.group_offsets = group_offsets;
+    g.row_index = row_index;
+    g.out = b.h;
+    g.ld_out = I;
+    int rc = launch_gemm_stream(EPI_PAIR_SILU, gate.q, up.q, E, I, D, x, D, rows, nt, g, stream);
+    if (rc) return rc;
+    StreamArgs d = stream_args(down, nullptr);
+    d.group_offsets = group_offsets;
+    d.out = ys;
+    d.ld_out = D;
+    d.row_token = row_token;
+    d.row_weight = row_weight;
+    return launch_gemm_stream(mode, down.q, nullptr, E, D, I, b.h, I, rows, nt, d, stream);
+  }
+  KW8_REQUIRE(row_index == nullptr, KW8_ERR_INVALID_ARG, "tensor-core path takes gathered rows");
+  const int nt = pick_nt(rows, E);
   int rc = launch_build_tiles(group_offsets, E, nt, b.tiles, b.num_tiles, stream);
   if (rc) return rc;
   GemmArgs g = base_args(gate, &up);
@@ -210,7 +253,7 @@ int expert_ffn(const void* xs, int64_t rows, int64_t D, int64_t I, int64_t E,
   g.nt = nt;
   g.out = b.h;
   g.ld_out = I;
-  rc = run_gemm(simt, EPI_PAIR_SILU, gate, &up, E, I, D, xs, rows, D, g, stream);
+  rc = run_gemm(EPI_PAIR_SILU, gate, &up, E, I, D, x, rows, D, g, stream);
   if (rc) return rc;
   GemmArgs d = base_args(down, nullptr);
   d.tiles = b.tiles;
@@ -220,21 +263,28 @@ int expert_ffn(const void* xs, int64_t rows, int64_t D, int64_t I, int64_t E,
   d.ld_out = D;
   d.row_token = row_token;
   d.row_weight = row_weight;
-  const int mode = row_token != nullptr ? EPI_COMBINE_F32 : EPI_PLAIN_BF16;
-  return run_gemm(simt, mode, down, nullptr, E, D, I, b.h, rows, I, d, stream);
+  return run_gemm(mode, down, nullptr, E, D, I, b.h, rows, I, d, stream);
 }
 
 int route(const void* x, int64_t T, int64_t D, int64_t E, int k, const kw8_weight& router,
           float* logits, int32_t* idx, void* w, cudaStream_t stream) {
-  const bool simt = use_simt(T, 1);
-  GemmArgs r = base_args(router, nullptr);
-  r.tiles = nullptr;
-  r.num_tiles = nullptr;
-  r.dense_rows = static_cast<int>(T);
-  r.nt = simt ? kSimtTN : pick_nt_dense(T, (E + 127) / 128);
-  r.out = logits;
-  r.ld_out = E;
-  int rc = run_gemm(simt, EPI_PLAIN_F32, router, nullptr, 1, E, D, x, T, D, r, stream);
+  int rc;
+  const int path = g_opt_path.load();
+  if (path == 2 || (path == 0 && T <= kStreamRouterMaxRows)) {
+    StreamArgs r = stream_args(router, nullptr);
+    r.dense_rows = static_cast<int>(T);
+    r.out = logits;
+    r.ld_out = E;
+    rc = launch_gemm_stream(EPI_PLAIN_F32, router.q, nullptr, 1, E, D, x, D, T,
+                            stream_nt(static_cast<double>(T)), r, stream);
+  } else {
+    GemmArgs r = base_args(router, nullptr);
+    r.dense_rows = static_cast<int>(T);
+    r.nt = pick_nt_dense(T, (E + 127) / 128);
+    r.out = logits;
+    r.ld_out = E;
+    rc = run_gemm(EPI_PLAIN_F32, router, nullptr, 1, E, D, x, T, D, r, stream);
+  }
   if (rc) return rc;
   return launch_topk(logits, T, E, k, idx, w, stream);
 }
@@ -320,22 +370,35 @@ int kw8_dense_ffn(const void* x, int64_t T, int64_t D, int64_t H, kw8_weight gat
   Carver c(workspace, workspace_bytes);
   __nv_bfloat16* h = c.take<__nv_bfloat16>(T * H);
   KW8_REQUIRE(workspace != nullptr && c.ok, KW8_ERR_WORKSPACE, "dense FFN workspace too small");
-  const bool simt = use_simt(T, 1);
+  const int epi_pair = act == KW8_ACT_GELU_TANH ? EPI_PAIR_GELU : EPI_PAIR_SILU;
+  const int epi_out = out_dtype == KW8_DT_F32 ? EPI_PLAIN_F32 : EPI_PLAIN_BF16;
+  if (use_stream(static_cast<double>(T))) {
+    const int nt = stream_nt(static_cast<double>(T));
+    StreamArgs g = stream_args(gate, &up);
+    g.dense_rows = static_cast<int>(T);
+    g.out = h;
+    g.ld_out = H;
+    rc = launch_gemm_stream(epi_pair, gate.q, up.q, 1, H, D, x, D, T, nt, g, stream);
+    if (rc) return rc;
+    StreamArgs d = stream_args(down, nullptr);
+    d.dense_rows = static_cast<int>(T);
+    d.out = out;
+    d.ld_out = D;
+    return launch_gemm_stream(epi_out, down.q, nullptr, 1, D, H, h, H, T, nt, d, stream);
+  }
   GemmArgs g = base_args(gate, &up);
   g.dense_rows = static_cast<int>(T);
-  g.nt = simt ? kSimtTN : pick_nt_dense(T, (H + 63) / 64);
+  g.nt = pick_nt_dense(T, (H + 63) / 64);
   g.out = h;
   g.ld_out = H;
-  rc = run_gemm(simt, act == KW8_ACT_GELU_TANH ? EPI_PAIR_GELU : EPI_PAIR_SILU, gate, &up, 1, H, D,
-                x, T, D, g, stream);
+  rc = run_gemm(epi_pair, gate, &up, 1, H, D, x, T, D, g, stream);
   if (rc) return rc;
   GemmArgs d = base_args(down, nullptr);
   d.dense_rows = static_cast<int>(T);
-  d.nt = simt ? kSimtTN : pick_nt_dense(T, (D + 127) / 128);
+  d.nt = pick_nt_dense(T, (D + 127) / 128);
   d.out = out;
   d.ld_out = D;
-  return run_gemm(simt, out_dtype == KW8_DT_F32 ? EPI_PLAIN_F32 : EPI_PLAIN_BF16, down, nullptr, 1,
-                  D, H, h, T, H, d, stream);
+  return run_gemm(epi_out, down, nullptr, 1, D, H, h, T, H, d, stream);
 }
 
 int kw8_moe_route(const void* x, int64_t T, int64_t D, int64_t E, int32_t k, kw8_weight router,
@@ -407,7 +470,8 @@ int kw8_moe_expert_ffn(const void* xs, int64_t rows, int64_t D, int64_t I, int64
   Carver c(workspace, workspace_bytes);
   ExpertBuffers b = carve_expert(c, rows, I, E);
   KW8_REQUIRE(workspace != nullptr && c.ok, KW8_ERR_WORKSPACE, "expert FFN workspace too small");
-  return expert_ffn(xs, rows, D, I, E, group_offsets, gate, up, down, ys, b, stream);
+  return expert_ffn(use_stream(rows_hint(rows, E)), xs, nullptr, rows, D, I, E, group_offsets, gate,
+                    up, down, ys, b, stream);
 }
 
 int kw8_moe_combine(const void* ys, const int32_t* inv_pos, const void* w, int64_t T, int32_t k,
@@ -449,15 +513,20 @@ int kw8_moe_ffn(const void* x, int64_t T, int64_t D, int64_t I, int64_t E, int32
   rc = launch_permute_multi(b.idx, T, k, E, capacity, b.perm_hist, b.sorted_token, b.inv_pos,
                             b.group_sizes, b.group_offsets, stream, b.w, b.sorted_w);
   if (rc) return rc;
-  rc = launch_gather(x, b.sorted_token, b.group_offsets + E, m, D, b.xs, stream);
-  if (rc) return rc;
+  // Few rows per expert: the weight-streaming kernels read x rows through
+  // the permutation (no gathered copy); otherwise gather for the TMA loads.
+  const bool streamed = use_stream(rows_hint(m, E));
+  if (!streamed) {
+    rc = launch_gather(x, b.sorted_token, b.group_offsets + E, m, D, b.xs, stream);
+    if (rc) return rc;
+  }
   // The down projection adds w * y of every routed row straight into the
   // fp32 token buffer (no bf16 rounding of the per-expert outputs, no
   // [T*k][D] round trip); one conversion pass writes the bf16 output.
   KW8_CUDA_TRY(cudaMemsetAsync(b.acc, 0, static_cast<size_t>(T * D) * sizeof(float), stream));
   ExpertBuffers eb{b.tiles, b.num_tiles, b.h};
-  rc = expert_ffn(b.xs, m, D, I, E, b.group_offsets, gate, up, down, b.acc, eb, stream,
-                  b.sorted_token, b.sorted_w);
+  rc = expert_ffn(streamed, streamed ? x : b.xs, streamed ? b.sorted_token : nullptr, m, D, I, E,
+                  b.group_offsets, gate, up, down, b.acc, eb, stream, b.sorted_token, b.sorted_w);
   if (rc) return rc;
   return launch_f32_to_bf16(b.acc, T * D, out, stream);
 }

@@ -4,7 +4,7 @@
 #include "host.cu"
 #include "quant.cu"
 #include "gemm_tc.cu"
-#include "gemm_simt.cu"
+#include "gemm_stream.cu"
 #include "moe.cu"
 #include "api.cu"
 #include "noalloc.cu"

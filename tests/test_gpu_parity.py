@@ -206,10 +206,11 @@ def test_dense_golden_fixture():
 
 
 @pytest.mark.parametrize("path", [0, 1, 2])
-@pytest.mark.parametrize("T,D,H,per_channel", [(200, 256, 512, True), (7, 128, 256, False), (256, 2560, 10240, True)])
+@pytest.mark.parametrize("T,D,H,per_channel", [(200, 256, 512, True), (7, 128, 256, False), (256, 2560, 10240, True),
+                                                 (16, 2560, 10240, True), (13, 208, 336, True)])
 def test_gemma_feed_forward(path, T, D, H, per_channel):
     if T >= 256 and path == 2:
-        pytest.skip("GEMV path is for decode sizes")
+        pytest.skip("the weight-streaming path is for decode sizes")
     _lib.set_option(_lib.OPT_GEMM_PATH, path)
     rng = np.random.default_rng(T + H)
     x = normal(rng, (1, T, D)).astype(O.BF16)
@@ -307,7 +308,8 @@ def test_moe_golden_fixture():
 
 
 @pytest.mark.parametrize("path", [0, 1, 2])
-@pytest.mark.parametrize("T,D,I,E,k,per_channel", [(300, 256, 128, 16, 4, True), (64, 512, 256, 32, 8, False), (5, 256, 128, 16, 4, True)])
+@pytest.mark.parametrize("T,D,I,E,k,per_channel", [(300, 256, 128, 16, 4, True), (64, 512, 256, 32, 8, False), (5, 256, 128, 16, 4, True),
+                                                   (40, 208, 80, 8, 2, True)])
 def test_moe_layer_vs_oracle(path, T, D, I, E, k, per_channel):
     _lib.set_option(_lib.OPT_GEMM_PATH, path)
     x, g, o = _moe_case(T, D, I, E, k, per_channel, seed=T + E)
