@@ -9,7 +9,6 @@ namespace {
 constexpr int kStThreads = 256;  // 8 warps
 constexpr int kStWarps = kStThreads / 32;
 constexpr int kStStepK = 64;     // k per warp step: 4 lanes x 16 bytes
-constexpr int kStPrefetchSteps = 8;  // steps of each weight row requested into L2 up front
 
 // Per-warp copy ring: a stage holds one step's 16-byte chunks of every lane
 // (kMats x 2 weight rows, 2 per 8-token tile).  Depth from the chunk count,
@@ -40,12 +39,6 @@ __device__ __forceinline__ void cp_async_commit() {
 template <int kPending>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(kPending) : "memory");
-}
-
-// Requests [p, p + bytes) into L2 (a hint: nothing waits for it).  p and
-// bytes are multiples of 16.
-__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
 __device__ __forceinline__ void mma_16816_bf16(float (&d)[4], uint32_t a0, uint32_t a1,
@@ -114,19 +107,6 @@ __global__ void __launch_bounds__(kStThreads,
   if constexpr (kPair) {
     w_rows[1][0] = wb + fr0 * p.K;
     w_rows[1][1] = wb + fr1 * p.K;
-  }
-
-  // The first kStPrefetchSteps steps of the warp's weight slice into L2 up
-  // front: lane i < 16 row f0 + i of wa, lane 16 + i (paired mode) row
-  // f0 + i of wb.
-  if (tile_ok && s_hi > s_lo) {
-    const int rr = f0 + (lane & 15);
-    if (rr < p.N_out && (kPair || lane < 16)) {
-      const int8_t* base = (kPair && lane >= 16) ? wb : wa;
-      const int k_lo = s_lo * kStStepK;
-      const int k_hi = min(min(s_hi, s_lo + kStPrefetchSteps) * kStStepK, p.K);
-      prefetch_l2_bulk(base + (wbase + rr) * p.K + k_lo, static_cast<uint32_t>(k_hi - k_lo));
-    }
   }
 
   float s_a[2], s_b[2] = {0.f, 0.f};

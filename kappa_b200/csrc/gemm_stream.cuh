@@ -4,15 +4,18 @@
 //
 // When a group holds only a few rows the work is bound by int8 weight bytes,
 // not by arithmetic: every weight byte is used for at most a few dozen
-// multiply-adds.  This kernel streams each weight row once from HBM into
-// registers (16-byte non-allocating loads, the warp's whole slice first
-// requested into L2 with one bulk prefetch per row), widens int8 to bf16
-// exactly in registers and multiplies on the tensor core with
-// mma.sync.m16n8k16 (bf16 in, fp32 accumulate).  No shared-memory staging of
-// the weights, no barriers and no tile table: a CTA reads its group's row
-// range from the group offsets, and token rows are read through an optional
-// row index (the permutation's token of each sorted row), so the gather of
-// the routed rows is fused into the operand load.
+// multiply-adds.  This kernel streams each weight row once from HBM: every
+// lane copies its own 16-byte chunks of weights and token rows into a
+// per-warp shared-memory ring (cp.async, a few steps deep), widens int8 to
+// bf16 exactly in registers and multiplies on the tensor core with
+// mma.sync.m16n8k16 (bf16 in, fp32 accumulate).  A lane reads back only the
+// chunks it copied, so its own wait_group is the only synchronisation: no
+// mbarriers and no tile table.  A CTA reads its group's row range from the
+// group offsets, and token rows are read through an optional row index (the
+// permutation's token of each sorted row), so the gather of the routed rows
+// is fused into the operand load.  (Measured and dropped: bulk L2
+// prefetches of the weight rows, 128-k steps, token rows staged per CTA as
+// f16 with f16 weights; all slower.)
 //
 // A warp owns 16 output features (16 gate + 16 up rows in paired mode) and
 // one slice of K; a CTA of 8 warps covers 8/ks feature tiles x ks K slices
