@@ -351,7 +351,138 @@ def _extra_configs(lib, dev, stream, router, gate, up, down, sr, sg, su, sd):
     mlp = {"workload": "gemma3-4b W8 MLP, T=256 (BASELINE configs[0])", "us_per_call": sec * 1e6,
            "tokens_per_s": tg / sec, "tflops": flops / sec / 1e12, "frac_tc": flops / sec / 1e12 / peak_tf,
            "int8_weight_gbs": 3 * dg * hg / sec / 1e9}
-    return {"moe_decode": decode, "gemma_mlp": mlp, "peaks": f"{kind}: {peak_tf} TFLOP/s, {peak_gbs} GB/s"}
+    stack = _gemma_stack(lib, dev, timed, graphed, peak_tf, peak_gbs)
+    big = _qwen3_235b_layer(lib, dev, timed, timed_cold, graphed, peak_tf, peak_gbs)
+    return {"moe_decode": decode, "gemma_mlp": mlp, "gemma3_4b_ffn_stack": stack, "qwen3_235b_moe_layer": big,
+            "peaks": f"{kind}: {peak_tf} TFLOP/s, {peak_gbs} GB/s"}
+
+
+def _gemma_stack(lib, dev, timed, graphed, peak_tf, peak_gbs):
+    """BASELINE configs[3] on one GPU: 34 Gemma3-4B W8 MLP layers (own random
+    weights each, 2.67 GB int8), chunked prefill of 8192 tokens in 16 chunks
+    of 512, then 256 decode steps at batch 16 (each step one CUDA graph of
+    the 34 layers).  The FFN stack alone: every layer reads the same
+    activations (no attention or norms between layers in this stack), which
+    leaves the work of each FFN call unchanged."""
+    import torch
+
+    from kappa_b200 import _lib
+    from kappa_b200.qwen3.quant import kmajor, quantize_weight
+
+    n_layers, dg, hg, chunk, n_chunks, batch, steps = 34, 2560, 10240, 512, 16, 16, 256
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(3)
+    layers = []
+    for _ in range(n_layers):
+        gating = quantize_weight(torch.randn((2, hg, dg), generator=gen, device=dev) * 0.02, per_channel=True,
+                                 scale_dtype=torch.float32, in_axis=-1)
+        linear = quantize_weight(torch.randn((hg, dg), generator=gen, device=dev) * 0.02, per_channel=True,
+                                 scale_dtype=torch.float32)
+        g, lw = kmajor(gating, -1), kmajor(linear, -2)
+        layers.append((g, lw, g.struct(0), g.struct(hg), lw.struct()))
+        del gating, linear
+
+    def make_call(T):
+        x = torch.randn((T, dg), generator=gen, device=dev).to(torch.bfloat16)
+        out = torch.empty_like(x)
+        ws = torch.empty(int(lib.kw8_dense_ffn_workspace_size(T, dg, hg)), dtype=torch.uint8, device=dev)
+
+        def run_layers():
+            sp = torch.cuda.current_stream(dev).cuda_stream
+            for _, _, sg_, su_, sd_ in layers:
+                rc = lib.kw8_dense_ffn(x.data_ptr(), T, dg, hg, sg_, su_, sd_, _lib.ACT_GELU_TANH, _lib.DT_BF16,
+                                       out.data_ptr(), ws.data_ptr(), ws.numel(), sp)
+                if rc != 0:
+                    raise RuntimeError(_lib.last_error())
+
+        return run_layers
+
+    prefill_layers = make_call(chunk)
+    sec_p = timed(lambda: [prefill_layers() for _ in range(n_chunks)], reps=2)
+    step = graphed(make_call(batch))
+    sec_d = timed(step.replay, reps=steps) * steps
+    del step
+    flops = 6.0 * chunk * n_chunks * dg * hg * n_layers
+    step_bytes = n_layers * (3 * dg * hg + (2 * hg + dg) * 4)
+    return {
+        "workload": "gemma3-4b W8 FFN stack, 34 layers: prefill 8192 tokens in 16 chunks of 512, then 256 decode "
+                    "steps at batch 16 (BASELINE configs[3], 1 GPU)",
+        "prefill_ms": sec_p * 1e3, "prefill_tokens_per_s": chunk * n_chunks / sec_p,
+        "prefill_tflops": flops / sec_p / 1e12, "prefill_frac_tc": flops / sec_p / 1e12 / peak_tf,
+        "decode_ms": sec_d * 1e3, "decode_us_per_step": sec_d / steps * 1e6,
+        "decode_tokens_per_s": batch * steps / sec_d,
+        "decode_gbs": step_bytes * steps / sec_d / 1e9, "decode_frac_hbm": step_bytes * steps / sec_d / 1e9 / peak_gbs,
+        "note": "FFN layers only; each layer reads the same activations; weights (2.67 GB) exceed L2",
+    }
+
+
+def _q8_experts(shape, gen, dev, chunk=16):
+    """Per-channel W8 expert weights [E, K, N] built 16 experts at a time
+    (the scales of an expert do not depend on the others)."""
+    import torch
+
+    from kappa_b200.qwen3.quant import Q8Weight, quantize_weight
+
+    vals, scales = [], []
+    for e0 in range(0, shape[0], chunk):
+        n = min(chunk, shape[0] - e0)
+        w = torch.randn((n,) + tuple(shape[1:]), generator=gen, device=dev) * 0.02
+        q = quantize_weight(w, per_channel=True, scale_dtype=torch.float32)
+        vals.append(q.values.transpose(-1, -2))  # the K-major storage [n, N, K]
+        scales.append(q.scale)
+        del w, q
+    return Q8Weight(values=torch.cat(vals).transpose(-1, -2), scale=torch.cat(scales))
+
+
+def _qwen3_235b_layer(lib, dev, timed, timed_cold, graphed, peak_tf, peak_gbs):
+    """BASELINE configs[4], one of its 94 layers on one GPU (the 227 GB stack
+    needs the 8-GPU expert-parallel run): D=4096, I=1536, 128 experts, top-8;
+    prefill T=2048 and decode B=64."""
+    import torch
+
+    from kappa_b200 import _lib
+    from kappa_b200.qwen3 import ffn_moe as M
+    from kappa_b200.qwen3.quant import kmajor, quantize_weight
+
+    d2, i2, e2, k2 = 4096, 1536, 128, 8
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4)
+    router = quantize_weight(torch.randn((d2, e2), generator=gen, device=dev) * 0.02, per_channel=True,
+                             scale_dtype=torch.float32)
+    gate = _q8_experts((e2, d2, i2), gen, dev)
+    up = _q8_experts((e2, d2, i2), gen, dev)
+    down = _q8_experts((e2, i2, d2), gen, dev)
+    ks = [kmajor(w, -2) for w in (router, gate, up, down)]
+    st = [k.struct() for k in ks]
+    res = {"workload": "qwen3-235b-a22b-shaped W8 MoE layer (D=4096, I=1536, 128 experts, top-8; "
+                       "BASELINE configs[4], one layer of the 94 on 1 GPU)"}
+    for T, tag in ((2048, "prefill"), (64, "decode")):
+        x = torch.randn((T, d2), generator=gen, device=dev).to(torch.bfloat16)
+        out = torch.empty_like(x)
+        ws = torch.empty(int(lib.kw8_moe_ffn_workspace_size(T, d2, i2, e2, k2)), dtype=torch.uint8, device=dev)
+
+        def call():
+            rc = lib.kw8_moe_ffn(x.data_ptr(), T, d2, i2, e2, k2, -1, *st, out.data_ptr(), ws.data_ptr(),
+                                 ws.numel(), torch.cuda.current_stream(dev).cuda_stream)
+            if rc != 0:
+                raise RuntimeError(_lib.last_error())
+
+        if tag == "prefill":
+            sec = timed(call, reps=10)
+            flops = 2.0 * T * k2 * 3 * d2 * i2 + 2.0 * T * d2 * e2
+            res.update({"prefill_tokens": T, "prefill_us": sec * 1e6, "prefill_tokens_per_s": T / sec,
+                        "prefill_tflops": flops / sec / 1e12, "prefill_frac_tc": flops / sec / 1e12 / peak_tf})
+        else:
+            g = graphed(call)
+            sec = timed_cold(g.replay)
+            del g
+            _, idx, _ = M.route_logits(x.view(1, T, d2), router, num_experts=e2, num_experts_per_tok=k2)
+            active = int(torch.unique(idx).numel())
+            nbytes = active * (3 * d2 * i2 + (2 * i2 + d2) * 4) + d2 * e2
+            res.update({"decode_tokens": T, "decode_active_experts": active, "decode_us": sec * 1e6,
+                        "decode_tokens_per_s": T / sec, "decode_gbs": nbytes / sec / 1e9,
+                        "decode_frac_hbm": nbytes / sec / 1e9 / peak_gbs})
+    return res
 
 
 def run_gpu(args):
