@@ -25,6 +25,12 @@ T=4096: the same ~256 routed rows per expert, 151 MB of expert weights) and
 exits; it is the workload the committed ncu summaries capture with the full
 metric set (the full layer is captured with single-pass metrics only).
 
+``--profile-decode B`` runs two calls of the full configs[1] layer at a
+decode batch of B tokens (the workload of the committed decode captures).
+``--no-extra-configs`` leaves out the other BASELINE configs (decode
+batches, Gemma3 MLP and stack, the Qwen3-235B-shaped layer), e.g. for a
+launch list of the headline step alone.
+
 ``--impl reference`` times the reference arm instead: kappa itself is JAX,
 which is not installed here, so the arm runs the oracle restatement of
 kappa's ``_moe_ragged`` path on the host cores (rank 0 only).
@@ -221,6 +227,32 @@ def run_reference(args):
         "wall_s": elapsed,
     }
     print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_profile_decode(batch: int):
+    """Two calls of the full configs[1] layer at a decode batch (ncu captures)."""
+    import torch
+
+    from kappa_b200.qwen3 import ffn_moe as M
+    from kappa_b200.qwen3.architecture import MoEConfig
+    from kappa_b200.qwen3.quant import quantize_weight
+
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(0)
+
+    def q8(shape):
+        w = torch.randn(shape, generator=gen, device=dev, dtype=torch.float32) * 0.02
+        return quantize_weight(w, per_channel=True, scale_dtype=torch.float32)
+
+    router, gate, up, down = q8((D, E)), q8((E, D, I)), q8((E, D, I)), q8((E, I, D))
+    x = torch.randn((1, batch, D), generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    cfg = MoEConfig(use_moe=True, num_experts=E, num_experts_per_tok=K_TOP, moe_impl="ragged_jax")
+    for _ in range(2):
+        y = M.moe_swiglu_ffn(x, router, gate, up, down, cfg=cfg)
+    torch.cuda.synchronize(dev)
+    print(json.dumps({"profile_decode": batch, "mean_abs_out": float(y.float().abs().mean())}), flush=True)
     return 0
 
 
@@ -639,7 +671,8 @@ def run_gpu(args):
     if status != 0:
         raise RuntimeError(f"device status {status}")
 
-    extra = _extra_configs(lib, dev, stream, router, gate, up, down, sr, sg, su, sd) if world == 1 else None
+    extra = (_extra_configs(lib, dev, stream, router, gate, up, down, sr, sg, su, sd)
+             if world == 1 and not args.no_extra_configs else None)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -718,11 +751,15 @@ def main():
     ap.add_argument("--impl", default="kappa_b200", choices=["kappa_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-small", action="store_true")
+    ap.add_argument("--profile-decode", type=int, default=0, metavar="B")
+    ap.add_argument("--no-extra-configs", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
     if args.profile_small:
         return run_profile_small()
+    if args.profile_decode > 0:
+        return run_profile_decode(args.profile_decode)
     return run_gpu(args)
 
 
