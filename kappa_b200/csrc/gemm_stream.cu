@@ -77,7 +77,11 @@ __global__ void __launch_bounds__(kStThreads,
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
-  const int group = blockIdx.y;
+  int group = blockIdx.y;
+  if (p.active_groups != nullptr) {
+    if (group >= p.active_groups[0]) return;  // uniform over the CTA
+    group = p.active_groups[1 + group];
+  }
   int r_begin = 0, r_end = p.dense_rows;
   if (p.group_offsets != nullptr) {
     r_begin = p.group_offsets[group];
@@ -390,7 +394,9 @@ int launch_gemm_stream(int mode, const int8_t* wa, const int8_t* wb, int64_t gro
   a.ks = ks;
   const int64_t fblocks = (ftiles + (kStWarps / ks) - 1) / (kStWarps / ks);
   KW8_REQUIRE(fblocks < (1ll << 31), KW8_ERR_UNSUPPORTED, "too many feature blocks");
-  const dim3 grid(static_cast<unsigned>(fblocks), static_cast<unsigned>(groups),
+  // With an active-group list at most min(groups, routed rows) groups hold rows.
+  const int64_t grid_y = a.active_groups != nullptr ? active : groups;
+  const dim3 grid(static_cast<unsigned>(fblocks), static_cast<unsigned>(grid_y),
                   static_cast<unsigned>(zc));
   switch (mode) {
     case EPI_PAIR_GELU:

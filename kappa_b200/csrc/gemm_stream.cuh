@@ -39,6 +39,10 @@ struct StreamArgs {
   // nullptr => one group of dense_rows rows.
   const int32_t* group_offsets;
   int dense_rows;
+  // Optional list of the groups holding rows (active[0] = count, then the
+  // groups): grid row y serves group active[1 + y], so empty groups cost no
+  // CTAs.  nullptr: grid row y serves group y.
+  const int32_t* active_groups;
   // x row of sorted row r: row_index[r] (fused gather), or r when nullptr.
   const int32_t* row_index;
   // Scales (gate/plain = a, up = b).

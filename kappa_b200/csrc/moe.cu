@@ -252,19 +252,20 @@ __global__ void __launch_bounds__(kPermThreads)
                            int chunk, const int32_t* __restrict__ hist, int32_t* __restrict__ sorted_token,
                            int32_t* __restrict__ inv_pos, int32_t* __restrict__ group_sizes,
                            int32_t* __restrict__ group_offsets, const __nv_bfloat16* __restrict__ w,
-                           float* __restrict__ sorted_w) {
+                           float* __restrict__ sorted_w, int32_t* __restrict__ active) {
   extern __shared__ int sm[];
   constexpr int kWarps = kPermThreads / 32;
   int* base = sm;
   int* goff = sm + E;
   int* run = sm + 2 * E;
   int* wcnt = sm + 3 * E;
-  __shared__ int carry_sh;
+  __shared__ int carry_sh, active_sh;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int b = blockIdx.x, nblk = gridDim.x;
 
-  // Expert totals, this block's base, and the expert offsets.
-  if (threadIdx.x == 0) carry_sh = 0;
+  // Expert totals, this block's base, and the expert offsets (block 0 also
+  // lists the experts that kept rows, in order, when `active` is given).
+  if (threadIdx.x == 0) carry_sh = active_sh = 0;
   __syncthreads();
   for (int e0 = 0; e0 < E; e0 += blockDim.x) {
     const int e = e0 + threadIdx.x;
@@ -291,11 +292,21 @@ __global__ void __launch_bounds__(kPermThreads)
         group_offsets[e] = carry + off;
       }
     }
+    if (b == 0 && active != nullptr) {  // uniform over the block
+      int n_active;
+      const int pos = block_exclusive_scan((e < E && kept > 0) ? 1 : 0, &n_active);
+      if (e < E && kept > 0) active[1 + active_sh + pos] = e;
+      __syncthreads();
+      if (threadIdx.x == 0) active_sh += n_active;
+    }
     __syncthreads();
     if (threadIdx.x == 0) carry_sh = carry + total;
     __syncthreads();
   }
-  if (b == 0 && threadIdx.x == 0) group_offsets[E] = carry_sh;
+  if (b == 0 && threadIdx.x == 0) {
+    group_offsets[E] = carry_sh;
+    if (active != nullptr) active[0] = active_sh;
+  }
 
   const int beg = b * chunk;
   const int end = min(m, beg + chunk);
@@ -487,7 +498,7 @@ int64_t permute_hist_ints(int64_t E) { return static_cast<int64_t>(kPermMaxBlock
 int launch_permute_multi(const int32_t* idx, int64_t T, int k, int64_t E, int64_t capacity,
                          int32_t* hist, int32_t* sorted_token, int32_t* inv_pos,
                          int32_t* group_sizes, int32_t* group_offsets, cudaStream_t stream,
-                         const void* w, float* sorted_w) {
+                         const void* w, float* sorted_w, int32_t* active) {
   KW8_REQUIRE(E >= 1 && E <= 1024, KW8_ERR_UNSUPPORTED, "permute supports 1..1024 experts");
   KW8_REQUIRE(k >= 1 && T >= 0 && T * k < (1ll << 31), KW8_ERR_INVALID_ARG, "bad T/k");
   const int m = static_cast<int>(T * k);
@@ -513,7 +524,7 @@ int launch_permute_multi(const int32_t* idx, int64_t T, int k, int64_t E, int64_
   KW8_CHECK_LAUNCH();
   permute_scatter_kernel<<<nblk, kPermThreads, smem2, stream>>>(
       idx, m, k, static_cast<int>(E), cap, chunk, hist, sorted_token, inv_pos, group_sizes,
-      group_offsets, static_cast<const __nv_bfloat16*>(w), sorted_w);
+      group_offsets, static_cast<const __nv_bfloat16*>(w), sorted_w, active);
   KW8_CHECK_LAUNCH();
   return KW8_OK;
 }

@@ -14,13 +14,15 @@ int launch_permute(const int32_t* idx, int64_t T, int k, int64_t E, int64_t capa
                    int32_t* group_offsets, cudaStream_t stream, const void* w = nullptr,
                    float* sorted_w = nullptr);
 // Multi-block version of launch_permute (same outputs) for callers with
-// scratch: `hist` holds permute_hist_ints(E) ints.
+// scratch: `hist` holds permute_hist_ints(E) ints.  With `active` (E + 1
+// ints, optional) it also lists the experts that kept rows: active[0] =
+// their count, active[1..] = the experts in increasing order.
 constexpr int kPermMaxBlocks = 148;
 int64_t permute_hist_ints(int64_t E);
 int launch_permute_multi(const int32_t* idx, int64_t T, int k, int64_t E, int64_t capacity,
                          int32_t* hist, int32_t* sorted_token, int32_t* inv_pos,
                          int32_t* group_sizes, int32_t* group_offsets, cudaStream_t stream,
-                         const void* w, float* sorted_w);
+                         const void* w, float* sorted_w, int32_t* active = nullptr);
 int launch_f32_to_bf16(const float* acc, int64_t n, void* out, cudaStream_t stream);
 int launch_build_tiles(const int32_t* group_offsets, int64_t E, int nt, TileEntry* tiles,
                        int32_t* num_tiles, cudaStream_t stream);
