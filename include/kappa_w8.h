@@ -242,8 +242,8 @@ int kw8_moe_ffn_noalloc(const void* x, int64_t T, int64_t D, int64_t I,
  * between dispatch and the expert FFN, and between return and combine).
  *
  * kw8_ipc_*: device buffers shareable between the ranks' processes
- * (cudaMalloc + cudaIpcGetMemHandle; handles of kw8_ipc_handle_size()
- * bytes are exchanged by the caller).                                       */
+ * (cudaMalloc + cudaIpcGetMemHandle, zero-filled before returning; handles
+ * of kw8_ipc_handle_size() bytes are exchanged by the caller).             */
 size_t kw8_ipc_handle_size(void);
 int kw8_ipc_alloc(size_t bytes, void** ptr_out, void* handle_out);
 int kw8_ipc_free(void* ptr);
@@ -269,6 +269,56 @@ int kw8_ep_return(const void* ys, int64_t max_rows, int64_t D,
  * kw8_moe_expert_ffn on the received rows).                                */
 int kw8_ep_local_offsets(const int32_t* counts, int32_t world, int32_t rank,
                          int64_t E, int32_t* local_offsets, kw8_stream_t stream);
+
+/* An expert-parallel group as one rank sees it.  Every rank owns four
+ * buffers, allocated with kw8_ipc_alloc and mapped by the others with
+ * kw8_ipc_open; the device arrays hold each rank's mapping of them (this
+ * rank's own buffer at [rank]):
+ *   recv   : world * max_tokens * k rows of D bf16 (rows sent to this rank);
+ *   out    : max_tokens * k rows of D bf16 (this rank's rows coming back);
+ *   counts : int32 [2][world][E] (per-expert row counts of every rank, two
+ *            copies alternating by call);
+ *   flags  : uint32 [3][world], zero before the first call on any rank.
+ * own_* are this rank's buffers again, as host-side values.               */
+typedef struct kw8_ep_peers {
+  int32_t world;
+  int32_t rank;
+  int64_t max_tokens;
+  const uint64_t* recv;
+  const uint64_t* out;
+  const uint64_t* counts;
+  const uint64_t* flags;
+  void* own_recv;
+  void* own_out;
+  int32_t* own_counts;
+  uint32_t* own_flags;
+} kw8_ep_peers;
+
+/* The expert-parallel MoE layer over this rank's T <= max_tokens tokens in
+ * one call, with no host synchronisation and no collective library: route,
+ * permute, exchange the per-expert counts with every peer, write each
+ * routed row into its expert owner's receive buffer, wait for every peer's
+ * rows, run the local experts' FFN, write each output row back to its
+ * source, wait for every peer, combine.  The phases are ordered by flag
+ * words stored into the peers' memory (release/acquire at system scope)
+ * and tagged with `epoch`, which must grow by one per call on every rank
+ * of the group (start at 1).  gate/up/down hold this rank's E/world
+ * experts.  Every wait is bounded (2 s): a peer that never arrives leaves
+ * KW8_ERR_DEVICE_TIMEOUT in the device status (kw8_device_status) and an
+ * unspecified `out`, but no hung kernel.                                   */
+size_t kw8_moe_ffn_ep_workspace_size(int64_t max_tokens, int64_t D, int64_t I, int64_t E,
+                                     int32_t k, int32_t world);
+int kw8_moe_ffn_ep(const void* x, int64_t T, int64_t D, int64_t I, int64_t E, int32_t k,
+                   int64_t capacity, kw8_weight router, kw8_weight gate_local,
+                   kw8_weight up_local, kw8_weight down_local, void* out,
+                   const kw8_ep_peers* peers, uint32_t epoch, void* workspace,
+                   size_t workspace_bytes, kw8_stream_t stream);
+
+/* Phase `phase` (0..2) of the group barrier: with `signal` this rank first
+ * marks the phase done at every peer; then it waits (bounded) until every
+ * rank has marked it for `epoch`.                                           */
+int kw8_ep_barrier(const kw8_ep_peers* peers, int32_t phase, uint32_t epoch, int32_t signal,
+                   kw8_stream_t stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

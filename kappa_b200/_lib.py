@@ -56,6 +56,24 @@ class KW8Weight(ctypes.Structure):
     ]
 
 
+class KW8EpPeers(ctypes.Structure):
+    """``kw8_ep_peers`` (include/kappa_w8.h): an expert-parallel group seen from one rank."""
+
+    _fields_ = [
+        ("world", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("max_tokens", ctypes.c_int64),
+        ("recv", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+        ("counts", ctypes.c_void_p),
+        ("flags", ctypes.c_void_p),
+        ("own_recv", ctypes.c_void_p),
+        ("own_out", ctypes.c_void_p),
+        ("own_counts", ctypes.c_void_p),
+        ("own_flags", ctypes.c_void_p),
+    ]
+
+
 _i64 = ctypes.c_int64
 _i32 = ctypes.c_int32
 _vp = ctypes.c_void_p
@@ -90,6 +108,13 @@ SIGNATURES: dict[str, tuple] = {
     "kw8_ep_dispatch": (ctypes.c_int, [_vp, _i64, _i64, _vp, _vp, _vp, _i32, _i32, _i64, _vp, _vp]),
     "kw8_ep_return": (ctypes.c_int, [_vp, _i64, _i64, _vp, _i32, _i32, _i64, _vp, _vp]),
     "kw8_ep_local_offsets": (ctypes.c_int, [_vp, _i32, _i32, _i64, _vp, _vp]),
+    "kw8_moe_ffn_ep_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i32, _i32]),
+    "kw8_moe_ffn_ep": (
+        ctypes.c_int,
+        [_vp, _i64, _i64, _i64, _i64, _i32, _i64, KW8Weight, KW8Weight, KW8Weight, KW8Weight, _vp,
+         ctypes.POINTER(KW8EpPeers), ctypes.c_uint32, _vp, _sz, _vp],
+    ),
+    "kw8_ep_barrier": (ctypes.c_int, [ctypes.POINTER(KW8EpPeers), _i32, ctypes.c_uint32, _i32, _vp]),
     "kw8_moe_permute_ws": (ctypes.c_int, [_vp, _i64, _i32, _i64, _i64, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
     "kw8_moe_expert_ffn_workspace_size": (_sz, [_i64, _i64, _i64, _i64]),
     "kw8_moe_expert_ffn": (

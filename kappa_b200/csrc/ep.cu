@@ -116,6 +116,70 @@ __global__ void ep_local_offsets_kernel(const int32_t* __restrict__ counts, int 
   }
 }
 
+// ------------------------------------------------- group flags (peers) --
+// Phase p of call `epoch` is done by rank r when flag word [p][r] of a
+// rank's flags holds >= epoch.  Writers make their earlier stores visible
+// system-wide first (fence), then store the flag with release semantics;
+// waiters load it with acquire semantics, bounded by kWaitLimitNs.
+
+__device__ __forceinline__ void flag_release(uint32_t* f, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t flag_acquire(const uint32_t* f) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+  return v;
+}
+
+// Epochs grow by one per call: v is at or past `epoch` when the unsigned
+// difference is below half the range (robust to wrap-around).
+__device__ __forceinline__ bool flag_reached(uint32_t v, uint32_t epoch) {
+  return v - epoch < 0x80000000u;
+}
+
+__device__ bool flag_wait(const uint32_t* f, uint32_t epoch) {
+  if (flag_reached(flag_acquire(f), epoch)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (flag_reached(flag_acquire(f), epoch)) return true;
+    if ((i & 63u) == 0 && global_ns() - t0 > kWaitLimitNs) {
+      report(KW8_ERR_DEVICE_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// Signal (optionally) and wait for phase `phase` of `epoch`: lane r < world
+// marks this rank's word at rank r, then waits for rank r's word here.
+__global__ void ep_barrier_kernel(const uint64_t* __restrict__ flags, uint32_t* own_flags, int world,
+                                  int rank, int phase, uint32_t epoch, int signal) {
+  const int lane = threadIdx.x;
+  if (signal && lane < world) {
+    __threadfence_system();
+    flag_release(reinterpret_cast<uint32_t*>(flags[lane]) + phase * world + rank, epoch);
+  }
+  if (lane < world) flag_wait(own_flags + phase * world + lane, epoch);
+}
+
+// This rank's per-expert row counts into every rank's counts[epoch & 1]
+// (row `rank`), then phase 0 of the barrier: afterwards own counts[epoch &
+// 1] holds every rank's counts.
+__global__ void ep_counts_kernel(const int32_t* __restrict__ sizes, int E, const uint64_t* __restrict__ counts,
+                                 const uint64_t* __restrict__ flags, uint32_t* own_flags, int world, int rank,
+                                 uint32_t epoch) {
+  const int parity = static_cast<int>(epoch & 1u);
+  for (int p = 0; p < world; ++p) {
+    int32_t* dst = reinterpret_cast<int32_t*>(counts[p]) + (static_cast<int64_t>(parity) * world + rank) * E;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) dst[e] = sizes[e];
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < world) flag_release(reinterpret_cast<uint32_t*>(flags[threadIdx.x]) + rank, epoch);
+  if (threadIdx.x < world) flag_wait(own_flags + threadIdx.x, epoch);
+  __syncthreads();
+}
+
 int check_ep(int64_t D, int world, int rank, int64_t E) {
   KW8_REQUIRE(world >= 1 && world <= kEpMaxRanks && rank >= 0 && rank < world, KW8_ERR_INVALID_ARG,
               "bad rank %d of %d", rank, world);
@@ -164,6 +228,26 @@ int launch_ep_local_offsets(const int32_t* counts, int world, int rank, int64_t 
   if (rc) return rc;
   ep_local_offsets_kernel<<<1, 32, 0, stream>>>(counts, world, rank, static_cast<int>(E),
                                                 static_cast<int>(E / world), loc_off);
+  KW8_CHECK_LAUNCH();
+  return KW8_OK;
+}
+
+int launch_ep_barrier(const uint64_t* flags, uint32_t* own_flags, int world, int rank, int phase,
+                      uint32_t epoch, bool signal, cudaStream_t stream) {
+  KW8_REQUIRE(world >= 1 && world <= kEpMaxRanks && rank >= 0 && rank < world && phase >= 0 &&
+                  phase < 3,
+              KW8_ERR_INVALID_ARG, "bad barrier args");
+  ep_barrier_kernel<<<1, 32, 0, stream>>>(flags, own_flags, world, rank, phase, epoch, signal ? 1 : 0);
+  KW8_CHECK_LAUNCH();
+  return KW8_OK;
+}
+
+int launch_ep_counts(const int32_t* sizes, int64_t E, const uint64_t* counts, const uint64_t* flags,
+                     uint32_t* own_flags, int world, int rank, uint32_t epoch, cudaStream_t stream) {
+  int rc = check_ep(8, world, rank, E);
+  if (rc) return rc;
+  ep_counts_kernel<<<1, 256, 0, stream>>>(sizes, static_cast<int>(E), counts, flags, own_flags, world, rank,
+                                         epoch);
   KW8_CHECK_LAUNCH();
   return KW8_OK;
 }

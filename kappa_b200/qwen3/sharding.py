@@ -252,20 +252,23 @@ class EPContext:
         hsize = int(lib.kw8_ipc_handle_size())
         self.recv_rows = self.world * max_tokens * k
         self.out_rows = max_tokens * k
+        # Shared buffers (zero-filled): receive rows, return rows, per-expert
+        # counts [2][world][E] int32, phase flags [3][world] uint32.
+        sizes = (self.recv_rows * d * 2, self.out_rows * d * 2, 2 * self.world * num_experts * 4, 3 * self.world * 4)
         self._own = []
         handles = []
-        for rows in (self.recv_rows, self.out_rows):
+        for nbytes in sizes:
             ptr = ctypes.c_void_p()
             h = ctypes.create_string_buffer(hsize)
-            _lib.check(lib.kw8_ipc_alloc(rows * d * 2, ctypes.byref(ptr), h))
+            _lib.check(lib.kw8_ipc_alloc(nbytes, ctypes.byref(ptr), h))
             self._own.append(ptr.value)
             handles.append(h.raw)
         allh = [None] * self.world
         dist.all_gather_object(allh, handles, group=group)
         self._opened = []
-        peers = [[], []]
+        peers = [[] for _ in sizes]
         for r, hs in enumerate(allh):
-            for b in range(2):
+            for b in range(len(sizes)):
                 if r == self.rank:
                     peers[b].append(self._own[b])
                 else:
@@ -277,9 +280,18 @@ class EPContext:
         def as_i64(v):
             return [int(a) - (1 << 64) if int(a) >= (1 << 63) else int(a) for a in v]
 
-        self.peer_recv = torch.tensor(as_i64(peers[0]), dtype=torch.int64, device=self.device)
-        self.peer_out = torch.tensor(as_i64(peers[1]), dtype=torch.int64, device=self.device)
-        self.recv_ptr, self.out_ptr = self._own
+        self.peer_recv, self.peer_out, self.peer_counts, self.peer_flags = (
+            torch.tensor(as_i64(v), dtype=torch.int64, device=self.device) for v in peers)
+        self.recv_ptr, self.out_ptr, self.counts_ptr, self.flags_ptr = self._own
+        self.peers = _lib.KW8EpPeers(
+            self.world, self.rank, max_tokens, self.peer_recv.data_ptr(), self.peer_out.data_ptr(),
+            self.peer_counts.data_ptr(), self.peer_flags.data_ptr(), self.recv_ptr, self.out_ptr,
+            self.counts_ptr, self.flags_ptr)
+        self.epoch = 0  # calls of the fused layer so far (the group's phase tag)
+        self.ep_ws = torch.empty(
+            int(lib.kw8_moe_ffn_ep_workspace_size(max_tokens, d, hidden, num_experts, k, self.world)),
+            dtype=torch.uint8, device=self.device)
+        # Staged path (kw8_ep_dispatch / kw8_ep_return + collectives).
         self.ys_loc = torch.empty((self.recv_rows, d), dtype=torch.bfloat16, device=self.device)
         e_loc = num_experts // self.world
         self.ws = torch.empty(int(lib.kw8_moe_expert_ffn_workspace_size(self.recv_rows, d, hidden, e_loc)),
@@ -288,6 +300,9 @@ class EPContext:
         self.counts = torch.empty((self.world, num_experts), dtype=torch.int32, device=self.device)
         self.flag = torch.zeros(1, dtype=torch.float32, device=self.device)
         self.closed = False
+        # Every rank's buffers (flags included) are zero before anyone signals.
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=group)
 
     def sync(self):
         """Orders the phases across ranks on the current stream (a one-element all-reduce)."""
@@ -308,7 +323,8 @@ class EPContext:
         self.closed = True
 
 
-def _moe_ep_p2p(x, router_w, gate_local, up_local, down_local, *, cfg, ctx: EPContext, capacity):
+def _moe_ep_p2p(x, router_w, gate_local, up_local, down_local, *, cfg, ctx: EPContext, capacity,
+                staged: bool = False):
     from kappa_b200.qwen3 import ffn_moe
 
     lib = _lib.load()
@@ -325,6 +341,18 @@ def _moe_ep_p2p(x, router_w, gate_local, up_local, down_local, *, cfg, ctx: EPCo
         raise ValueError("local expert weights do not match the EPContext")
     xc = x.contiguous()
     stream = _lib.stream_of(x)
+    if not staged:
+        # One call: device-side counts exchange and phase flags, no host
+        # round trip and no collective library.
+        r = kmajor(router_w, -2, "router_w")
+        out = torch.empty((b, t, d), dtype=torch.bfloat16, device=x.device)
+        ctx.epoch += 1
+        _lib.check(lib.kw8_moe_ffn_ep(
+            xc.data_ptr(), T, d, i, e, k, -1 if capacity is None else int(capacity), r.struct(), g.struct(),
+            u.struct(), dn.struct(), out.data_ptr(), ctypes.byref(ctx.peers), ctx.epoch & 0xFFFFFFFF,
+            ctx.ep_ws.data_ptr(), ctx.ep_ws.numel(), stream))
+        del r, g, u, dn
+        return out
     _, idx, w = ffn_moe.route_logits(xc, router_w, num_experts=e, num_experts_per_tok=k)
     st, inv, sizes, offs = ffn_moe.permute(idx, e, capacity)
     dist.all_gather_into_tensor(ctx.counts, sizes, group=ctx.group)
@@ -347,18 +375,23 @@ def _moe_ep_p2p(x, router_w, gate_local, up_local, down_local, *, cfg, ctx: EPCo
 
 
 def moe_swiglu_ffn_ep(x: torch.Tensor, router_w: Weight, gate_local: Weight, up_local: Weight, down_local: Weight,
-                      *, cfg, group=None, ops: MoEOps | None = None, ctx: EPContext | None = None) -> torch.Tensor:
+                      *, cfg, group=None, ops: MoEOps | None = None, ctx: EPContext | None = None,
+                      staged: bool = False) -> torch.Tensor:
     """Expert-parallel MoE layer over this rank's tokens ``x`` ``[B, T, D]`` (prefill).
 
     ``gate_local`` / ``up_local`` / ``down_local`` hold this rank's E/R experts
     (``shard_experts``); ``router_w`` is the full router.  Returns the same
     ``[B, T, D]`` bf16 as the single-GPU layer on ``x`` with every expert.
     With ``ctx`` (an :class:`EPContext` of this group) the rows move over
-    NVLink with the B200 kernels; otherwise with NCCL all-to-allv.
+    NVLink with the B200 kernels: by default the whole layer is one library
+    call (``kw8_moe_ffn_ep``: counts exchange and phase order by flags in the
+    peers' memory); ``staged=True`` runs the same movement as separate calls
+    ordered by NCCL collectives.  Without ``ctx``: NCCL all-to-allv.
     """
     if ctx is not None and ops is None:
         _, _, _, capacity = _moe_args(cfg, x)
-        return _moe_ep_p2p(x, router_w, gate_local, up_local, down_local, cfg=cfg, ctx=ctx, capacity=capacity)
+        return _moe_ep_p2p(x, router_w, gate_local, up_local, down_local, cfg=cfg, ctx=ctx, capacity=capacity,
+                           staged=staged)
     ops = ops or KernelMoEOps()
     world, rank = _world(group)
     e, k = cfg.num_experts, cfg.num_experts_per_tok

@@ -417,3 +417,26 @@ def test_moe_errors_match_kappa():
     with pytest.raises(ValueError, match="moe_capacity_factor"):
         M.moe_swiglu_ffn(to_dev(x), *g, cfg=MoEConfig(use_moe=True, num_experts=E, num_experts_per_tok=k,
                                                       moe_impl="fixed_capacity", moe_capacity_factor=0.0))
+
+
+def test_ep_barrier_wait_times_out():
+    """Failure detection of the expert-parallel phase flags without a fault:
+    a wait for a phase that no rank marks runs out after its bound (about
+    2 s), records KW8_ERR_DEVICE_TIMEOUT in the device status and returns;
+    the context stays usable and a signalled phase then passes."""
+    import ctypes
+
+    dev = torch.device("cuda", 0)
+    counts = torch.zeros(2 * 1 * 8, dtype=torch.int32, device=dev)
+    flags = torch.zeros(3, dtype=torch.int32, device=dev)
+    buf = torch.zeros(64, dtype=torch.uint8, device=dev)
+    arr = [torch.tensor([t.data_ptr()], dtype=torch.int64, device=dev) for t in (buf, buf, counts, flags)]
+    peers = _lib.KW8EpPeers(1, 0, 0, arr[0].data_ptr(), arr[1].data_ptr(), arr[2].data_ptr(), arr[3].data_ptr(),
+                            buf.data_ptr(), buf.data_ptr(), counts.data_ptr(), flags.data_ptr())
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    _lib.check(lib.kw8_ep_barrier(ctypes.byref(peers), 1, 7, 0, stream))  # nobody marks epoch 7
+    assert _lib.device_status(buf) == _lib.KW8_ERR_DEVICE_TIMEOUT
+    _lib.check(lib.kw8_ep_barrier(ctypes.byref(peers), 1, 7, 1, stream))  # this rank marks it
+    assert _lib.device_status(buf) == 0
+    assert int(flags[1].item()) == 7

@@ -32,6 +32,12 @@ def _oracle_q(w, axis=-2):
     return O.quantize_weight(w, per_channel_axis=axis, scale_dtype=np.float32)
 
 
+def _lib_status(dev) -> int:
+    from kappa_b200 import _lib
+
+    return _lib.device_status(torch.zeros(1, device=dev))
+
+
 def _rank_main(rank: int, world: int, port: int, errfile: str):
     try:
         os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -53,8 +59,15 @@ def _rank_main(rank: int, world: int, port: int, errfile: str):
         x = normal(np.random.default_rng(100 + rank), (1, 300 + 50 * rank, D)).astype(O.BF16)
         y = S.moe_swiglu_ffn_ep(to_dev(x, dev), router, gl, ul, dl, cfg=cfg)  # NCCL all-to-allv
         ctx = S.EPContext(max_tokens=400, d=D, k=K, hidden=I, num_experts=E)
-        y2 = S.moe_swiglu_ffn_ep(to_dev(x, dev), router, gl, ul, dl, cfg=cfg, ctx=ctx)  # NVLink P2P
+        y2 = S.moe_swiglu_ffn_ep(to_dev(x, dev), router, gl, ul, dl, cfg=cfg, ctx=ctx)  # one call, peer flags
         y3 = S.moe_swiglu_ffn_ep(to_dev(x, dev), router, gl, ul, dl, cfg=cfg, ctx=ctx)  # buffers reused
+        y4 = S.moe_swiglu_ffn_ep(to_dev(x, dev), router, gl, ul, dl, cfg=cfg, ctx=ctx, staged=True)  # collectives
+        # a rank with fewer tokens than the others, then with none at all
+        few = to_dev(x[:, : 37 + 100 * rank], dev)
+        y5 = S.moe_swiglu_ffn_ep(few, router, gl, ul, dl, cfg=cfg, ctx=ctx)
+        none = to_dev(x[:, :0] if rank == 0 else x, dev)
+        y6 = S.moe_swiglu_ffn_ep(none, router, gl, ul, dl, cfg=cfg, ctx=ctx)
+        assert _lib_status(dev) == 0
         # reference on this rank's tokens with the routing the GPU chose
         from kappa_b200.qwen3 import ffn_moe as M
 
@@ -64,6 +77,12 @@ def _rank_main(rank: int, world: int, port: int, errfile: str):
         parity(to_np(y), ref, tol=2e-2)
         parity(to_np(y2), ref, tol=2e-2)
         assert torch.equal(y2, y3)
+        parity(to_np(y4), to_np(y2), tol=1e-2)
+        parity(to_np(y5), to_np(y2)[:, : 37 + 100 * rank], tol=1e-2)
+        if rank == 0:
+            assert tuple(y6.shape) == (1, 0, D)
+        else:
+            parity(to_np(y6), to_np(y2), tol=1e-2)
         # the single-GPU layer with every expert on the same tokens
         y1 = M.moe_swiglu_ffn(to_dev(x, dev), router, gate, up, down, cfg=cfg)
         parity(to_np(y2), to_np(y1), tol=2e-2)
