@@ -111,6 +111,31 @@ int pick_nt_dense(int64_t rows, int64_t m_tiles) {
   return best;
 }
 
+// K splits for a dense tensor-core GEMM of `tiles` output tiles over
+// k_tiles k tiles: split only when the tiles fill at most half the SMs,
+// into at most 8 ranges of at least 4 k tiles, filling the SMs once
+// (fp32 partials, summed in range order by launch_reduce_splits).
+int pick_k_splits(int64_t tiles, int64_t k_tiles) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+  const int64_t sms = num_sms(dev);
+  if (tiles <= 0 || tiles * 2 > sms) return 1;
+  const int64_t want = std::min<int64_t>({sms / tiles, k_tiles / 4, 8});
+  return valid_k_splits(static_cast<int>(std::max<int64_t>(want, 1)), k_tiles);
+}
+
+// Split plan of a dense tensor-core GEMM with fp32 output: T rows, N_out
+// features (128 per tile), K; 1 = no split.
+int dense_f32_splits(int64_t T, int64_t N_out, int64_t K) {
+  const int64_t m_tiles = (N_out + 127) / 128;
+  const int nt = pick_nt_dense(T, m_tiles);
+  return pick_k_splits((T + nt - 1) / nt * m_tiles, (K + kTcBK - 1) / kTcBK);
+}
+
+// Router logits on the tensor-core path (T above kStreamRouterMaxRows) with
+// a split: the fp32 partial buffer it needs, in floats (0 without split).
+int64_t router_part_floats(int64_t T, int64_t D, int64_t E);
+
 // Routed rows per group up to m + 3 sqrt(m) for groups of mean m rows.
 double rows_hint(int64_t rows, int64_t groups) {
   const double mean = static_cast<double>(rows) / static_cast<double>(groups > 0 ? groups : 1);
@@ -200,6 +225,7 @@ struct MoeBuffers {
   float* acc;  // [T][D] fp32 accumulation of the fused combine
   int32_t* perm_hist;  // per-block expert histograms of the permutation
   int32_t* active;     // [E + 1]: count, then the experts that kept rows
+  float* router_part;  // split-K partial logits of the tensor-core router (or empty)
 };
 
 struct ExpertBuffers {
@@ -236,6 +262,7 @@ MoeBuffers carve_moe(Carver& c, int64_t T, int64_t D, int64_t I, int64_t E, int 
   b.xs = c.take<__nv_bfloat16>(m * D);
   b.h = c.take<__nv_bfloat16>(m * I);
   b.acc = c.take<float>(T * D);
+  b.router_part = c.take<float>(router_part_floats(T, D, E));
   b.perm_hist = c.take<int32_t>(permute_hist_ints(E));
   b.active = c.take<int32_t>(E + 1);
   return b;
@@ -295,11 +322,23 @@ int expert_ffn(bool streamed, const void* x, const int32_t* row_index, int64_t r
   return run_gemm(mode, down, nullptr, E, D, I, b.h, rows, I, d, stream);
 }
 
-int route(const void* x, int64_t T, int64_t D, int64_t E, int k, const kw8_weight& router,
-          float* logits, int32_t* idx, void* w, cudaStream_t stream) {
-  int rc;
+bool router_streamed(int64_t T) {
   const int path = g_opt_path.load();
-  if (path == 2 || (path == 0 && T <= kStreamRouterMaxRows)) {
+  return path == 2 || (path == 0 && T <= kStreamRouterMaxRows);
+}
+
+int64_t router_part_floats(int64_t T, int64_t D, int64_t E) {
+  if (router_streamed(T)) return 0;
+  const int splits = dense_f32_splits(T, E, D);
+  return splits > 1 ? splits * T * E : 0;
+}
+
+// Router logits + top-k.  `part` (router_part_floats(T, D, E) floats, or
+// nullptr) lets the tensor-core path split K over more SMs.
+int route(const void* x, int64_t T, int64_t D, int64_t E, int k, const kw8_weight& router,
+          float* logits, int32_t* idx, void* w, cudaStream_t stream, float* part = nullptr) {
+  int rc;
+  if (router_streamed(T)) {
     StreamArgs r = stream_args(router, nullptr);
     r.dense_rows = static_cast<int>(T);
     r.out = logits;
@@ -312,10 +351,24 @@ int route(const void* x, int64_t T, int64_t D, int64_t E, int k, const kw8_weigh
     r.nt = pick_nt_dense(T, (E + 127) / 128);
     r.out = logits;
     r.ld_out = E;
+    const int splits = part != nullptr ? dense_f32_splits(T, E, D) : 1;
+    if (splits > 1) {
+      r.out = part;
+      r.k_splits = splits;
+      r.split_stride = T * E;
+    }
     rc = run_gemm(EPI_PLAIN_F32, router, nullptr, 1, E, D, x, T, D, r, stream);
+    if (!rc && splits > 1) rc = launch_reduce_splits(part, splits, T * E, T * E, logits, false, stream);
   }
   if (rc) return rc;
   return launch_topk(logits, T, E, k, idx, w, stream);
+}
+
+// Down projection split over K (tensor-core path only): its fp32 partials.
+int64_t dense_down_part_floats(int64_t T, int64_t D, int64_t H) {
+  if (T <= 0 || use_stream(static_cast<double>(T))) return 0;
+  const int splits = dense_f32_splits(T, D, H);
+  return splits > 1 ? splits * T * D : 0;
 }
 
 }  // namespace
@@ -375,9 +428,9 @@ int kw8_dequantize(kw8_weight w, int64_t groups, int64_t N, int64_t K, int32_t o
 }
 
 size_t kw8_dense_ffn_workspace_size(int64_t T, int64_t D, int64_t H) {
-  (void)D;
   Carver c(nullptr, SIZE_MAX);
   c.take<__nv_bfloat16>(T * H);
+  c.take<float>(dense_down_part_floats(T, D, H));
   return c.off;
 }
 
@@ -398,6 +451,8 @@ int kw8_dense_ffn(const void* x, int64_t T, int64_t D, int64_t H, kw8_weight gat
   KW8_REQUIRE(T < (1ll << 31), KW8_ERR_UNSUPPORTED, "too many tokens");
   Carver c(workspace, workspace_bytes);
   __nv_bfloat16* h = c.take<__nv_bfloat16>(T * H);
+  const int64_t part_floats = dense_down_part_floats(T, D, H);
+  float* part = c.take<float>(part_floats);
   KW8_REQUIRE(workspace != nullptr && c.ok, KW8_ERR_WORKSPACE, "dense FFN workspace too small");
   const int epi_pair = act == KW8_ACT_GELU_TANH ? EPI_PAIR_GELU : EPI_PAIR_SILU;
   const int epi_out = out_dtype == KW8_DT_F32 ? EPI_PLAIN_F32 : EPI_PLAIN_BF16;
@@ -427,6 +482,16 @@ int kw8_dense_ffn(const void* x, int64_t T, int64_t D, int64_t H, kw8_weight gat
   d.nt = pick_nt_dense(T, (D + 127) / 128);
   d.out = out;
   d.ld_out = D;
+  if (part_floats > 0) {
+    // Few output tiles: split K over more SMs into fp32 partials, then sum
+    // them in order into the output.
+    d.out = part;
+    d.k_splits = static_cast<int>(part_floats / (T * D));
+    d.split_stride = T * D;
+    rc = run_gemm(EPI_PLAIN_F32, down, nullptr, 1, D, H, h, T, H, d, stream);
+    if (rc) return rc;
+    return launch_reduce_splits(part, d.k_splits, T * D, T * D, out, out_dtype == KW8_DT_BF16, stream);
+  }
   return run_gemm(epi_out, down, nullptr, 1, D, H, h, T, H, d, stream);
 }
 
@@ -537,7 +602,8 @@ int kw8_moe_ffn(const void* x, int64_t T, int64_t D, int64_t I, int64_t E, int32
   KW8_REQUIRE(workspace != nullptr && c.ok, KW8_ERR_WORKSPACE,
               "MoE workspace too small (%zu < %zu)", workspace_bytes, c.off);
   const int64_t m = T * k;
-  rc = kw8::route(x, T, D, E, k, router, b.logits, b.idx, b.w, stream);
+  rc = kw8::route(x, T, D, E, k, router, b.logits, b.idx, b.w, stream,
+                  router_part_floats(T, D, E) > 0 ? b.router_part : nullptr);
   if (rc) return rc;
   rc = launch_permute_multi(b.idx, T, k, E, capacity, b.perm_hist, b.sorted_token, b.inv_pos,
                             b.group_sizes, b.group_offsets, stream, b.w, b.sorted_w, b.active);

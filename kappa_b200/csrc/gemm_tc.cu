@@ -8,10 +8,18 @@ namespace {
 
 struct TileInfo {
   int group, row0, nrows, mt;
+  int ks, kt0, kt1;  // K split and its k tiles [kt0, kt1)
 };
 
-__device__ __forceinline__ TileInfo decode_tile(const GemmArgs& p, int t) {
+// Work unit t: K split t % k_splits of feature tile mt of table entry e.
+__device__ __forceinline__ TileInfo decode_tile(const GemmArgs& p, int t, int k_tiles) {
   TileInfo ti;
+  const int nks = p.k_splits > 1 ? p.k_splits : 1;
+  ti.ks = t % nks;
+  t /= nks;
+  const int per = (k_tiles + nks - 1) / nks;
+  ti.kt0 = ti.ks * per;
+  ti.kt1 = min(k_tiles, ti.kt0 + per);
   const int e = t / p.m_tiles;
   ti.mt = t - e * p.m_tiles;
   if (p.tiles == nullptr) {
@@ -156,7 +164,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& p, const TileInfo&
           const float y = __uint_as_float(r[j]) * s;
           const int64_t o = static_cast<int64_t>(ti.row0 + tok) * p.ld_out + f;
           if constexpr (kMode == EPI_PLAIN_F32)
-            static_cast<float*>(p.out)[o] = y;
+            static_cast<float*>(p.out)[o + ti.ks * p.split_stride] = y;
           else
             static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(y);
         }
@@ -223,8 +231,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   const int n_entries =
       (p.tiles == nullptr) ? (p.dense_rows + p.nt - 1) / p.nt : *p.num_tiles;
-  const int total_tiles = n_entries * p.m_tiles;
   const int k_tiles = (p.K + kTcBK - 1) / kTcBK;
+  const int total_tiles = n_entries * p.m_tiles * (p.k_splits > 1 ? p.k_splits : 1);
 
   if (warp == 0 || warp == 2 || warp == 3) {
     if (lane == 0) {
@@ -241,9 +249,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       uint32_t issued_mask = 0, issued_parity = 0;
       bool ok = true;
       for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
-        const TileInfo ti = decode_tile(p, t);
+        const TileInfo ti = decode_tile(p, t, k_tiles);
         const int a_row = ti.group * p.N_out + ti.mt * (kPair ? 64 : 128);
-        for (int kt = 0; kt < k_tiles; ++kt) {
+        for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
             ok = false;
             break;
@@ -287,14 +295,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       uint32_t phase = 0, acc_phase = 0;  // acc_phase bit b: phase of buffer b
       bool ok = true;
       for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x, ++nt_done) {
-        const TileInfo ti = decode_tile(p, t);
+        const TileInfo ti = decode_tile(p, t, k_tiles);
         const int ab = nt_done % nbuf;
         const uint32_t n_mma = static_cast<uint32_t>(max(16, (ti.nrows + 15) & ~15));
         const uint32_t idesc = idesc_bf16_f32(128, n_mma);
         if (!mbar_wait(&acc_empty[ab], ((acc_phase >> ab) & 1u) ^ 1u, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem + static_cast<uint32_t>(ab) * acc_cols;
-        for (int kt = 0; kt < k_tiles; ++kt) {
+        for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
           // aready[s] completes after every converter saw full[s], so the
           // token tile of the stage has landed as well.
           if (!mbar_wait(&aready[stage], phase, abort_flag)) {
@@ -311,7 +319,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if (kk < kk_n) {
               const uint64_t bdesc =
                   smem_desc_kmajor_sw128(b_addr + (kk >> 2) * b_half + (kk & 3) * 32);
-              mma_ts_bf16(d_tmem, a_tmem + kk * 8, bdesc, idesc, (kt | kk) != 0 ? 1u : 0u);
+              mma_ts_bf16(d_tmem, a_tmem + kk * 8, bdesc, idesc, (kt != ti.kt0 || kk != 0) ? 1u : 0u);
             }
           }
           mma_commit(&empty[stage]);
@@ -341,7 +349,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint32_t phase = 0;
     bool ok = true;
     for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
-      for (int kt = 0; kt < k_tiles; ++kt) {
+      const TileInfo ti = decode_tile(p, t, k_tiles);
+      for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
         // Warp-uniform outcome: the tcgen05.st below needs all 32 lanes.
         if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], phase, abort_flag))) {
           ok = false;
@@ -376,7 +385,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint32_t acc_phase = 0;
     int nt_done = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++nt_done) {
-      const TileInfo ti = decode_tile(p, t);
+      const TileInfo ti = decode_tile(p, t, k_tiles);
       const int ab = nt_done % nbuf;
       if (!__all_sync(0xffffffffu,
                       mbar_wait(&acc_full[ab], (acc_phase >> ab) & 1u, abort_flag)))
@@ -431,6 +440,49 @@ int launch_mode(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap&
 }
 
 }  // namespace
+
+namespace {
+
+__global__ void reduce_splits_kernel(const float4* __restrict__ part, int splits, int64_t stride4, int64_t n4,
+                                     void* out, int out_bf16) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float4 a = part[i];
+    for (int s = 1; s < splits; ++s) {
+      const float4 b = part[s * stride4 + i];
+      a.x += b.x;
+      a.y += b.y;
+      a.z += b.z;
+      a.w += b.w;
+    }
+    if (out_bf16) {
+      __nv_bfloat162 lo = __floats2bfloat162_rn(a.x, a.y), hi = __floats2bfloat162_rn(a.z, a.w);
+      uint2 v;
+      v.x = *reinterpret_cast<uint32_t*>(&lo);
+      v.y = *reinterpret_cast<uint32_t*>(&hi);
+      static_cast<uint2*>(out)[i] = v;
+    } else {
+      static_cast<float4*>(out)[i] = a;
+    }
+  }
+}
+
+}  // namespace
+
+int launch_reduce_splits(const float* part, int splits, int64_t stride, int64_t n, void* out,
+                         bool out_bf16, cudaStream_t stream) {
+  KW8_REQUIRE(n % 4 == 0 && stride % 4 == 0 && splits >= 1 &&
+                  (reinterpret_cast<uintptr_t>(part) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(out) & (out_bf16 ? 7 : 15)) == 0,
+              KW8_ERR_UNSUPPORTED, "split reduction needs 4-element alignment");
+  if (n <= 0) return KW8_OK;
+  const int64_t n4 = n / 4;
+  const int64_t blocks = std::min<int64_t>((n4 + 255) / 256, 148 * 8);
+  reduce_splits_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(
+      reinterpret_cast<const float4*>(part), splits, stride / 4, n4, out, out_bf16 ? 1 : 0);
+  KW8_CHECK_LAUNCH();
+  return KW8_OK;
+}
 
 // Launches the grouped GEMM.  `wa` (and `wb` in paired mode) are int8
 // [groups][N_out][K]; x is bf16 [x_rows][ldx].  `args_in` carries the tile
@@ -495,7 +547,13 @@ int launch_gemm_tc(int mode, const int8_t* wa, const int8_t* wb, int64_t groups,
   int64_t max_entries = args.tiles == nullptr
                             ? (args.dense_rows + args.nt - 1) / args.nt
                             : groups + (x_rows + args.nt - 1) / args.nt;
-  int64_t max_tiles = max_entries * args.m_tiles;
+  const int64_t k_tiles = (K + kTcBK - 1) / kTcBK;
+  if (args.k_splits > 1) {
+    KW8_REQUIRE(mode == EPI_PLAIN_F32 && args.k_splits == valid_k_splits(args.k_splits, k_tiles) &&
+                    args.split_stride > 0,
+                KW8_ERR_INVALID_ARG, "split K needs fp32 output, non-empty ranges and a stride");
+  }
+  int64_t max_tiles = max_entries * args.m_tiles * (args.k_splits > 1 ? args.k_splits : 1);
   if (max_tiles <= 0) return KW8_OK;
   int dev = 0;
   KW8_CUDA_TRY(cudaGetDevice(&dev));

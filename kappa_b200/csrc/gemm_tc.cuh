@@ -91,6 +91,11 @@ struct GemmArgs {
   // EPI_COMBINE_F32 only: token and routing weight of every sorted row.
   const int32_t* row_token;
   const float* row_weight;
+  // Split K (EPI_PLAIN_F32 only): each tile's k tiles are cut into
+  // k_splits near-equal ranges run by different CTAs; range s writes its
+  // partial sums to out + s * split_stride floats (0 or 1: no split).
+  int k_splits;
+  int64_t split_stride;
   // Pipeline plan (tc_plan), filled in by the launcher.
   int stages, stage_bytes, acc_cols, nbuf;
 };
@@ -135,6 +140,18 @@ inline TcPlan tc_plan(int nt) {
   pl.smem_bytes = pl.stages * pl.stage_bytes + 1024;  // + 1 KB alignment slack
   return pl;
 }
+
+// Largest k_splits <= want for k_tiles k tiles with every range non-empty.
+inline int valid_k_splits(int want, int64_t k_tiles) {
+  int s = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, k_tiles)));
+  while (s > 1 && (s - 1) * ((k_tiles + s - 1) / s) >= k_tiles) --s;
+  return s;
+}
+
+// out[i] = sum over s < splits of part[s * stride + i] (in that order), as
+// fp32 or bf16; n a multiple of 4.
+int launch_reduce_splits(const float* part, int splits, int64_t stride, int64_t n, void* out,
+                         bool out_bf16, cudaStream_t stream);
 
 int launch_gemm_tc(int mode, const int8_t* wa, const int8_t* wb, int64_t groups,
                    int64_t N_out, int64_t K, const void* x, int64_t x_rows,
