@@ -158,6 +158,8 @@ bool use_stream(double hint) {
   return hint <= kStreamMaxRowsHint;
 }
 
+constexpr int kStreamMaxKz = 16;  // CTAs sharing a feature tile's K, weight-streaming path
+
 // Router logits: dense rows of the router GEMM up to this many go to the
 // weight-streaming kernel.
 constexpr int64_t kStreamRouterMaxRows = 256;
@@ -297,6 +299,7 @@ int expert_ffn(bool streamed, const void* x, const int32_t* row_index, int64_t r
     d.ld_out = D;
     d.row_token = row_token;
     d.row_weight = row_weight;
+    d.kz_max = kStreamMaxKz;  // used by the combine mode only (its atomics add the K ranges)
     return launch_gemm_stream(mode, down.q, nullptr, E, D, I, b.h, I, rows, nt, d, stream);
   }
   KW8_REQUIRE(row_index == nullptr, KW8_ERR_INVALID_ARG, "tensor-core path takes gathered rows");
@@ -327,9 +330,14 @@ bool router_streamed(int64_t T) {
   return path == 2 || (path == 0 && T <= kStreamRouterMaxRows);
 }
 
+// K split over CTAs of a dense fp32-output weight-streaming GEMM (1: none).
+int stream_f32_kz(int64_t T, int64_t N_out, int64_t K) {
+  const int nt = stream_nt(static_cast<double>(T));
+  return stream_plan(EPI_PLAIN_F32, nt, false, false, 1, T, T, N_out, K, kStreamMaxKz).kz;
+}
+
 int64_t router_part_floats(int64_t T, int64_t D, int64_t E) {
-  if (router_streamed(T)) return 0;
-  const int splits = dense_f32_splits(T, E, D);
+  const int splits = router_streamed(T) ? stream_f32_kz(T, E, D) : dense_f32_splits(T, E, D);
   return splits > 1 ? splits * T * E : 0;
 }
 
@@ -343,8 +351,15 @@ int route(const void* x, int64_t T, int64_t D, int64_t E, int k, const kw8_weigh
     r.dense_rows = static_cast<int>(T);
     r.out = logits;
     r.ld_out = E;
+    const int kz = part != nullptr ? stream_f32_kz(T, E, D) : 1;
+    if (kz > 1) {
+      r.out = part;
+      r.kz_max = kStreamMaxKz;
+      r.split_stride = T * E;
+    }
     rc = launch_gemm_stream(EPI_PLAIN_F32, router.q, nullptr, 1, E, D, x, D, T,
                             stream_nt(static_cast<double>(T)), r, stream);
+    if (!rc && kz > 1) rc = launch_reduce_splits(part, kz, T * E, T * E, logits, false, stream);
   } else {
     GemmArgs r = base_args(router, nullptr);
     r.dense_rows = static_cast<int>(T);
@@ -366,8 +381,9 @@ int route(const void* x, int64_t T, int64_t D, int64_t E, int k, const kw8_weigh
 
 // Down projection split over K (tensor-core path only): its fp32 partials.
 int64_t dense_down_part_floats(int64_t T, int64_t D, int64_t H) {
-  if (T <= 0 || use_stream(static_cast<double>(T))) return 0;
-  const int splits = dense_f32_splits(T, D, H);
+  if (T <= 0) return 0;
+  const int splits =
+      use_stream(static_cast<double>(T)) ? stream_f32_kz(T, D, H) : dense_f32_splits(T, D, H);
   return splits > 1 ? splits * T * D : 0;
 }
 
@@ -468,6 +484,17 @@ int kw8_dense_ffn(const void* x, int64_t T, int64_t D, int64_t H, kw8_weight gat
     d.dense_rows = static_cast<int>(T);
     d.out = out;
     d.ld_out = D;
+    if (part_floats > 0) {
+      // Few rows and long K: the CTAs split K into fp32 partials, summed in
+      // order into the output.
+      const int kz = static_cast<int>(part_floats / (T * D));
+      d.out = part;
+      d.kz_max = kStreamMaxKz;
+      d.split_stride = T * D;
+      rc = launch_gemm_stream(EPI_PLAIN_F32, down.q, nullptr, 1, D, H, h, H, T, nt, d, stream);
+      if (rc) return rc;
+      return launch_reduce_splits(part, kz, T * D, T * D, out, out_dtype == KW8_DT_BF16, stream);
+    }
     return launch_gemm_stream(epi_out, down.q, nullptr, 1, D, H, h, H, T, nt, d, stream);
   }
   GemmArgs g = base_args(gate, &up);

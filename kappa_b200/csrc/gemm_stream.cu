@@ -9,6 +9,7 @@ namespace {
 constexpr int kStThreads = 256;  // 8 warps
 constexpr int kStWarps = kStThreads / 32;
 constexpr int kStStepK = 64;     // k per warp step: 4 lanes x 16 bytes
+constexpr double kStCtaSteps = 3.0;  // fixed cost of a CTA, in warp steps (stream_plan)
 
 // Per-warp copy ring: a stage holds one step's 16-byte chunks of every lane
 // (kMats x 2 weight rows, 2 per 8-token tile).  Depth from the chunk count,
@@ -87,8 +88,12 @@ __global__ void __launch_bounds__(kStThreads,
     r_begin = p.group_offsets[group];
     r_end = p.group_offsets[group + 1];
   }
+  // grid z = (K range kzi) x (row pass zi).
+  const int kz = p.kz > 1 ? p.kz : 1;
+  const int zc = static_cast<int>(gridDim.z) / kz;
+  const int zi = static_cast<int>(blockIdx.z) % zc, kzi = static_cast<int>(blockIdx.z) / zc;
   // Same outcome for every thread of the CTA (no barrier has been passed).
-  if (r_begin + static_cast<int>(blockIdx.z) * kNT >= r_end) return;
+  if (r_begin + zi * kNT >= r_end) return;
 
   const int ks = p.ks;
   const int ftile = blockIdx.x * (kStWarps / ks) + warp / ks;
@@ -96,8 +101,9 @@ __global__ void __launch_bounds__(kStThreads,
   const int f0 = ftile * 16;
   const bool tile_ok = f0 < p.N_out;
   const int nsteps = (p.K + kStStepK - 1) / kStStepK;
-  const int s_lo = nsteps * kslice / ks;
-  const int s_hi = nsteps * (kslice + 1) / ks;
+  const int c_lo = nsteps * kzi / kz, c_hi = nsteps * (kzi + 1) / kz;  // this CTA's steps
+  const int s_lo = c_lo + (c_hi - c_lo) * kslice / ks;
+  const int s_hi = c_lo + (c_hi - c_lo) * (kslice + 1) / ks;
 
   // Feature rows g and g + 8 of the tile; rows past N_out read the last
   // row (a valid address) and are zeroed.
@@ -121,8 +127,7 @@ __global__ void __launch_bounds__(kStThreads,
     s_b[1] = load_scale(p.scale_b, p.scale_b_dtype, p.scale_b_pc ? fr1 : 0);
   }
 
-  for (int row0 = r_begin + static_cast<int>(blockIdx.z) * kNT; row0 < r_end;
-       row0 += static_cast<int>(gridDim.z) * kNT) {
+  for (int row0 = r_begin + zi * kNT; row0 < r_end; row0 += zc * kNT) {
     const int nrows = min(kNT, r_end - row0);
     // Token row g of each 8-row tile; rows past nrows read row0 and are zeroed.
     const __nv_bfloat16* x_rows[kNTiles];
@@ -294,7 +299,7 @@ __global__ void __launch_bounds__(kStThreads,
           atomicAdd(static_cast<float*>(p.out) + static_cast<int64_t>(p.row_token[row]) * p.ld_out + f,
                     y * p.row_weight[row]);
         } else if constexpr (kMode == EPI_PLAIN_F32) {
-          static_cast<float*>(p.out)[static_cast<int64_t>(row) * p.ld_out + f] = y;
+          static_cast<float*>(p.out)[kzi * p.split_stride + static_cast<int64_t>(row) * p.ld_out + f] = y;
         } else {
           static_cast<__nv_bfloat16*>(p.out)[static_cast<int64_t>(row) * p.ld_out + f] =
               __float2bfloat16_rn(y);
@@ -338,6 +343,40 @@ int launch_stream_mode(int nt, dim3 grid, const int8_t* wa, const int8_t* wb, co
 
 }  // namespace
 
+// Work split: ks warps per CTA and kz CTAs share a feature tile's K.  The
+// estimate per (ks, kz): CTAs over the resident CTA slots times (the steps
+// of a warp + kStCtaSteps of fixed cost: pipeline fill, setup), plus one
+// CTA's steps for the last wave; the cheapest with >= 2 steps per warp.
+StreamPlan stream_plan(int mode, int nt, bool grouped, bool active_list, int64_t groups,
+                       int64_t dense_rows, int64_t routed_rows, int64_t N_out, int64_t K, int kz_max) {
+  (void)active_list;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+  const int64_t zc = grouped ? 1 : std::max<int64_t>(1, (dense_rows + nt - 1) / nt);
+  const int64_t ftiles = (N_out + 15) / 16;
+  const int64_t nsteps = (K + kStStepK - 1) / kStStepK;
+  const int64_t active = grouped ? std::max<int64_t>(1, std::min<int64_t>(groups, routed_rows)) : 1;
+  const int64_t resident =
+      static_cast<int64_t>(num_sms(dev)) * (stream_smem_bytes(epi_is_pair(mode), nt) <= 113 * 1024 ? 2 : 1);
+  const int kz_cap = (mode == EPI_COMBINE_F32 || mode == EPI_PLAIN_F32) ? std::max(1, kz_max) : 1;
+  StreamPlan best_plan{1, 1};
+  double best = 1e300;
+  for (int kz = 1; kz <= kz_cap; kz *= 2) {
+    for (int k2 = 1; k2 <= kStWarps; k2 *= 2) {
+      if ((k2 > 1 || kz > 1) && nsteps / (k2 * kz) < 2) break;
+      const int64_t ctas = active * zc * kz * ((ftiles + (kStWarps / k2) - 1) / (kStWarps / k2));
+      const double steps = static_cast<double>(nsteps) / (k2 * kz);
+      const double cost =
+          static_cast<double>(ctas) / static_cast<double>(resident) * (steps + kStCtaSteps) + steps;
+      if (cost < best) {
+        best = cost;
+        best_plan = {k2, kz};
+      }
+    }
+  }
+  return best_plan;
+}
+
 int launch_gemm_stream(int mode, const int8_t* wa, const int8_t* wb, int64_t groups,
                        int64_t N_out, int64_t K, const void* x, int64_t ldx, int64_t routed_rows,
                        int nt, const StreamArgs& args_in, cudaStream_t stream) {
@@ -362,42 +401,25 @@ int launch_gemm_stream(int mode, const int8_t* wa, const int8_t* wb, int64_t gro
   a.N_out = static_cast<int>(N_out);
   if (a.group_offsets == nullptr && a.dense_rows <= 0) return KW8_OK;
 
+  const StreamPlan plan = stream_plan(mode, nt, a.group_offsets != nullptr, a.active_groups != nullptr,
+                                      groups, a.dense_rows, routed_rows, N_out, K, a.kz_max);
+  KW8_REQUIRE(plan.kz == 1 || mode == EPI_COMBINE_F32 || (mode == EPI_PLAIN_F32 && a.split_stride > 0),
+              KW8_ERR_INVALID_ARG, "a K split over CTAs needs fp32 partials");
+  a.ks = plan.ks;
+  a.kz = plan.kz;
   // Dense rows are split over grid z; a group's rows are looped over.
   const int64_t zc =
       a.group_offsets == nullptr ? std::min<int64_t>((a.dense_rows + nt - 1) / nt, 65535) : 1;
-  // K slices per feature tile: the fewest that give the GPU about two
-  // waves of warps (16 resident per SM), keeping >= 2 steps per slice.
-  int dev = 0;
-  KW8_CUDA_TRY(cudaGetDevice(&dev));
+  KW8_REQUIRE(zc * plan.kz <= 65535, KW8_ERR_UNSUPPORTED, "too many row passes");
   const int64_t ftiles = (N_out + 15) / 16;
-  const int64_t nsteps = (K + kStStepK - 1) / kStStepK;
-  const int64_t active =
-      a.group_offsets == nullptr ? 1 : std::max<int64_t>(1, std::min<int64_t>(groups, routed_rows));
-  // Estimated time per K split ks: CTAs over the resident slots, each CTA
-  // costing its steps plus a fixed ~3 steps of pipeline fill, and a last
-  // partial wave; the cheapest ks with >= 2 steps per slice wins.
-  const int64_t resident =
-      static_cast<int64_t>(num_sms(dev)) *
-      (stream_smem_bytes(pair, nt) <= 113 * 1024 ? 2 : 1);
-  int ks = 1;
-  double best = 1e300;
-  for (int k2 = 1; k2 <= kStWarps; k2 *= 2) {
-    if (k2 > 1 && nsteps / k2 < 2) break;
-    const int64_t ctas = active * zc * ((ftiles + (kStWarps / k2) - 1) / (kStWarps / k2));
-    const double steps = static_cast<double>(nsteps) / k2;
-    const double cost = static_cast<double>(ctas) / static_cast<double>(resident) * (steps + 3.0) + steps;
-    if (cost < best) {
-      best = cost;
-      ks = k2;
-    }
-  }
-  a.ks = ks;
-  const int64_t fblocks = (ftiles + (kStWarps / ks) - 1) / (kStWarps / ks);
+  const int64_t fblocks = (ftiles + (kStWarps / plan.ks) - 1) / (kStWarps / plan.ks);
   KW8_REQUIRE(fblocks < (1ll << 31), KW8_ERR_UNSUPPORTED, "too many feature blocks");
   // With an active-group list at most min(groups, routed rows) groups hold rows.
-  const int64_t grid_y = a.active_groups != nullptr ? active : groups;
+  const int64_t grid_y = a.active_groups != nullptr
+                             ? std::max<int64_t>(1, std::min<int64_t>(groups, routed_rows))
+                             : groups;
   const dim3 grid(static_cast<unsigned>(fblocks), static_cast<unsigned>(grid_y),
-                  static_cast<unsigned>(zc));
+                  static_cast<unsigned>(zc * plan.kz));
   switch (mode) {
     case EPI_PAIR_GELU:
       return launch_stream_mode<EPI_PAIR_GELU>(nt, grid, wa, wb, x, ldx, a, stream);

@@ -56,8 +56,25 @@ struct StreamArgs {
   // EPI_COMBINE_F32 only: token and routing weight of every sorted row.
   const int32_t* row_token;
   const float* row_weight;
-  int ks;  // warps splitting K (1, 2, 4 or 8), filled in by the launcher
+  // K split over CTAs: at most kz_max ranges (EPI_COMBINE_F32: any, its
+  // atomics add the ranges; EPI_PLAIN_F32: range r writes out + r *
+  // split_stride floats, the caller sums them; other modes: 1).
+  int kz_max;
+  int64_t split_stride;
+  // Filled in by the launcher (stream_plan).
+  int ks;  // warps of a CTA splitting its K range (1, 2, 4 or 8)
+  int kz;  // CTAs splitting K
 };
+
+// Work split of a launch: K ranges over kz CTAs and ks warps per CTA.
+struct StreamPlan {
+  int ks, kz;
+};
+
+// The split launch_gemm_stream uses for these arguments (callers size the
+// EPI_PLAIN_F32 partial buffer and decide on the reduction with it).
+StreamPlan stream_plan(int mode, int nt, bool grouped, bool active_list, int64_t groups,
+                       int64_t dense_rows, int64_t routed_rows, int64_t N_out, int64_t K, int kz_max);
 
 constexpr int kStreamMaxNT = 32;  // token rows per pass of a CTA over its weights
 
