@@ -14,8 +14,8 @@
 // group offsets, and token rows are read through an optional row index (the
 // permutation's token of each sorted row), so the gather of the routed rows
 // is fused into the operand load.  (Measured and dropped: bulk L2
-// prefetches of the weight rows, 128-k steps, token rows staged per CTA as
-// f16 with f16 weights; all slower.)
+// prefetches of the weight rows, 128-k steps, token rows staged once per
+// CTA in shared memory as bf16 or as f16 with f16 weights; all slower.)
 //
 // A warp owns 16 output features (16 gate + 16 up rows in paired mode) and
 // one slice of K; a CTA of 8 warps covers 8/ks feature tiles x ks K slices
