@@ -279,7 +279,16 @@ int kw8_ep_local_offsets(const int32_t* counts, int32_t world, int32_t rank,
  *   counts : int32 [2][world][E] (per-expert row counts of every rank, two
  *            copies alternating by call);
  *   flags  : uint32 [3][world], zero before the first call on any rank.
- * own_* are this rank's buffers again, as host-side values.               */
+ * own_* are this rank's buffers again, as host-side values.
+ *
+ * With rows != NULL, kw8_moe_ffn_ep sends every token once per rank that
+ * owns one of its experts instead of once per routed expert, and returns
+ * one partial sum per token and rank; it then uses, instead of recv / out:
+ *   rows : world * max_tokens rows of D bf16 (tokens sent to this rank);
+ *   meta : world * max_tokens * k int32 row indices, then as many fp32
+ *          routing weights (one record per routed pair);
+ *   ret  : [world][max_tokens] rows of D bf16 (partial sums coming back);
+ * and counts is int32 [2][world][E + world].                               */
 typedef struct kw8_ep_peers {
   int32_t world;
   int32_t rank;
@@ -292,6 +301,12 @@ typedef struct kw8_ep_peers {
   void* own_out;
   int32_t* own_counts;
   uint32_t* own_flags;
+  const uint64_t* rows;
+  const uint64_t* meta;
+  const uint64_t* ret;
+  void* own_rows;
+  void* own_meta;
+  void* own_ret;
 } kw8_ep_peers;
 
 /* The expert-parallel MoE layer over this rank's T <= max_tokens tokens in

@@ -71,6 +71,12 @@ class KW8EpPeers(ctypes.Structure):
         ("own_out", ctypes.c_void_p),
         ("own_counts", ctypes.c_void_p),
         ("own_flags", ctypes.c_void_p),
+        ("rows", ctypes.c_void_p),
+        ("meta", ctypes.c_void_p),
+        ("ret", ctypes.c_void_p),
+        ("own_rows", ctypes.c_void_p),
+        ("own_meta", ctypes.c_void_p),
+        ("own_ret", ctypes.c_void_p),
     ]
 
 

@@ -18,15 +18,16 @@ namespace {
 
 constexpr int kEpThreads = 256;
 
-// dest_base[e] = recv_pos(src, e, 0) on e's owner for this source `src`.
-__device__ void recv_bases(const int32_t* __restrict__ counts, int world, int E, int El, int src,
+// dest_base[e] = recv_pos(src, e, 0) on e's owner for this source `src`
+// (counts row s at counts + s * cstride).
+__device__ void recv_bases(const int32_t* __restrict__ counts, int cstride, int world, int E, int El, int src,
                            int* dest_base) {
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     const int r0 = (e / El) * El;
     int base = 0;
     for (int e2 = r0; e2 < e; ++e2)
-      for (int s = 0; s < world; ++s) base += counts[s * E + e2];
-    for (int s = 0; s < src; ++s) base += counts[s * E + e];
+      for (int s = 0; s < world; ++s) base += counts[s * cstride + e2];
+    for (int s = 0; s < src; ++s) base += counts[s * cstride + e];
     dest_base[e] = base;
   }
 }
@@ -51,7 +52,7 @@ __global__ void __launch_bounds__(kEpThreads)
   int* off = sh;            // [E+1] this rank's offsets
   int* dest = sh + E + 1;   // [E]
   for (int e = threadIdx.x; e <= E; e += blockDim.x) off[e] = offsets[e];
-  recv_bases(counts, world, E, El, rank, dest);
+  recv_bases(counts, E, world, E, El, rank, dest);
   __syncthreads();
   const int rows = off[E];
   const int lane = threadIdx.x & 31;
@@ -104,13 +105,13 @@ __global__ void __launch_bounds__(kEpThreads)
 }
 
 // Local experts' group offsets [El+1] of the receive layout.
-__global__ void ep_local_offsets_kernel(const int32_t* __restrict__ counts, int world, int rank, int E,
+__global__ void ep_local_offsets_kernel(const int32_t* __restrict__ counts, int cstride, int world, int rank,
                                         int El, int32_t* __restrict__ loc_off) {
   if (threadIdx.x == 0 && blockIdx.x == 0) {
     int acc = 0;
     loc_off[0] = 0;
     for (int j = 0; j < El; ++j) {
-      for (int s = 0; s < world; ++s) acc += counts[s * E + rank * El + j];
+      for (int s = 0; s < world; ++s) acc += counts[s * cstride + rank * El + j];
       loc_off[j + 1] = acc;
     }
   }
@@ -223,11 +224,11 @@ int launch_ep_return(const void* ys, int64_t max_rows, int64_t D, const int32_t*
 }
 
 int launch_ep_local_offsets(const int32_t* counts, int world, int rank, int64_t E, int32_t* loc_off,
-                            cudaStream_t stream) {
+                            cudaStream_t stream, int64_t cstride) {
   int rc = check_ep(8, world, rank, E);
   if (rc) return rc;
-  ep_local_offsets_kernel<<<1, 32, 0, stream>>>(counts, world, rank, static_cast<int>(E),
-                                                static_cast<int>(E / world), loc_off);
+  ep_local_offsets_kernel<<<1, 32, 0, stream>>>(counts, static_cast<int>(cstride > 0 ? cstride : E), world,
+                                                rank, static_cast<int>(E / world), loc_off);
   KW8_CHECK_LAUNCH();
   return KW8_OK;
 }

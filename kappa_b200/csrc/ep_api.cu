@@ -20,7 +20,12 @@ struct EpBuffers {
   int32_t* perm_hist;
   int32_t* loc_off;
   ExpertBuffers eb;
-  __nv_bfloat16* ys_loc;
+  __nv_bfloat16* ys_loc;  // expert outputs (or, deduplicated path, the gathered rows)
+  // Deduplicated path only.
+  float* sorted_w;
+  int32_t* tok_slot;  // [max_tokens][world]
+  int32_t* u_cnt;     // [world]
+  float* part;        // [world * max_tokens][D] fp32 partial sums
 };
 
 EpBuffers carve_ep(Carver& c, int64_t max_tokens, int64_t D, int64_t I, int64_t E, int k, int world) {
@@ -39,6 +44,10 @@ EpBuffers carve_ep(Carver& c, int64_t max_tokens, int64_t D, int64_t I, int64_t 
   b.loc_off = c.take<int32_t>(e_loc + 1);
   b.eb = carve_expert(c, recv_rows, I, e_loc);
   b.ys_loc = c.take<__nv_bfloat16>(recv_rows * D);
+  b.sorted_w = c.take<float>(m);
+  b.tok_slot = c.take<int32_t>(max_tokens * world);
+  b.u_cnt = c.take<int32_t>(kEpMaxRanks);
+  b.part = c.take<float>(static_cast<int64_t>(world) * max_tokens * D);
   return b;
 }
 
@@ -170,9 +179,46 @@ int kw8_moe_ffn_ep(const void* x, int64_t T, int64_t D, int64_t I, int64_t E, in
     rc = kw8::route(x, T, D, E, k, router, b.logits, b.idx, b.w, stream);
     if (rc) return rc;
   }
+  const bool dedup = peers->rows != nullptr;
   rc = launch_permute_multi(b.idx, T, k, E, capacity, b.perm_hist, b.sorted_token, b.inv_pos,
-                            b.group_sizes, b.group_offsets, stream, nullptr, nullptr);
+                            b.group_sizes, b.group_offsets, stream, dedup ? b.w : nullptr,
+                            dedup ? b.sorted_w : nullptr);
   if (rc) return rc;
+  if (dedup) {
+    // Each token once per owning rank (ep_dedup.cu).
+    KW8_REQUIRE(peers->meta && peers->ret && peers->own_rows && peers->own_meta && peers->own_ret &&
+                    D % 8 == 0,
+                KW8_ERR_INVALID_ARG, "incomplete peers for the deduplicated step");
+    const int64_t pair_cap = recv_rows;
+    rc = launch_ep_slots(b.idx, b.inv_pos, T, k, E, world, b.tok_slot, b.u_cnt, stream);
+    if (rc) return rc;
+    rc = launch_ep_counts2(b.group_sizes, b.u_cnt, E, peers->counts, peers->flags, peers->own_flags, world,
+                           rank, epoch, stream);
+    if (rc) return rc;
+    const int32_t* cnt = peers->own_counts + static_cast<int64_t>(epoch & 1u) * world * (E + world);
+    rc = launch_ep_dispatch2(x, T, k, D, b.sorted_token, b.group_offsets, b.sorted_w, b.tok_slot, cnt, world,
+                             rank, E, pair_cap, peers->rows, peers->meta, stream);
+    if (rc) return rc;
+    rc = launch_ep_barrier(peers->flags, peers->own_flags, world, rank, 1, epoch, true, stream);
+    if (rc) return rc;
+    rc = launch_ep_local_offsets(cnt, world, rank, E, b.loc_off, stream, E + world);
+    if (rc) return rc;
+    const int32_t* meta_u = static_cast<const int32_t*>(peers->own_meta);
+    const float* meta_w = reinterpret_cast<const float*>(meta_u + pair_cap);
+    rc = launch_ep_gather2(peers->own_rows, meta_u, b.loc_off, e_loc, cnt, world, rank, E, D, recv_rows,
+                           b.ys_loc, b.part, stream);
+    if (rc) return rc;
+    // The down projection adds w * y of every pair into its token's fp32
+    // partial row (rows indexed by the pair records).
+    rc = expert_ffn(use_stream(rows_hint(recv_rows, e_loc)), b.ys_loc, nullptr, recv_rows, D, I, e_loc,
+                    b.loc_off, gate_local, up_local, down_local, b.part, b.eb, stream, meta_u, meta_w);
+    if (rc) return rc;
+    rc = launch_ep_return2(b.part, D, cnt, world, rank, E, peers->max_tokens, peers->ret, stream);
+    if (rc) return rc;
+    rc = launch_ep_barrier(peers->flags, peers->own_flags, world, rank, 2, epoch, true, stream);
+    if (rc) return rc;
+    return launch_ep_final2(peers->own_ret, b.tok_slot, T, world, peers->max_tokens, D, out, stream);
+  }
   // Counts to every peer (phase 0), rows to their expert owners (phase 1).
   rc = launch_ep_counts(b.group_sizes, E, peers->counts, peers->flags, peers->own_flags, world, rank,
                         epoch, stream);

@@ -9,4 +9,5 @@
 #include "api.cu"
 #include "noalloc.cu"
 #include "ep.cu"
+#include "ep_dedup.cu"
 #include "ep_api.cu"

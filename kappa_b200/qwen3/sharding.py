@@ -241,7 +241,8 @@ class EPContext:
     arguments and calls :meth:`close` (also collective) when done.
     """
 
-    def __init__(self, *, max_tokens: int, d: int, k: int, hidden: int, num_experts: int, group=None):
+    def __init__(self, *, max_tokens: int, d: int, k: int, hidden: int, num_experts: int, group=None,
+                 dedup: bool = True):
         self.group = group
         self.world, self.rank = _world(group)
         if num_experts % self.world:
@@ -252,9 +253,14 @@ class EPContext:
         hsize = int(lib.kw8_ipc_handle_size())
         self.recv_rows = self.world * max_tokens * k
         self.out_rows = max_tokens * k
-        # Shared buffers (zero-filled): receive rows, return rows, per-expert
-        # counts [2][world][E] int32, phase flags [3][world] uint32.
-        sizes = (self.recv_rows * d * 2, self.out_rows * d * 2, 2 * self.world * num_experts * 4, 3 * self.world * 4)
+        # Shared buffers (zero-filled): receive rows, return rows, counts
+        # [2][world][E + world] int32, phase flags [3][world] uint32, and for
+        # the deduplicated step: token rows [world * max_tokens][d], pair
+        # records (int32 row + fp32 weight per received pair), partial sums
+        # [world][max_tokens][d].
+        pairs = self.world * max_tokens * k
+        sizes = (self.recv_rows * d * 2, self.out_rows * d * 2, 2 * self.world * (num_experts + self.world) * 4,
+                 3 * self.world * 4, self.world * max_tokens * d * 2, pairs * 8, self.world * max_tokens * d * 2)
         self._own = []
         handles = []
         for nbytes in sizes:
@@ -280,13 +286,18 @@ class EPContext:
         def as_i64(v):
             return [int(a) - (1 << 64) if int(a) >= (1 << 63) else int(a) for a in v]
 
-        self.peer_recv, self.peer_out, self.peer_counts, self.peer_flags = (
-            torch.tensor(as_i64(v), dtype=torch.int64, device=self.device) for v in peers)
-        self.recv_ptr, self.out_ptr, self.counts_ptr, self.flags_ptr = self._own
+        (self.peer_recv, self.peer_out, self.peer_counts, self.peer_flags, self.peer_rows, self.peer_meta,
+         self.peer_ret) = (torch.tensor(as_i64(v), dtype=torch.int64, device=self.device) for v in peers)
+        (self.recv_ptr, self.out_ptr, self.counts_ptr, self.flags_ptr, self.rows_ptr, self.meta_ptr,
+         self.ret_ptr) = self._own
+        self.dedup = dedup
         self.peers = _lib.KW8EpPeers(
             self.world, self.rank, max_tokens, self.peer_recv.data_ptr(), self.peer_out.data_ptr(),
             self.peer_counts.data_ptr(), self.peer_flags.data_ptr(), self.recv_ptr, self.out_ptr,
-            self.counts_ptr, self.flags_ptr)
+            self.counts_ptr, self.flags_ptr,
+            self.peer_rows.data_ptr() if dedup else None, self.peer_meta.data_ptr() if dedup else None,
+            self.peer_ret.data_ptr() if dedup else None, self.rows_ptr if dedup else None,
+            self.meta_ptr if dedup else None, self.ret_ptr if dedup else None)
         self.epoch = 0  # calls of the fused layer so far (the group's phase tag)
         self.ep_ws = torch.empty(
             int(lib.kw8_moe_ffn_ep_workspace_size(max_tokens, d, hidden, num_experts, k, self.world)),

@@ -62,6 +62,9 @@ def _rank_main(rank: int, world: int, port: int, errfile: str):
         y2 = S.moe_swiglu_ffn_ep(to_dev(x, dev), router, gl, ul, dl, cfg=cfg, ctx=ctx)  # one call, peer flags
         y3 = S.moe_swiglu_ffn_ep(to_dev(x, dev), router, gl, ul, dl, cfg=cfg, ctx=ctx)  # buffers reused
         y4 = S.moe_swiglu_ffn_ep(to_dev(x, dev), router, gl, ul, dl, cfg=cfg, ctx=ctx, staged=True)  # collectives
+        ctx_nd = S.EPContext(max_tokens=400, d=D, k=K, hidden=I, num_experts=E, dedup=False)
+        y7 = S.moe_swiglu_ffn_ep(to_dev(x, dev), router, gl, ul, dl, cfg=cfg, ctx=ctx_nd)  # a row per routed pair
+        ctx_nd.close()
         # a rank with fewer tokens than the others, then with none at all
         few = to_dev(x[:, : 37 + 100 * rank], dev)
         y5 = S.moe_swiglu_ffn_ep(few, router, gl, ul, dl, cfg=cfg, ctx=ctx)
@@ -76,13 +79,17 @@ def _rank_main(rank: int, world: int, port: int, errfile: str):
                                         idx=to_np(idx), w=to_np(w))
         parity(to_np(y), ref, tol=2e-2)
         parity(to_np(y2), ref, tol=2e-2)
-        assert torch.equal(y2, y3)
-        parity(to_np(y4), to_np(y2), tol=1e-2)
-        parity(to_np(y5), to_np(y2)[:, : 37 + 100 * rank], tol=1e-2)
+        parity(to_np(y7), ref, tol=2e-2)
+        # buffers reused: the same result up to the order of the fp32 atomic
+        # adds of the partial sums (then bf16), as in the single-GPU layer
+        d23 = (y2.float() - y3.float()).abs().max().item()
+        assert d23 <= 2 ** -7 * y2.float().abs().max().item(), d23
+        parity(to_np(y4), ref, tol=2e-2)
+        parity(to_np(y5), ref[:, : 37 + 100 * rank], tol=2e-2)
         if rank == 0:
             assert tuple(y6.shape) == (1, 0, D)
         else:
-            parity(to_np(y6), to_np(y2), tol=1e-2)
+            parity(to_np(y6), ref, tol=2e-2)
         # the single-GPU layer with every expert on the same tokens
         y1 = M.moe_swiglu_ffn(to_dev(x, dev), router, gate, up, down, cfg=cfg)
         parity(to_np(y2), to_np(y1), tol=2e-2)
