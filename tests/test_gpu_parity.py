@@ -419,6 +419,57 @@ def test_moe_errors_match_kappa():
                                                       moe_impl="fixed_capacity", moe_capacity_factor=0.0))
 
 
+def _ep_single_rank_peers(dev, Tm, D, E, k, dedup):
+    """A one-rank expert-parallel group: its own buffers are the peers'."""
+    world = 1
+    bufs = {
+        "recv": torch.zeros((world * Tm * k, D), dtype=torch.bfloat16, device=dev),
+        "out": torch.zeros((Tm * k, D), dtype=torch.bfloat16, device=dev),
+        "counts": torch.zeros(2 * world * (E + world), dtype=torch.int32, device=dev),
+        "flags": torch.zeros(3 * world, dtype=torch.int32, device=dev),
+        "rows": torch.zeros((world * Tm, D), dtype=torch.bfloat16, device=dev),
+        "meta": torch.zeros(2 * world * Tm * k, dtype=torch.int32, device=dev),
+        "ret": torch.zeros((world * Tm, D), dtype=torch.bfloat16, device=dev),
+    }
+    arr = {n: torch.tensor([t.data_ptr()], dtype=torch.int64, device=dev) for n, t in bufs.items()}
+    p = _lib.KW8EpPeers(
+        world, 0, Tm, arr["recv"].data_ptr(), arr["out"].data_ptr(), arr["counts"].data_ptr(),
+        arr["flags"].data_ptr(), bufs["recv"].data_ptr(), bufs["out"].data_ptr(), bufs["counts"].data_ptr(),
+        bufs["flags"].data_ptr(),
+        arr["rows"].data_ptr() if dedup else None, arr["meta"].data_ptr() if dedup else None,
+        arr["ret"].data_ptr() if dedup else None, bufs["rows"].data_ptr() if dedup else None,
+        bufs["meta"].data_ptr() if dedup else None, bufs["ret"].data_ptr() if dedup else None)
+    return p, (bufs, arr)
+
+
+@pytest.mark.parametrize("dedup", [True, False])
+def test_moe_ep_single_rank(dedup):
+    """kw8_moe_ffn_ep on a group of one rank: every step of the expert-parallel
+    call (counts exchange, row and record dispatch, phase flags, local
+    experts, return, combine) runs on one GPU against the fp32 reference, for
+    two calls in a row (epochs 1 and 2, both count copies)."""
+    import ctypes
+
+    from kappa_b200.qwen3.quant import kmajor
+
+    T, D, I, E, k = 200, 256, 128, 16, 4
+    x, g, o = _moe_case(T, D, I, E, k, True, seed=31)
+    dev = torch.device("cuda", 0)
+    peers, keep = _ep_single_rank_peers(dev, T, D, E, k, dedup)
+    lib = _lib.load()
+    ws = torch.empty(int(lib.kw8_moe_ffn_ep_workspace_size(T, D, I, E, k, 1)), dtype=torch.uint8, device=dev)
+    km = [kmajor(w, -2) for w in g]
+    xd = to_dev(x).reshape(T, D)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    for epoch in (1, 2):
+        out = torch.empty_like(xd)
+        _lib.check(lib.kw8_moe_ffn_ep(xd.data_ptr(), T, D, I, E, k, -1, *[w.struct() for w in km], out.data_ptr(),
+                                      ctypes.byref(peers), epoch, ws.data_ptr(), ws.numel(), stream))
+        assert _lib.device_status(out) == 0
+        _moe_check(x, g, o, E, k, out.reshape(1, T, D))
+    del keep
+
+
 def test_ep_barrier_wait_times_out():
     """Failure detection of the expert-parallel phase flags without a fault:
     a wait for a phase that no rank marks runs out after its bound (about
