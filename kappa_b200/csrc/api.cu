@@ -336,22 +336,29 @@ int stream_f32_kz(int64_t T, int64_t N_out, int64_t K) {
   return stream_plan(EPI_PLAIN_F32, nt, false, false, 1, T, T, N_out, K, kStreamMaxKz).kz;
 }
 
+// K split of the weight-streaming router: none up to 16 tokens, where the
+// reduction of the partials cost more than the split saved.
+int router_stream_kz(int64_t T, int64_t D, int64_t E) {
+  return T <= 16 ? 1 : stream_f32_kz(T, E, D);
+}
+
 int64_t router_part_floats(int64_t T, int64_t D, int64_t E) {
-  const int splits = router_streamed(T) ? stream_f32_kz(T, E, D) : dense_f32_splits(T, E, D);
+  const int splits = router_streamed(T) ? router_stream_kz(T, D, E) : dense_f32_splits(T, E, D);
   return splits > 1 ? splits * T * E : 0;
 }
 
 // Router logits + top-k.  `part` (router_part_floats(T, D, E) floats, or
 // nullptr) lets the tensor-core path split K over more SMs.
 int route(const void* x, int64_t T, int64_t D, int64_t E, int k, const kw8_weight& router,
-          float* logits, int32_t* idx, void* w, cudaStream_t stream, float* part = nullptr) {
+          float* logits, int32_t* idx, void* w, cudaStream_t stream, float* part = nullptr,
+          float* zero_rows = nullptr, int64_t zero_cols = 0) {
   int rc;
   if (router_streamed(T)) {
     StreamArgs r = stream_args(router, nullptr);
     r.dense_rows = static_cast<int>(T);
     r.out = logits;
     r.ld_out = E;
-    const int kz = part != nullptr ? stream_f32_kz(T, E, D) : 1;
+    const int kz = part != nullptr ? router_stream_kz(T, D, E) : 1;
     if (kz > 1) {
       r.out = part;
       r.kz_max = kStreamMaxKz;
@@ -376,7 +383,7 @@ int route(const void* x, int64_t T, int64_t D, int64_t E, int k, const kw8_weigh
     if (!rc && splits > 1) rc = launch_reduce_splits(part, splits, T * E, T * E, logits, false, stream);
   }
   if (rc) return rc;
-  return launch_topk(logits, T, E, k, idx, w, stream);
+  return launch_topk(logits, T, E, k, idx, w, stream, zero_rows, zero_cols);
 }
 
 // Down projection split over K (tensor-core path only): its fp32 partials.
@@ -629,8 +636,9 @@ int kw8_moe_ffn(const void* x, int64_t T, int64_t D, int64_t I, int64_t E, int32
   KW8_REQUIRE(workspace != nullptr && c.ok, KW8_ERR_WORKSPACE,
               "MoE workspace too small (%zu < %zu)", workspace_bytes, c.off);
   const int64_t m = T * k;
+  // The top-k kernel also zeroes the fp32 combine buffer (one row per token).
   rc = kw8::route(x, T, D, E, k, router, b.logits, b.idx, b.w, stream,
-                  router_part_floats(T, D, E) > 0 ? b.router_part : nullptr);
+                  router_part_floats(T, D, E) > 0 ? b.router_part : nullptr, b.acc, D);
   if (rc) return rc;
   rc = launch_permute_multi(b.idx, T, k, E, capacity, b.perm_hist, b.sorted_token, b.inv_pos,
                             b.group_sizes, b.group_offsets, stream, b.w, b.sorted_w, b.active);
@@ -643,9 +651,9 @@ int kw8_moe_ffn(const void* x, int64_t T, int64_t D, int64_t I, int64_t E, int32
     if (rc) return rc;
   }
   // The down projection adds w * y of every routed row straight into the
-  // fp32 token buffer (no bf16 rounding of the per-expert outputs, no
-  // [T*k][D] round trip); one conversion pass writes the bf16 output.
-  KW8_CUDA_TRY(cudaMemsetAsync(b.acc, 0, static_cast<size_t>(T * D) * sizeof(float), stream));
+  // fp32 token buffer (zeroed by the top-k kernel; no bf16 rounding of the
+  // per-expert outputs, no [T*k][D] round trip); one conversion pass writes
+  // the bf16 output.
   ExpertBuffers eb{b.tiles, b.num_tiles, b.h};
   rc = expert_ffn(streamed, streamed ? x : b.xs, streamed ? b.sorted_token : nullptr, m, D, I, E,
                   b.group_offsets, gate, up, down, b.acc, eb, stream, b.sorted_token, b.sorted_w,

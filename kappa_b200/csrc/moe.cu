@@ -51,10 +51,16 @@ constexpr int kMaxPerLane = 8;
 
 __global__ void topk_softmax_kernel(const float* __restrict__ logits, int T, int E, int k,
                                     int32_t* __restrict__ idx_out,
-                                    __nv_bfloat16* __restrict__ w_out) {
+                                    __nv_bfloat16* __restrict__ w_out, float4* __restrict__ zero_rows,
+                                    int zero_vec4) {
   const int lane = threadIdx.x & 31;
   const int tok = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (tok >= T) return;
+  // Optional: this token's row of a buffer the caller needs zeroed (the
+  // fp32 combine buffer the down projection adds into).
+  if (zero_rows != nullptr)
+    for (int c = lane; c < zero_vec4; c += 32)
+      zero_rows[static_cast<int64_t>(tok) * zero_vec4 + c] = make_float4(0.f, 0.f, 0.f, 0.f);
   const float* row = logits + static_cast<int64_t>(tok) * E;
   float v[kMaxPerLane];
   bool taken[kMaxPerLane];
@@ -454,7 +460,10 @@ int grid_for(int64_t n, int threads, int cap) {
 }  // namespace
 
 int launch_topk(const float* logits, int64_t T, int64_t E, int k, int32_t* idx, void* w,
-                cudaStream_t stream) {
+                cudaStream_t stream, float* zero_rows, int64_t zero_cols) {
+  KW8_REQUIRE(zero_rows == nullptr ||
+                  (zero_cols % 4 == 0 && (reinterpret_cast<uintptr_t>(zero_rows) & 15) == 0),
+              KW8_ERR_UNSUPPORTED, "rows to zero need 4-float alignment");
   KW8_REQUIRE(E >= 1 && E <= 32 * kMaxPerLane, KW8_ERR_UNSUPPORTED,
               "top-k supports 1..%d experts (got %lld)", 32 * kMaxPerLane, (long long)E);
   KW8_REQUIRE(k >= 1 && k <= 32 && k <= E, KW8_ERR_INVALID_ARG, "k=%d invalid for E=%lld", k,
@@ -464,7 +473,8 @@ int launch_topk(const float* logits, int64_t T, int64_t E, int k, int32_t* idx, 
   const int64_t blocks = (T + warps - 1) / warps;
   KW8_REQUIRE(blocks < (1ll << 31), KW8_ERR_UNSUPPORTED, "too many tokens");
   topk_softmax_kernel<<<static_cast<unsigned>(blocks), warps * 32, 0, stream>>>(
-      logits, static_cast<int>(T), static_cast<int>(E), k, idx, static_cast<__nv_bfloat16*>(w));
+      logits, static_cast<int>(T), static_cast<int>(E), k, idx, static_cast<__nv_bfloat16*>(w),
+      reinterpret_cast<float4*>(zero_rows), static_cast<int>(zero_cols / 4));
   KW8_CHECK_LAUNCH();
   return KW8_OK;
 }

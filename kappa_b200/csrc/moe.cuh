@@ -5,8 +5,9 @@
 
 namespace kw8 {
 
+// With zero_rows: also zeroes zero_rows[T][zero_cols] (fp32, zero_cols % 4 == 0).
 int launch_topk(const float* logits, int64_t T, int64_t E, int k, int32_t* idx, void* w,
-                cudaStream_t stream);
+                cudaStream_t stream, float* zero_rows = nullptr, int64_t zero_cols = 0);
 // `w` / `sorted_w` (both optional): routing weights [T*k] bf16 and their
 // fp32 copies in sorted-row order, for the fused down-projection combine.
 int launch_permute(const int32_t* idx, int64_t T, int k, int64_t E, int64_t capacity,
