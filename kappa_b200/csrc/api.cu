@@ -347,11 +347,10 @@ int64_t router_part_floats(int64_t T, int64_t D, int64_t E) {
   return splits > 1 ? splits * T * E : 0;
 }
 
-// Router logits + top-k.  `part` (router_part_floats(T, D, E) floats, or
-// nullptr) lets the tensor-core path split K over more SMs.
-int route(const void* x, int64_t T, int64_t D, int64_t E, int k, const kw8_weight& router,
-          float* logits, int32_t* idx, void* w, cudaStream_t stream, float* part = nullptr,
-          float* zero_rows = nullptr, int64_t zero_cols = 0) {
+// Router logits [T][E] fp32.  `part` (router_part_floats(T, D, E) floats,
+// or nullptr) lets the GEMM split K over more SMs.
+int router_logits(const void* x, int64_t T, int64_t D, int64_t E, const kw8_weight& router,
+                  float* logits, cudaStream_t stream, float* part = nullptr) {
   int rc;
   if (router_streamed(T)) {
     StreamArgs r = stream_args(router, nullptr);
@@ -382,6 +381,14 @@ int route(const void* x, int64_t T, int64_t D, int64_t E, int k, const kw8_weigh
     rc = run_gemm(EPI_PLAIN_F32, router, nullptr, 1, E, D, x, T, D, r, stream);
     if (!rc && splits > 1) rc = launch_reduce_splits(part, splits, T * E, T * E, logits, false, stream);
   }
+  return rc;
+}
+
+// Router logits + top-k (zero_rows: see launch_topk).
+int route(const void* x, int64_t T, int64_t D, int64_t E, int k, const kw8_weight& router,
+          float* logits, int32_t* idx, void* w, cudaStream_t stream, float* part = nullptr,
+          float* zero_rows = nullptr, int64_t zero_cols = 0) {
+  const int rc = router_logits(x, T, D, E, router, logits, stream, part);
   if (rc) return rc;
   return launch_topk(logits, T, E, k, idx, w, stream, zero_rows, zero_cols);
 }
@@ -637,11 +644,19 @@ int kw8_moe_ffn(const void* x, int64_t T, int64_t D, int64_t I, int64_t E, int32
               "MoE workspace too small (%zu < %zu)", workspace_bytes, c.off);
   const int64_t m = T * k;
   // The top-k kernel also zeroes the fp32 combine buffer (one row per token).
-  rc = kw8::route(x, T, D, E, k, router, b.logits, b.idx, b.w, stream,
-                  router_part_floats(T, D, E) > 0 ? b.router_part : nullptr, b.acc, D);
-  if (rc) return rc;
-  rc = launch_permute_multi(b.idx, T, k, E, capacity, b.perm_hist, b.sorted_token, b.inv_pos,
-                            b.group_sizes, b.group_offsets, stream, b.w, b.sorted_w, b.active);
+  float* part = router_part_floats(T, D, E) > 0 ? b.router_part : nullptr;
+  if (route_tail_small_ok(T, E, k)) {  // decode: top-k, permutation and zeroing in one launch
+    rc = router_logits(x, T, D, E, router, b.logits, stream, part);
+    if (!rc)
+      rc = launch_route_tail_small(b.logits, T, E, k, capacity, b.idx, b.w, b.sorted_token,
+                                   b.inv_pos, b.group_sizes, b.group_offsets, b.sorted_w,
+                                   b.active, b.acc, D, stream);
+  } else {
+    rc = kw8::route(x, T, D, E, k, router, b.logits, b.idx, b.w, stream, part, b.acc, D);
+    if (!rc)
+      rc = launch_permute_multi(b.idx, T, k, E, capacity, b.perm_hist, b.sorted_token, b.inv_pos,
+                                b.group_sizes, b.group_offsets, stream, b.w, b.sorted_w, b.active);
+  }
   if (rc) return rc;
   // Few rows per expert: the weight-streaming kernels read x rows through
   // the permutation (no gathered copy); otherwise gather for the TMA loads.

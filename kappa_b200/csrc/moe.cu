@@ -49,19 +49,10 @@ __device__ int block_exclusive_scan(int v, int* total) {
 // the k winners is fp32 exp(v - max) / sum, rounded to bf16.
 constexpr int kMaxPerLane = 8;
 
-__global__ void topk_softmax_kernel(const float* __restrict__ logits, int T, int E, int k,
-                                    int32_t* __restrict__ idx_out,
-                                    __nv_bfloat16* __restrict__ w_out, float4* __restrict__ zero_rows,
-                                    int zero_vec4) {
-  const int lane = threadIdx.x & 31;
-  const int tok = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (tok >= T) return;
-  // Optional: this token's row of a buffer the caller needs zeroed (the
-  // fp32 combine buffer the down projection adds into).
-  if (zero_rows != nullptr)
-    for (int c = lane; c < zero_vec4; c += 32)
-      zero_rows[static_cast<int64_t>(tok) * zero_vec4 + c] = make_float4(0.f, 0.f, 0.f, 0.f);
-  const float* row = logits + static_cast<int64_t>(tok) * E;
+// Top-k + softmax of one logit row by one warp: lane j < k receives the
+// j-th winner and its bf16 weight.
+__device__ __forceinline__ void topk_row(const float* __restrict__ row, int E, int k, int lane,
+                                         int* my_idx, __nv_bfloat16* my_w) {
   float v[kMaxPerLane];
   bool taken[kMaxPerLane];
 #pragma unroll
@@ -105,9 +96,101 @@ __global__ void topk_softmax_kernel(const float* __restrict__ logits, int T, int
   float s = ex;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  *my_idx = my_i;
+  *my_w = __float2bfloat16_rn(__fdiv_rn(ex, s));
+}
+
+__global__ void topk_softmax_kernel(const float* __restrict__ logits, int T, int E, int k,
+                                    int32_t* __restrict__ idx_out,
+                                    __nv_bfloat16* __restrict__ w_out, float4* __restrict__ zero_rows,
+                                    int zero_vec4) {
+  const int lane = threadIdx.x & 31;
+  const int tok = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (tok >= T) return;
+  // Optional: this token's row of a buffer the caller needs zeroed (the
+  // fp32 combine buffer the down projection adds into).
+  if (zero_rows != nullptr)
+    for (int c = lane; c < zero_vec4; c += 32)
+      zero_rows[static_cast<int64_t>(tok) * zero_vec4 + c] = make_float4(0.f, 0.f, 0.f, 0.f);
+  int my_i;
+  __nv_bfloat16 my_w;
+  topk_row(logits + static_cast<int64_t>(tok) * E, E, k, lane, &my_i, &my_w);
   if (lane < k) {
     idx_out[static_cast<int64_t>(tok) * k + lane] = my_i;
-    w_out[static_cast<int64_t>(tok) * k + lane] = __float2bfloat16_rn(__fdiv_rn(ex, s));
+    w_out[static_cast<int64_t>(tok) * k + lane] = my_w;
+  }
+}
+
+// ------------------------------------------------ small routing tail ----
+// Everything between the router logits and the expert GEMMs for a handful
+// of tokens, in one CTA of kTailThreads: top-k + softmax of every token (one
+// warp per token, topk_row as above), then the same stable permutation as
+// permute_kernel (entries sorted by expert, ties by flat index, at most
+// `capacity` rows per expert), the active-expert list, and the zeroing of
+// the fp32 combine buffer.  The rank of entry i among its expert's entries
+// is the count of equal experts before it, read from shared memory (m <=
+// kTailMaxRows entries, so the quadratic count is a few hundred steps).
+constexpr int kTailThreads = 256;
+
+__global__ void __launch_bounds__(kTailThreads)
+    route_tail_small_kernel(const float* __restrict__ logits, int T, int E, int k, int capacity,
+                            int32_t* __restrict__ idx_out, __nv_bfloat16* __restrict__ w_out,
+                            int32_t* __restrict__ sorted_token, int32_t* __restrict__ inv_pos,
+                            int32_t* __restrict__ group_sizes, int32_t* __restrict__ group_offsets,
+                            float* __restrict__ sorted_w, int32_t* __restrict__ active,
+                            float4* __restrict__ zero_rows, int zero_vec4) {
+  __shared__ int ent_e[kTailMaxRows];    // expert of flat entry i = t * k + j
+  __shared__ float ent_w[kTailMaxRows];  // its weight, bf16 value in fp32
+  __shared__ int cnt[kTailThreads];      // entries per expert (E <= kTailThreads)
+  __shared__ int goff[kTailThreads];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int m = T * k;
+  cnt[threadIdx.x] = 0;
+  if (zero_rows != nullptr)
+    for (int c = threadIdx.x; c < T * zero_vec4; c += kTailThreads)
+      zero_rows[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int tok = warp; tok < T; tok += kTailThreads / 32) {
+    int my_i;
+    __nv_bfloat16 my_w;
+    topk_row(logits + static_cast<int64_t>(tok) * E, E, k, lane, &my_i, &my_w);
+    if (lane < k) {
+      idx_out[tok * k + lane] = my_i;
+      w_out[tok * k + lane] = my_w;
+      ent_e[tok * k + lane] = my_i;
+      ent_w[tok * k + lane] = __bfloat162float(my_w);
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < m; i += kTailThreads) atomicAdd(&cnt[ent_e[i]], 1);
+  __syncthreads();
+  const int e = threadIdx.x;
+  const int kept = e < E ? (capacity >= 0 ? min(cnt[e], capacity) : cnt[e]) : 0;
+  int total, n_active;
+  const int off = block_exclusive_scan(kept, &total);
+  const int apos = block_exclusive_scan(kept > 0 ? 1 : 0, &n_active);
+  if (e < E) {
+    group_sizes[e] = kept;
+    group_offsets[e] = off;
+    goff[e] = off;
+    if (kept > 0) active[1 + apos] = e;
+  }
+  if (threadIdx.x == 0) {
+    group_offsets[E] = total;
+    active[0] = n_active;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < m; i += kTailThreads) {
+    const int ei = ent_e[i];
+    int rank = 0;
+    for (int j = 0; j < i; ++j) rank += (ent_e[j] == ei) ? 1 : 0;
+    if (capacity < 0 || rank < capacity) {
+      const int p = goff[ei] + rank;
+      sorted_token[p] = i / k;
+      inv_pos[i] = p;
+      sorted_w[p] = ent_w[i];
+    } else {
+      inv_pos[i] = -1;
+    }
   }
 }
 
@@ -475,6 +558,27 @@ int launch_topk(const float* logits, int64_t T, int64_t E, int k, int32_t* idx, 
   topk_softmax_kernel<<<static_cast<unsigned>(blocks), warps * 32, 0, stream>>>(
       logits, static_cast<int>(T), static_cast<int>(E), k, idx, static_cast<__nv_bfloat16*>(w),
       reinterpret_cast<float4*>(zero_rows), static_cast<int>(zero_cols / 4));
+  KW8_CHECK_LAUNCH();
+  return KW8_OK;
+}
+
+int launch_route_tail_small(const float* logits, int64_t T, int64_t E, int k, int64_t capacity,
+                            int32_t* idx, void* w, int32_t* sorted_token, int32_t* inv_pos,
+                            int32_t* group_sizes, int32_t* group_offsets, float* sorted_w,
+                            int32_t* active, float* zero_rows, int64_t zero_cols,
+                            cudaStream_t stream) {
+  KW8_REQUIRE(route_tail_small_ok(T, E, k), KW8_ERR_UNSUPPORTED,
+              "small routing tail: T*k <= %d and E <= %d (got T=%lld E=%lld k=%d)", kTailMaxRows,
+              kTailThreads, (long long)T, (long long)E, k);
+  KW8_REQUIRE(w && sorted_w && active, KW8_ERR_INVALID_ARG, "null routing output");
+  KW8_REQUIRE(zero_rows == nullptr ||
+                  (zero_cols % 4 == 0 && (reinterpret_cast<uintptr_t>(zero_rows) & 15) == 0),
+              KW8_ERR_UNSUPPORTED, "rows to zero need 4-float alignment");
+  const int cap = capacity < 0 ? -1 : static_cast<int>(std::min<int64_t>(capacity, 1ll << 30));
+  route_tail_small_kernel<<<1, kTailThreads, 0, stream>>>(
+      logits, static_cast<int>(T), static_cast<int>(E), k, cap, idx,
+      static_cast<__nv_bfloat16*>(w), sorted_token, inv_pos, group_sizes, group_offsets, sorted_w,
+      active, reinterpret_cast<float4*>(zero_rows), static_cast<int>(zero_cols / 4));
   KW8_CHECK_LAUNCH();
   return KW8_OK;
 }

@@ -8,6 +8,18 @@ namespace kw8 {
 // With zero_rows: also zeroes zero_rows[T][zero_cols] (fp32, zero_cols % 4 == 0).
 int launch_topk(const float* logits, int64_t T, int64_t E, int k, int32_t* idx, void* w,
                 cudaStream_t stream, float* zero_rows = nullptr, int64_t zero_cols = 0);
+// Top-k + softmax, stable permutation (as launch_permute_multi, with the
+// active-expert list) and the zeroing of zero_rows[T][zero_cols] in one
+// launch, for route_tail_small_ok shapes (decode batches).
+constexpr int kTailMaxRows = 256;
+inline bool route_tail_small_ok(int64_t T, int64_t E, int k) {
+  return T >= 1 && k >= 1 && k <= 32 && k <= E && E <= 256 && T * k <= kTailMaxRows;
+}
+int launch_route_tail_small(const float* logits, int64_t T, int64_t E, int k, int64_t capacity,
+                            int32_t* idx, void* w, int32_t* sorted_token, int32_t* inv_pos,
+                            int32_t* group_sizes, int32_t* group_offsets, float* sorted_w,
+                            int32_t* active, float* zero_rows, int64_t zero_cols,
+                            cudaStream_t stream);
 // `w` / `sorted_w` (both optional): routing weights [T*k] bf16 and their
 // fp32 copies in sorted-row order, for the fused down-projection combine.
 int launch_permute(const int32_t* idx, int64_t T, int k, int64_t E, int64_t capacity,

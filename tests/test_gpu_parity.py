@@ -349,8 +349,9 @@ def test_moe_staged_entry_points(path):
     parity(y_staged, ref.reshape(T, D), tol=2e-2)
 
 
-def test_moe_fixed_capacity_vs_oracle():
-    T, D, I, E, k = 256, 256, 128, 8, 2
+@pytest.mark.parametrize("T", [256, 24])  # 24 x 2 rows: the one-launch decode routing, 4 of 6 kept
+def test_moe_fixed_capacity_vs_oracle(T):
+    D, I, E, k = 256, 128, 8, 2
     x, g, o = _moe_case(T, D, I, E, k, True, seed=77)
     cfg = MoEConfig(use_moe=True, num_experts=E, num_experts_per_tok=k, moe_impl="fixed_capacity",
                     moe_capacity_factor=0.75, moe_fixed_capacity_slots=1024)

@@ -1,6 +1,7 @@
-"""Multi-GPU paths on B200s (NCCL, 2 ranks): expert-parallel MoE (prefill and
-decode) and tensor-parallel dense MLPs, each checked against the fp32
-dequantise-then-dot reference.  Skipped with fewer than two GPUs."""
+"""Multi-GPU paths on B200s (NCCL; 2 ranks, or KW8_TEST_WORLD ranks):
+expert-parallel MoE (prefill and decode) and tensor-parallel dense MLPs, each
+checked against the fp32 dequantise-then-dot reference.  Skipped with fewer
+GPUs than ranks."""
 
 from __future__ import annotations
 
@@ -19,7 +20,7 @@ import oracle as O
 from helpers import moe_weights, normal, parity, to_dev, to_np
 
 pytestmark = pytest.mark.gpu
-WORLD = 2
+WORLD = int(os.environ.get("KW8_TEST_WORLD", "2"))  # 2, 4 or 8 (16 experts split evenly)
 
 
 def _gpu_q(w, in_axis=-2):
@@ -58,11 +59,12 @@ def _rank_main(rank: int, world: int, port: int, errfile: str):
         cfg = MoEConfig(use_moe=True, num_experts=E, num_experts_per_tok=K, moe_impl="ragged_jax")
         x = normal(np.random.default_rng(100 + rank), (1, 300 + 50 * rank, D)).astype(O.BF16)
         y = S.moe_swiglu_ffn_ep(to_dev(x, dev), router, gl, ul, dl, cfg=cfg)  # NCCL all-to-allv
-        ctx = S.EPContext(max_tokens=400, d=D, k=K, hidden=I, num_experts=E)
+        max_tok = 300 + 50 * world  # the largest rank's token count, rounded up
+        ctx = S.EPContext(max_tokens=max_tok, d=D, k=K, hidden=I, num_experts=E)
         y2 = S.moe_swiglu_ffn_ep(to_dev(x, dev), router, gl, ul, dl, cfg=cfg, ctx=ctx)  # one call, peer flags
         y3 = S.moe_swiglu_ffn_ep(to_dev(x, dev), router, gl, ul, dl, cfg=cfg, ctx=ctx)  # buffers reused
         y4 = S.moe_swiglu_ffn_ep(to_dev(x, dev), router, gl, ul, dl, cfg=cfg, ctx=ctx, staged=True)  # collectives
-        ctx_nd = S.EPContext(max_tokens=400, d=D, k=K, hidden=I, num_experts=E, dedup=False)
+        ctx_nd = S.EPContext(max_tokens=max_tok, d=D, k=K, hidden=I, num_experts=E, dedup=False)
         y7 = S.moe_swiglu_ffn_ep(to_dev(x, dev), router, gl, ul, dl, cfg=cfg, ctx=ctx_nd)  # a row per routed pair
         ctx_nd.close()
         # a rank with fewer tokens than the others, then with none at all
@@ -133,7 +135,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < WORLD, reason=f"needs {WORLD} GPUs")
 def test_ep_tp_two_gpus():
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     with tempfile.NamedTemporaryFile("w+", suffix=".log", delete=False) as f:
