@@ -342,8 +342,10 @@ int router_stream_kz(int64_t T, int64_t D, int64_t E) {
   return T <= 16 ? 1 : stream_f32_kz(T, E, D);
 }
 
+// Sized for the larger split of the two paths, so that a workspace sized
+// under one GEMM-path option also serves the other.
 int64_t router_part_floats(int64_t T, int64_t D, int64_t E) {
-  const int splits = router_streamed(T) ? router_stream_kz(T, D, E) : dense_f32_splits(T, E, D);
+  const int splits = std::max(router_stream_kz(T, D, E), dense_f32_splits(T, E, D));
   return splits > 1 ? splits * T * E : 0;
 }
 
@@ -393,11 +395,17 @@ int route(const void* x, int64_t T, int64_t D, int64_t E, int k, const kw8_weigh
   return launch_topk(logits, T, E, k, idx, w, stream, zero_rows, zero_cols);
 }
 
-// Down projection split over K (tensor-core path only): its fp32 partials.
+// K split of the dense down projection on the path the option selects (1:
+// none), and its fp32 partials sized for the larger split of the two paths
+// (a workspace sized under one option also serves the other).
+int dense_down_splits(int64_t T, int64_t D, int64_t H) {
+  if (T <= 0) return 1;
+  return use_stream(static_cast<double>(T)) ? stream_f32_kz(T, D, H) : dense_f32_splits(T, D, H);
+}
+
 int64_t dense_down_part_floats(int64_t T, int64_t D, int64_t H) {
   if (T <= 0) return 0;
-  const int splits =
-      use_stream(static_cast<double>(T)) ? stream_f32_kz(T, D, H) : dense_f32_splits(T, D, H);
+  const int splits = std::max(stream_f32_kz(T, D, H), dense_f32_splits(T, D, H));
   return splits > 1 ? splits * T * D : 0;
 }
 
@@ -481,8 +489,8 @@ int kw8_dense_ffn(const void* x, int64_t T, int64_t D, int64_t H, kw8_weight gat
   KW8_REQUIRE(T < (1ll << 31), KW8_ERR_UNSUPPORTED, "too many tokens");
   Carver c(workspace, workspace_bytes);
   __nv_bfloat16* h = c.take<__nv_bfloat16>(T * H);
-  const int64_t part_floats = dense_down_part_floats(T, D, H);
-  float* part = c.take<float>(part_floats);
+  float* part = c.take<float>(dense_down_part_floats(T, D, H));
+  const int splits = dense_down_splits(T, D, H);
   KW8_REQUIRE(workspace != nullptr && c.ok, KW8_ERR_WORKSPACE, "dense FFN workspace too small");
   const int epi_pair = act == KW8_ACT_GELU_TANH ? EPI_PAIR_GELU : EPI_PAIR_SILU;
   const int epi_out = out_dtype == KW8_DT_F32 ? EPI_PLAIN_F32 : EPI_PLAIN_BF16;
@@ -498,10 +506,10 @@ int kw8_dense_ffn(const void* x, int64_t T, int64_t D, int64_t H, kw8_weight gat
     d.dense_rows = static_cast<int>(T);
     d.out = out;
     d.ld_out = D;
-    if (part_floats > 0) {
+    if (splits > 1) {
       // Few rows and long K: the CTAs split K into fp32 partials, summed in
       // order into the output.
-      const int kz = static_cast<int>(part_floats / (T * D));
+      const int kz = splits;
       d.out = part;
       d.kz_max = kStreamMaxKz;
       d.split_stride = T * D;
@@ -523,11 +531,11 @@ int kw8_dense_ffn(const void* x, int64_t T, int64_t D, int64_t H, kw8_weight gat
   d.nt = pick_nt_dense(T, (D + 127) / 128);
   d.out = out;
   d.ld_out = D;
-  if (part_floats > 0) {
+  if (splits > 1) {
     // Few output tiles: split K over more SMs into fp32 partials, then sum
     // them in order into the output.
     d.out = part;
-    d.k_splits = static_cast<int>(part_floats / (T * D));
+    d.k_splits = splits;
     d.split_stride = T * D;
     rc = run_gemm(EPI_PLAIN_F32, down, nullptr, 1, D, H, h, T, H, d, stream);
     if (rc) return rc;

@@ -37,6 +37,20 @@ def test_cpu_only_queries():
     assert lib.kw8_quantize_workspace_size(128, 768) >= 128 * 768 * 4
 
 
+def test_workspace_sizes_do_not_depend_on_the_path_option():
+    """A workspace sized under one OPT_GEMM_PATH value serves the others."""
+    lib = L.load()
+    sizes = []
+    try:
+        for opt in (0, 1, 2):
+            L.set_option(L.OPT_GEMM_PATH, opt)
+            sizes.append(([lib.kw8_moe_ffn_workspace_size(T, 2048, 768, 128, 8) for T in (1, 16, 64, 256, 4096)],
+                          [lib.kw8_dense_ffn_workspace_size(T, 2560, 10240) for T in (1, 16, 64, 256)]))
+    finally:
+        L.set_option(L.OPT_GEMM_PATH, 0)
+    assert sizes[0] == sizes[1] == sizes[2]
+
+
 def test_invalid_arguments_fail_before_any_launch():
     lib = L.load()
     w = L.KW8Weight(None, None, 0, 0)
