@@ -156,12 +156,17 @@ __global__ void __launch_bounds__(kTailThreads)
     if (lane < k) {
       idx_out[tok * k + lane] = my_i;
       w_out[tok * k + lane] = my_w;
-      ent_e[tok * k + lane] = my_i;
+      // A row without k ordered logits (NaN, or -inf everywhere) yields no
+      // expert: reported like an invalid id in the permutation, and dropped.
+      const bool valid = my_i >= 0 && my_i < E;
+      if (!valid) report(KW8_ERR_INVALID_ARG);
+      ent_e[tok * k + lane] = valid ? my_i : -1;
       ent_w[tok * k + lane] = __bfloat162float(my_w);
     }
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < m; i += kTailThreads) atomicAdd(&cnt[ent_e[i]], 1);
+  for (int i = threadIdx.x; i < m; i += kTailThreads)
+    if (ent_e[i] >= 0) atomicAdd(&cnt[ent_e[i]], 1);
   __syncthreads();
   const int e = threadIdx.x;
   const int kept = e < E ? (capacity >= 0 ? min(cnt[e], capacity) : cnt[e]) : 0;
@@ -181,6 +186,10 @@ __global__ void __launch_bounds__(kTailThreads)
   __syncthreads();
   for (int i = threadIdx.x; i < m; i += kTailThreads) {
     const int ei = ent_e[i];
+    if (ei < 0) {
+      inv_pos[i] = -1;
+      continue;
+    }
     int rank = 0;
     for (int j = 0; j < i; ++j) rank += (ent_e[j] == ei) ? 1 : 0;
     if (capacity < 0 || rank < capacity) {
