@@ -406,6 +406,26 @@ def test_moe_qwen3_30b_a3b_decode_vs_oracle(B):
     _moe_check(x, g, o, E, k, y)
 
 
+@pytest.mark.parametrize("T", [5, 300])  # 5 x 4 rows: the one-launch decode routing; 300: the multi-block sort
+def test_moe_nan_token_is_reported_and_dropped(T):
+    """A token whose router logits are NaN has no top-k order: its expert ids
+    are invalid, the device status says KW8_ERR_INVALID_ARG, its output row is
+    zero, and every other token gets the result it gets without it."""
+    D, I, E, k = 256, 128, 16, 4
+    x, g, _ = _moe_case(T, D, I, E, k, True, seed=91)
+    cfg = MoEConfig(use_moe=True, num_experts=E, num_experts_per_tok=k, moe_impl="ragged_jax",
+                    moe_ragged_decode_token_threshold=0)
+    xd = to_dev(x)
+    xd[0, 0] = float("nan")
+    assert _lib.device_status(xd) == 0
+    y = M.moe_swiglu_ffn(xd, *g, cfg=cfg).float()
+    assert _lib.device_status(xd) == _lib.KW8_ERR_INVALID_ARG
+    assert float(y[0, 0].abs().max()) == 0.0
+    rest = M.moe_swiglu_ffn(xd[:, 1:].contiguous(), *g, cfg=cfg).float()
+    assert _lib.device_status(xd) == 0
+    assert float((y[0, 1:] - rest[0]).abs().max()) <= 2 ** -7 * float(rest.abs().max())
+
+
 def test_moe_errors_match_kappa():
     T, D, I, E, k = 8, 64, 32, 4, 2
     x, g, _ = _moe_case(T, D, I, E, k)
