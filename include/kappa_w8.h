@@ -75,7 +75,9 @@ int32_t kw8_abi_version(void);
 
 /* Reads and clears the device-side status word that kernels set when a
  * bounded wait runs out (KW8_ERR_DEVICE_TIMEOUT) or a kernel-side check
- * fails.  Synchronises `stream`.  *status_out receives 0 or a kw8_status.   */
+ * fails (KW8_ERR_INVALID_ARG: an expert id out of range, e.g. a token whose
+ * router logits are NaN; its routed entries are dropped and its output row
+ * is zero).  Synchronises `stream`.  *status_out receives 0 or a kw8_status. */
 int kw8_device_status(int32_t* status_out, kw8_stream_t stream);
 
 /* Tuning and testing knobs, process wide; no kappa counterpart (kappa
