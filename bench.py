@@ -155,51 +155,96 @@ def _cores() -> int:
     return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
 
 
-def cpu_reference_sample(tokens: int, reps: int):
-    """Time the oracle's ragged MoE (kappa's _moe_ragged restated) on the host.
+def _blas_threads(n: int) -> int:
+    """Give the host BLAS ``n`` threads (torchrun sets OMP_NUM_THREADS=1 for
+    its children, which would otherwise make the CPU arm single threaded)
+    and return the thread count the BLAS library reports."""
+    import numpy as np  # noqa: F401  (loads the BLAS library threadpoolctl controls)
+    from threadpoolctl import threadpool_info, threadpool_limits
 
-    Weights are the configs[1] shapes, drawn and quantised on the host; the
-    timed call is the whole layer (route, fp32 dequant of every expert as
-    kappa does each call, three ragged dots, combine) on ``tokens`` tokens.
-    Returns (tokens/s, seconds per call).
-    """
-    import numpy as np
+    threadpool_limits(limits=n, user_api="blas")
+    counts = [int(i.get("num_threads", 0)) for i in threadpool_info() if i.get("user_api") == "blas"]
+    return max(counts) if counts else 0
 
-    import oracle as O
 
-    rng = np.random.default_rng(0)
-    x = rng.standard_normal((1, tokens, D), dtype=np.float32).astype(O.BF16)
-    ws = [rng.standard_normal(s, dtype=np.float32) * np.float32(0.02) for s in ((D, E), (E, D, I), (E, D, I), (E, I, D))]
-    q = [O.quantize_weight(w, per_channel_axis=w.ndim - 2, scale_dtype=np.float32) for w in ws]
-    del ws
+class CpuMoE:
+    """kappa's ragged MoE layer (``_moe_ragged`` restated in the oracle) on the
+    host, on the configs[1] shapes: weights drawn and quantised on the host
+    once; every ``step()`` is the whole layer (route, fp32 dequant of every
+    expert as kappa does each call, three ragged dots, combine) on
+    ``tokens`` tokens."""
 
-    class Cfg:
-        use_moe = True
-        num_experts = E
-        num_experts_per_tok = K_TOP
-        moe_impl = "ragged_jax"
-        moe_capacity_factor = 1.25
-        moe_fixed_capacity_slots = None
-        moe_ragged_decode_token_threshold = 64
+    def __init__(self, tokens: int):
+        import numpy as np
 
-    O.moe_swiglu_ffn(x, *q, cfg=Cfg)  # warm-up
-    times = []
-    for _ in range(reps):
+        import oracle as O
+
+        self.O = O
+        self.tokens = tokens
+        self.cores = _cores()
+        self.blas_threads = _blas_threads(self.cores)
+        rng = np.random.default_rng(0)
+        self.x = rng.standard_normal((1, tokens, D), dtype=np.float32).astype(O.BF16)
+        ws = [rng.standard_normal(s, dtype=np.float32) * np.float32(0.02) for s in ((D, E), (E, D, I), (E, D, I), (E, I, D))]
+        self.q = [O.quantize_weight(w, per_channel_axis=w.ndim - 2, scale_dtype=np.float32) for w in ws]
+        del ws
+
+        class Cfg:
+            use_moe = True
+            num_experts = E
+            num_experts_per_tok = K_TOP
+            moe_impl = "ragged_jax"
+            moe_capacity_factor = 1.25
+            moe_fixed_capacity_slots = None
+            moe_ragged_decode_token_threshold = 64
+
+        self.cfg = Cfg
+
+    def step(self) -> float:
         t0 = time.perf_counter()
-        O.moe_swiglu_ffn(x, *q, cfg=Cfg)
-        times.append(time.perf_counter() - t0)
-    s = statistics.median(times)
-    return tokens / s, s
+        self.O.moe_swiglu_ffn(self.x, *self.q, cfg=self.cfg)
+        return time.perf_counter() - t0
+
+
+def cpu_reference_sample(tokens: int, reps: int):
+    """Median seconds per call of :class:`CpuMoE` over ``reps`` calls after one
+    warm-up call.  Returns (tokens/s, seconds per call, CpuMoE)."""
+    m = CpuMoE(tokens)
+    m.step()
+    s = statistics.median(m.step() for _ in range(reps))
+    return tokens / s, s, m
+
+
+def _config(world: int) -> dict:
+    """The workload of both arms (the reference arm runs it on rank 0's host)."""
+    return {
+        "workload": WORKLOAD,
+        "tokens_per_gpu": T_TOK,
+        "D": D,
+        "I": I,
+        "experts": E,
+        "top_k": K_TOP,
+        "parallelism": f"ep{world}" if world > 1 else "single",
+        "l2": "inputs larger than L2 (604 MB int8 expert weights read every step)",
+    }
+
+
+# The reference arm runs the configs[1] workload itself: all 4096 tokens
+# per step (a few seconds per step on the GPU box's host cores).
+REF_TOKENS = T_TOK
 
 
 def run_reference(args):
     world, rank, _ = _dist()
     if rank != 0:
         return 0
-    sample = 512
-    t0 = time.perf_counter()
-    tps, sec = cpu_reference_sample(sample, max(1, min(args.steps, 5)))
-    elapsed = time.perf_counter() - t0
+    t_start = time.perf_counter()
+    m = CpuMoE(REF_TOKENS)
+    for _ in range(args.warmup):
+        m.step()
+    times = [m.step() for _ in range(args.steps)]
+    total = sum(times)
+    tps = REF_TOKENS * args.steps / total
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -208,23 +253,26 @@ def run_reference(args):
         "n_gpus": args.gpus,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": sec * 1e3,
+        "ms_per_step": total / args.steps * 1e3,
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic (seeded N(0,1) x, N(0,0.02) weights, per-channel int8)",
-        "config": {"workload": WORKLOAD, "tokens_per_step": sample, "D": D, "I": I, "experts": E, "top_k": K_TOP},
+        "config": _config(world),
         "cpu_baseline": {
             "value": tps,
             "unit": UNIT,
-            "cores": _cores(),
+            "cores": m.cores,
+            "blas_threads": m.blas_threads,
             "kind": "port",
-            "sample": f"{sample} tokens of the configs[1] layer per step (kappa's ragged_jax formulation "
-            "restated in NumPy, fp32 BLAS on all host cores; JAX is not installed, so kappa itself cannot run)",
+            "sample": f"the whole configs[1] layer ({REF_TOKENS} tokens) per step, {args.steps} timed steps after "
+            f"{args.warmup} warm-up steps: kappa's ragged_jax formulation restated in NumPy, fp32 BLAS on "
+            f"{m.blas_threads} threads (JAX is not installed, so kappa itself cannot run); rank 0 only",
         },
         "e2e": {"value": tps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "wall_s": elapsed,
+        "wall_s": time.perf_counter() - t_start,
+        "timed_s": total,
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -712,15 +760,17 @@ def run_gpu(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        tps, sec = cpu_reference_sample(256, 2)
+        tps, sec, m = cpu_reference_sample(512, 2)
         cpu = {
             "value": tps,
             "unit": UNIT,
-            "cores": _cores(),
+            "cores": m.cores,
+            "blas_threads": m.blas_threads,
             "kind": "port",
-            "sample": "256 tokens of the configs[1] layer (NumPy restatement of kappa's ragged_jax path, "
-            "fp32 BLAS on the host cores), median of 2 calls",
+            "sample": "512 tokens of the configs[1] layer (NumPy restatement of kappa's ragged_jax path, "
+            f"fp32 BLAS on {m.blas_threads} threads), median of 2 calls after one warm-up call",
         }
+        del m
 
     if world > 1:
         ep_ctx.close()
@@ -741,16 +791,7 @@ def run_gpu(args):
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic: x ~ N(0,1) bf16, weights ~ N(0,0.02) -> per-channel int8 + fp32 scales (seeded)",
-        "config": {
-            "workload": WORKLOAD,
-            "tokens_per_gpu": T_TOK,
-            "D": D,
-            "I": I,
-            "experts": E,
-            "top_k": K_TOP,
-            "parallelism": f"ep{world}" if world > 1 else "single",
-            "l2": "inputs larger than L2 (604 MB int8 expert weights read every step)",
-        },
+        "config": _config(world),
         "roofline": {
             "bound": "tensor",
             "kernel": "grouped W8A16 expert GEMMs (gate/up + down)",

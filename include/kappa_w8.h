@@ -55,6 +55,11 @@ typedef enum kw8_act {
   KW8_ACT_SILU = 1,      /* jax.nn.silu                                      */
 } kw8_act;
 
+/* RMSNorm flavour: out = x * rsqrt(mean(x^2) + eps) * g with
+ * g = 1 + scale (Gemma3, kappa/gemma3/norms.py:8-13) or
+ * g = scale     (Qwen3,  kappa/qwen3/norms.py:10-16).                       */
+typedef enum kw8_norm_kind { KW8_NORM_GEMMA = 0, KW8_NORM_QWEN = 1 } kw8_norm_kind;
+
 /* One W8 weight: int8 values plus either one scale for the whole tensor
  * (kappa's Q8Weight, kappa/qwen3/quant.py:15-19) or one scale per output
  * channel (per expert when stacked): [groups][N] scales.                    */
@@ -134,6 +139,65 @@ int kw8_dense_ffn(const void* x, int64_t T, int64_t D, int64_t H,
                   int32_t out_dtype, void* out, void* workspace,
                   size_t workspace_bytes, kw8_stream_t stream);
 
+/* ------------------------------------------------------- W8 linears -- */
+
+/* One W8 linear layer: out[t][n] = (Σ_k x[t][k] * q[n][k]) * s[n].
+ * The attention projections of kappa (project_q / project_kv /
+ * project_attn_out, kappa/qwen3/linear.py:11-25 and kappa/gemma3/linear.py:
+ * 9-23) and the LM head (logits_from_hidden / _tied / _last_positions,
+ * kappa/qwen3/transformer.py:55-75) are this product with kappa's weight
+ * viewed K-major: w [N][K] int8 (N = heads*head_dim for Q/K/V, N = model dim
+ * for O with K = heads*head_dim, N = vocab for the head).
+ *   x    : bf16 rows of K features; row r of the product is x row
+ *          rows[r] when `rows` (device int32 [T]) is given, else x row r
+ *          (logits_from_hidden_last_positions gathers its rows this way).
+ *   out  : [T][N] in out_dtype (kappa's einsum output is bf16).
+ *   workspace >= kw8_linear_workspace_size(T, K, N) bytes.                  */
+size_t kw8_linear_workspace_size(int64_t T, int64_t K, int64_t N);
+int kw8_linear(const void* x, const int32_t* rows, int64_t T, int64_t K, int64_t N,
+               kw8_weight w, int32_t out_dtype, void* out, void* workspace,
+               size_t workspace_bytes, kw8_stream_t stream);
+
+/* gather_embed_tokens (kappa/qwen3/quant.py:51-57) for a W8 table:
+ * out[i][d] = dt(q[v][d]) * dt(s) with v = tokens[i], rounded once to
+ * out_dtype, s the table's scale (per tensor, or per row v).  Ids follow a
+ * JAX gather: a negative id counts from the end (v + V), then the id is
+ * clamped into [0, V).  table.q is [V][D] int8; out [n][D].               */
+int kw8_embed_gather(const int32_t* tokens, int64_t n, kw8_weight table, int64_t V,
+                     int64_t D, int32_t out_dtype, void* out, kw8_stream_t stream);
+
+/* ------------------------------------------------ norms + FFN sub-block -- */
+
+/* rms_norm: out = bf16((f32(x) * rsqrt(mean(f32(x)^2) + eps)) * g),
+ * g from kw8_norm_kind; x, out [T][D] bf16 (D % 8 == 0, D <= 16384);
+ * scale [D] in scale_dtype.                                                 */
+int kw8_rms_norm(const void* x, int64_t T, int64_t D, const void* scale, int32_t scale_dtype,
+                 int32_t kind, float eps, void* out, kw8_stream_t stream);
+
+/* The norms around a decoder block's FFN.  pre_scale [D] (required) is the
+ * pre-FFN RMSNorm; post_scale [D] (or NULL: none, as in Qwen3) the post-FFN
+ * RMSNorm; both in scale_dtype, of one kind.                                */
+typedef struct kw8_block_norms {
+  const void* pre_scale;
+  const void* post_scale;
+  int32_t scale_dtype;
+  int32_t kind;
+  float eps;
+} kw8_block_norms;
+
+/* The FFN sub-block of a dense decoder block, in one call:
+ *   out = h + post_norm(FFN(pre_norm(h)))
+ * with FFN = kw8_dense_ffn (act GELU_TANH: Gemma3, kappa/gemma3/block.py:
+ * 73-82; act SILU and no post norm: Qwen3, kappa/qwen3/block.py:68-81).
+ * Rounding as in kappa: the normed input, the FFN output, the post-normed
+ * output and the sum are each bf16.  The down projection writes fp32
+ * partial sums and one pass per row adds them, rounds, applies the post
+ * norm and adds the residual.  h, out [T][D] bf16 (out may not alias h).  */
+size_t kw8_dense_block_workspace_size(int64_t T, int64_t D, int64_t H);
+int kw8_dense_block(const void* h, int64_t T, int64_t D, int64_t H, kw8_weight gate,
+                    kw8_weight up, kw8_weight down, int32_t act, const kw8_block_norms* norms,
+                    void* out, void* workspace, size_t workspace_bytes, kw8_stream_t stream);
+
 /* ------------------------------------------------------------------ MoE -- */
 
 /* Router of moe_swiglu_ffn: _route (kappa/qwen3/ffn_moe.py:38-56).
@@ -205,6 +269,17 @@ int kw8_moe_ffn(const void* x, int64_t T, int64_t D, int64_t I, int64_t E,
                 int32_t k, int64_t capacity, kw8_weight router,
                 kw8_weight gate, kw8_weight up, kw8_weight down, void* out,
                 void* workspace, size_t workspace_bytes, kw8_stream_t stream);
+
+/* The FFN sub-block of a Qwen3 MoE decoder block (kappa/qwen3/block.py:
+ * 68-81) in one call: out = h + post_norm(moe_swiglu_ffn(pre_norm(h))),
+ * with the MoE layer of kw8_moe_ffn; the fp32 combine buffer goes through
+ * one pass per row that rounds it, applies the post norm (if any) and adds
+ * the residual.  h, out [T][D] bf16 (out may not alias h).                  */
+size_t kw8_moe_block_workspace_size(int64_t T, int64_t D, int64_t I, int64_t E, int32_t k);
+int kw8_moe_block(const void* h, int64_t T, int64_t D, int64_t I, int64_t E, int32_t k,
+                  int64_t capacity, kw8_weight router, kw8_weight gate, kw8_weight up,
+                  kw8_weight down, const kw8_block_norms* norms, void* out, void* workspace,
+                  size_t workspace_bytes, kw8_stream_t stream);
 
 /* ---------------------------------------------------- no-allocation -- */
 
@@ -289,7 +364,9 @@ int kw8_ep_local_offsets(const int32_t* counts, int32_t world, int32_t rank,
  *   rows : world * max_tokens rows of D bf16 (tokens sent to this rank);
  *   meta : world * max_tokens * k int32 row indices, then as many fp32
  *          routing weights (one record per routed pair);
- *   ret  : [world][max_tokens] rows of D bf16 (partial sums coming back);
+ *   ret  : [world][max_tokens] rows of D partial sums coming back, fp32
+ *          with ret_f32 (the source then rounds each output once, as one
+ *          GPU does) or bf16 (half the return traffic, one more rounding);
  * and counts is int32 [2][world][E + world].                               */
 typedef struct kw8_ep_peers {
   int32_t world;
@@ -309,6 +386,8 @@ typedef struct kw8_ep_peers {
   void* own_rows;
   void* own_meta;
   void* own_ret;
+  int32_t ret_f32; /* partial sums in ret as fp32 (ret rows of 4*D bytes)
+                      instead of bf16 (2*D bytes)                            */
 } kw8_ep_peers;
 
 /* The expert-parallel MoE layer over this rank's T <= max_tokens tokens in

@@ -49,3 +49,38 @@ def dense_ffn(
     )
     del keep
     return out
+
+
+def linear(
+    x2d: torch.Tensor,
+    w: KMajor,
+    *,
+    rows: torch.Tensor | None = None,
+    out_dtype: torch.dtype = torch.bfloat16,
+) -> torch.Tensor:
+    """``x2d[r] . w^T`` through ``kw8_linear``: x2d ``[R, K]`` bf16, ``w`` K-major ``[N, K]``.
+
+    With ``rows`` (int32 indices into x2d) the product runs on those rows
+    only, gathered inside the kernel.  Returns ``[len(rows) or R, N]``.
+    """
+    if out_dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError(f"out_dtype must be bfloat16 or float32, got {out_dtype}")
+    K = int(w.q.shape[-1])
+    N = w.q.numel() // K
+    xc = x2d.contiguous()
+    if xc.dim() != 2 or int(xc.shape[1]) != K:
+        raise ValueError(f"x rows have {tuple(xc.shape)[1:]} features, the weight takes {K}")
+    T = int(xc.shape[0]) if rows is None else int(rows.numel())
+    lib = _lib.load()
+    out = torch.empty((T, N), dtype=out_dtype, device=x2d.device)
+    ws = torch.empty(int(lib.kw8_linear_workspace_size(T, K, N)), dtype=torch.uint8, device=x2d.device)
+    rows_c = None if rows is None else rows.to(torch.int32).contiguous()
+    _lib.check(
+        lib.kw8_linear(
+            xc.data_ptr(), None if rows_c is None else rows_c.data_ptr(), T, K, N, w.struct(),
+            _lib.DT_F32 if out_dtype == torch.float32 else _lib.DT_BF16, out.data_ptr(), ws.data_ptr(),
+            ws.numel(), _lib.stream_of(x2d),
+        )
+    )
+    del rows_c
+    return out

@@ -32,9 +32,14 @@ DT_BF16 = 1
 ACT_GELU_TANH = 0
 ACT_SILU = 1
 
+# kw8_norm_kind
+NORM_GEMMA = 0  # x * rsqrt(mean(x^2) + eps) * (1 + scale)
+NORM_QWEN = 1  # x * rsqrt(mean(x^2) + eps) * scale
+
 # kw8_set_option
 OPT_GEMM_PATH = 0  # 0 auto, 1 tensor core, 2 weight streaming (decode kernel)
 OPT_TOKEN_TILE = 1  # 0 auto, 16..256
+OPT_DETERMINISTIC = 2  # 1: the MoE combine sums each token's k rows in a fixed order
 
 
 class KW8Error(RuntimeError):
@@ -53,6 +58,18 @@ class KW8Weight(ctypes.Structure):
         ("scale", ctypes.c_void_p),
         ("scale_dtype", ctypes.c_int32),
         ("per_channel", ctypes.c_int32),
+    ]
+
+
+class KW8BlockNorms(ctypes.Structure):
+    """``kw8_block_norms`` (include/kappa_w8.h): the norms around a block's FFN."""
+
+    _fields_ = [
+        ("pre_scale", ctypes.c_void_p),
+        ("post_scale", ctypes.c_void_p),
+        ("scale_dtype", ctypes.c_int32),
+        ("kind", ctypes.c_int32),
+        ("eps", ctypes.c_float),
     ]
 
 
@@ -77,6 +94,7 @@ class KW8EpPeers(ctypes.Structure):
         ("own_rows", ctypes.c_void_p),
         ("own_meta", ctypes.c_void_p),
         ("own_ret", ctypes.c_void_p),
+        ("ret_f32", ctypes.c_int32),
     ]
 
 
@@ -101,6 +119,22 @@ SIGNATURES: dict[str, tuple] = {
     "kw8_dense_ffn": (
         ctypes.c_int,
         [_vp, _i64, _i64, _i64, KW8Weight, KW8Weight, KW8Weight, _i32, _i32, _vp, _vp, _sz, _vp],
+    ),
+    "kw8_linear_workspace_size": (_sz, [_i64, _i64, _i64]),
+    "kw8_linear": (ctypes.c_int, [_vp, _vp, _i64, _i64, _i64, KW8Weight, _i32, _vp, _vp, _sz, _vp]),
+    "kw8_embed_gather": (ctypes.c_int, [_vp, _i64, KW8Weight, _i64, _i64, _i32, _vp, _vp]),
+    "kw8_rms_norm": (ctypes.c_int, [_vp, _i64, _i64, _vp, _i32, _i32, ctypes.c_float, _vp, _vp]),
+    "kw8_dense_block_workspace_size": (_sz, [_i64, _i64, _i64]),
+    "kw8_dense_block": (
+        ctypes.c_int,
+        [_vp, _i64, _i64, _i64, KW8Weight, KW8Weight, KW8Weight, _i32, ctypes.POINTER(KW8BlockNorms), _vp, _vp,
+         _sz, _vp],
+    ),
+    "kw8_moe_block_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i32]),
+    "kw8_moe_block": (
+        ctypes.c_int,
+        [_vp, _i64, _i64, _i64, _i64, _i32, _i64, KW8Weight, KW8Weight, KW8Weight, KW8Weight,
+         ctypes.POINTER(KW8BlockNorms), _vp, _vp, _sz, _vp],
     ),
     "kw8_moe_route": (ctypes.c_int, [_vp, _i64, _i64, _i64, _i32, KW8Weight, _vp, _vp, _vp, _vp]),
     "kw8_moe_topk": (ctypes.c_int, [_vp, _i64, _i64, _i32, _vp, _vp, _vp]),

@@ -6,6 +6,7 @@
 #include "gemm_stream.cuh"
 #include "gemm_tc.cuh"
 #include "moe.cuh"
+#include "norm.cuh"
 #include "quant.cuh"
 
 namespace kw8 {
@@ -17,6 +18,7 @@ namespace {
 
 std::atomic<int> g_opt_path{0};        // 0 auto, 1 tensor core, 2 weight streaming
 std::atomic<int> g_opt_token_tile{0};  // 0 auto, else 16..256 (multiple of 16)
+std::atomic<int> g_opt_deterministic{0};  // 1: MoE combine in a fixed order
 
 // Carves 256-byte aligned sub-buffers out of the caller's workspace.  With
 // base == nullptr it only measures.
@@ -409,6 +411,195 @@ int64_t dense_down_part_floats(int64_t T, int64_t D, int64_t H) {
   return splits > 1 ? splits * T * D : 0;
 }
 
+// Gate/up GEMM with the activation epilogue: h [T][H] bf16.
+int dense_gate_up(const void* x, int64_t T, int64_t D, int64_t H, const kw8_weight& gate,
+                  const kw8_weight& up, int act, __nv_bfloat16* h, cudaStream_t stream) {
+  const int epi_pair = act == KW8_ACT_GELU_TANH ? EPI_PAIR_GELU : EPI_PAIR_SILU;
+  if (use_stream(static_cast<double>(T))) {
+    StreamArgs g = stream_args(gate, &up);
+    g.dense_rows = static_cast<int>(T);
+    g.out = h;
+    g.ld_out = H;
+    return launch_gemm_stream(epi_pair, gate.q, up.q, 1, H, D, x, D, T, stream_nt(static_cast<double>(T)), g,
+                              stream);
+  }
+  GemmArgs g = base_args(gate, &up);
+  g.dense_rows = static_cast<int>(T);
+  g.nt = pick_nt_dense(T, (H + 63) / 64);
+  g.out = h;
+  g.ld_out = H;
+  return run_gemm(epi_pair, gate, &up, 1, H, D, x, T, D, g, stream);
+}
+
+// A dense W8 product y = x . w^T (x [T][K] bf16 -> [T][N]) as fp32 partial
+// sums part[s][T][N], s < splits (1: one slice), on the path the option
+// selects; `splits` comes from linear_splits().
+int dense_f32_parts(const void* x, int64_t T, int64_t K, int64_t N, const kw8_weight& w, int splits,
+                    float* part, cudaStream_t stream) {
+  if (use_stream(static_cast<double>(T))) {
+    StreamArgs d = stream_args(w, nullptr);
+    d.dense_rows = static_cast<int>(T);
+    d.out = part;
+    d.ld_out = N;
+    if (splits > 1) {
+      d.kz_max = kStreamMaxKz;
+      d.split_stride = T * N;
+    }
+    return launch_gemm_stream(EPI_PLAIN_F32, w.q, nullptr, 1, N, K, x, K, T, stream_nt(static_cast<double>(T)), d,
+                              stream);
+  }
+  GemmArgs d = base_args(w, nullptr);
+  d.dense_rows = static_cast<int>(T);
+  d.nt = pick_nt_dense(T, (N + 127) / 128);
+  d.out = part;
+  d.ld_out = N;
+  if (splits > 1) {
+    d.k_splits = splits;
+    d.split_stride = T * N;
+  }
+  return run_gemm(EPI_PLAIN_F32, w, nullptr, 1, N, K, x, T, K, d, stream);
+}
+
+// ------------------------------------------------------- W8 linear ----
+
+// A linear layer takes the weight-streaming kernel for few rows, or when
+// its output is narrow (at most two 128-feature tiles: the tensor-core
+// kernel would keep few SMs busy) up to kStreamRouterMaxRows rows.
+bool linear_streamed(int64_t T, int64_t N) {
+  const int path = g_opt_path.load();
+  if (path != 0) return path == 2;
+  return T <= static_cast<int64_t>(kStreamMaxRowsHint) || (N <= 256 && T <= kStreamRouterMaxRows);
+}
+
+// K split of a linear layer on its path (1: none).
+int linear_splits(int64_t T, int64_t K, int64_t N) {
+  return linear_streamed(T, N) ? stream_f32_kz(T, N, K) : dense_f32_splits(T, N, K);
+}
+
+struct LinearBuffers {
+  __nv_bfloat16* xg;  // gathered rows (tensor-core path with a row index)
+  float* part;        // split-K partial sums
+};
+
+LinearBuffers carve_linear(Carver& c, int64_t T, int64_t K, int64_t N) {
+  LinearBuffers b;
+  b.xg = c.take<__nv_bfloat16>(T * K);
+  const int splits = std::max(stream_f32_kz(T, N, K), dense_f32_splits(T, N, K));
+  b.part = c.take<float>(splits > 1 ? splits * T * N : 0);
+  return b;
+}
+
+int linear(const void* x, const int32_t* rows, int64_t T, int64_t K, int64_t N, const kw8_weight& w,
+           bool out_f32, void* out, const LinearBuffers& b, cudaStream_t stream) {
+  const bool streamed = linear_streamed(T, N);
+  const int splits = linear_splits(T, K, N);
+  const int mode = out_f32 ? EPI_PLAIN_F32 : EPI_PLAIN_BF16;
+  if (streamed) {
+    StreamArgs a = stream_args(w, nullptr);
+    a.dense_rows = static_cast<int>(T);
+    a.row_index = rows;  // the gather is fused into the operand load
+    a.out = out;
+    a.ld_out = N;
+    if (splits > 1) {
+      a.out = b.part;
+      a.kz_max = kStreamMaxKz;
+      a.split_stride = T * N;
+    }
+    int rc = launch_gemm_stream(splits > 1 ? EPI_PLAIN_F32 : mode, w.q, nullptr, 1, N, K, x, K, T,
+                                stream_nt(static_cast<double>(T)), a, stream);
+    if (rc || splits <= 1) return rc;
+    return launch_reduce_splits(b.part, splits, T * N, T * N, out, !out_f32, stream);
+  }
+  const void* xs = x;
+  if (rows != nullptr) {
+    // The TMA loads need the rows contiguous: gather them first.
+    int rc = launch_gather(x, rows, nullptr, T, K, b.xg, stream);
+    if (rc) return rc;
+    xs = b.xg;
+  }
+  GemmArgs a = base_args(w, nullptr);
+  a.dense_rows = static_cast<int>(T);
+  a.nt = pick_nt_dense(T, (N + 127) / 128);
+  a.out = out;
+  a.ld_out = N;
+  if (splits > 1) {
+    a.out = b.part;
+    a.k_splits = splits;
+    a.split_stride = T * N;
+  }
+  int rc = run_gemm(splits > 1 ? EPI_PLAIN_F32 : mode, w, nullptr, 1, N, K, xs, T, K, a, stream);
+  if (rc || splits <= 1) return rc;
+  return launch_reduce_splits(b.part, splits, T * N, T * N, out, !out_f32, stream);
+}
+
+int check_moe_args(int64_t T, int64_t D, int64_t I, int64_t E, int k, const kw8_weight& router,
+                   const kw8_weight& gate, const kw8_weight& up, const kw8_weight& down) {
+  KW8_REQUIRE(T >= 0 && D > 0 && I > 0 && E > 0 && k >= 1 && k <= E, KW8_ERR_INVALID_ARG,
+              "bad shape (T=%lld D=%lld I=%lld E=%lld k=%d)", (long long)T, (long long)D,
+              (long long)I, (long long)E, k);
+  int rc = check_weight(router, "router");
+  if (!rc) rc = check_weight(gate, "gate");
+  if (!rc) rc = check_weight(up, "up");
+  if (!rc) rc = check_weight(down, "down");
+  if (rc) return rc;
+  KW8_REQUIRE(T * k < (1ll << 31), KW8_ERR_UNSUPPORTED, "too many routed rows");
+  return KW8_OK;
+}
+
+// The MoE layer up to its fp32 output b.acc [T][D] (T >= 1).
+int moe_layer_acc(const void* x, int64_t T, int64_t D, int64_t I, int64_t E, int k, int64_t capacity,
+                  const kw8_weight& router, const kw8_weight& gate, const kw8_weight& up,
+                  const kw8_weight& down, const MoeBuffers& b, cudaStream_t stream) {
+  const int64_t m = T * k;
+  int rc;
+  // The top-k kernel also zeroes the fp32 combine buffer (one row per token).
+  float* part = router_part_floats(T, D, E) > 0 ? b.router_part : nullptr;
+  if (route_tail_small_ok(T, E, k)) {  // decode: top-k, permutation and zeroing in one launch
+    rc = router_logits(x, T, D, E, router, b.logits, stream, part);
+    if (!rc)
+      rc = launch_route_tail_small(b.logits, T, E, k, capacity, b.idx, b.w, b.sorted_token,
+                                   b.inv_pos, b.group_sizes, b.group_offsets, b.sorted_w,
+                                   b.active, b.acc, D, stream);
+  } else {
+    rc = kw8::route(x, T, D, E, k, router, b.logits, b.idx, b.w, stream, part, b.acc, D);
+    if (!rc)
+      rc = launch_permute_multi(b.idx, T, k, E, capacity, b.perm_hist, b.sorted_token, b.inv_pos,
+                                b.group_sizes, b.group_offsets, stream, b.w, b.sorted_w, b.active);
+  }
+  if (rc) return rc;
+  // Few rows per expert: the weight-streaming kernels read x rows through
+  // the permutation (no gathered copy); otherwise gather for the TMA loads.
+  const bool streamed = use_stream(rows_hint(m, E));
+  if (!streamed) {
+    rc = launch_gather(x, b.sorted_token, b.group_offsets + E, m, D, b.xs, stream);
+    if (rc) return rc;
+  }
+  ExpertBuffers eb{b.tiles, b.num_tiles, b.h};
+  if (g_opt_deterministic.load()) {
+    // Deterministic combine: the expert outputs are stored as bf16 rows in
+    // sorted order (into xs, free once gate/up has read it; kappa also
+    // rounds them to bf16, ffn_moe.py:213) and each token's k rows are
+    // summed in slot order.
+    rc = expert_ffn(streamed, streamed ? x : b.xs, streamed ? b.sorted_token : nullptr, m, D, I, E,
+                    b.group_offsets, gate, up, down, b.xs, eb, stream, nullptr, nullptr, b.active);
+    if (rc) return rc;
+    return launch_combine(b.xs, b.inv_pos, b.w, T, k, D, b.acc, stream, true);
+  }
+  // The down projection adds w * y of every routed row straight into the
+  // fp32 token buffer (zeroed by the top-k kernel; no bf16 rounding of the
+  // per-expert outputs, no [T*k][D] round trip).  The order of those fp32
+  // additions varies from call to call.
+  return expert_ffn(streamed, streamed ? x : b.xs, streamed ? b.sorted_token : nullptr, m, D, I, E,
+                    b.group_offsets, gate, up, down, b.acc, eb, stream, b.sorted_token, b.sorted_w,
+                    b.active);
+}
+
+int check_norms(const kw8_block_norms* n, int64_t D) {
+  KW8_REQUIRE(n != nullptr && n->pre_scale != nullptr, KW8_ERR_INVALID_ARG, "block norms: pre-FFN scale required");
+  (void)D;
+  return KW8_OK;
+}
+
 }  // namespace
 }  // namespace kw8
 
@@ -438,6 +629,11 @@ int kw8_set_option(int32_t option, int64_t value) {
     KW8_REQUIRE(value == 0 || (value >= 16 && value <= kTcMaxNT && value % 16 == 0),
                 KW8_ERR_INVALID_ARG, "token tile must be 0 or a multiple of 16 in [16, 256]");
     g_opt_token_tile.store(static_cast<int>(value));
+    return KW8_OK;
+  }
+  if (option == 2) {
+    KW8_REQUIRE(value == 0 || value == 1, KW8_ERR_INVALID_ARG, "deterministic must be 0 or 1");
+    g_opt_deterministic.store(static_cast<int>(value));
     return KW8_OK;
   }
   return fail(KW8_ERR_INVALID_ARG, "unknown option %d", option);
@@ -636,53 +832,118 @@ int kw8_moe_ffn(const void* x, int64_t T, int64_t D, int64_t I, int64_t E, int32
                 kw8_stream_t stream) {
   KW8_API_BEGIN
   KW8_REQUIRE(x && out, KW8_ERR_INVALID_ARG, "null x/out");
-  KW8_REQUIRE(T >= 0 && D > 0 && I > 0 && E > 0 && k >= 1 && k <= E, KW8_ERR_INVALID_ARG,
-              "bad shape (T=%lld D=%lld I=%lld E=%lld k=%d)", (long long)T, (long long)D,
-              (long long)I, (long long)E, k);
-  int rc = check_weight(router, "router");
-  if (!rc) rc = check_weight(gate, "gate");
-  if (!rc) rc = check_weight(up, "up");
-  if (!rc) rc = check_weight(down, "down");
-  if (rc) return rc;
-  if (T == 0) return KW8_OK;
-  KW8_REQUIRE(T * k < (1ll << 31), KW8_ERR_UNSUPPORTED, "too many routed rows");
+  int rc = check_moe_args(T, D, I, E, k, router, gate, up, down);
+  if (rc || T == 0) return rc;
   Carver c(workspace, workspace_bytes);
   MoeBuffers b = carve_moe(c, T, D, I, E, k);
   KW8_REQUIRE(workspace != nullptr && c.ok, KW8_ERR_WORKSPACE,
               "MoE workspace too small (%zu < %zu)", workspace_bytes, c.off);
-  const int64_t m = T * k;
-  // The top-k kernel also zeroes the fp32 combine buffer (one row per token).
-  float* part = router_part_floats(T, D, E) > 0 ? b.router_part : nullptr;
-  if (route_tail_small_ok(T, E, k)) {  // decode: top-k, permutation and zeroing in one launch
-    rc = router_logits(x, T, D, E, router, b.logits, stream, part);
-    if (!rc)
-      rc = launch_route_tail_small(b.logits, T, E, k, capacity, b.idx, b.w, b.sorted_token,
-                                   b.inv_pos, b.group_sizes, b.group_offsets, b.sorted_w,
-                                   b.active, b.acc, D, stream);
-  } else {
-    rc = kw8::route(x, T, D, E, k, router, b.logits, b.idx, b.w, stream, part, b.acc, D);
-    if (!rc)
-      rc = launch_permute_multi(b.idx, T, k, E, capacity, b.perm_hist, b.sorted_token, b.inv_pos,
-                                b.group_sizes, b.group_offsets, stream, b.w, b.sorted_w, b.active);
-  }
-  if (rc) return rc;
-  // Few rows per expert: the weight-streaming kernels read x rows through
-  // the permutation (no gathered copy); otherwise gather for the TMA loads.
-  const bool streamed = use_stream(rows_hint(m, E));
-  if (!streamed) {
-    rc = launch_gather(x, b.sorted_token, b.group_offsets + E, m, D, b.xs, stream);
-    if (rc) return rc;
-  }
-  // The down projection adds w * y of every routed row straight into the
-  // fp32 token buffer (zeroed by the top-k kernel; no bf16 rounding of the
-  // per-expert outputs, no [T*k][D] round trip); one conversion pass writes
-  // the bf16 output.
-  ExpertBuffers eb{b.tiles, b.num_tiles, b.h};
-  rc = expert_ffn(streamed, streamed ? x : b.xs, streamed ? b.sorted_token : nullptr, m, D, I, E,
-                  b.group_offsets, gate, up, down, b.acc, eb, stream, b.sorted_token, b.sorted_w,
-                  b.active);
+  rc = moe_layer_acc(x, T, D, I, E, k, capacity, router, gate, up, down, b, stream);
   if (rc) return rc;
   return launch_f32_to_bf16(b.acc, T * D, out, stream);
+}
+
+size_t kw8_moe_block_workspace_size(int64_t T, int64_t D, int64_t I, int64_t E, int32_t k) {
+  Carver c(nullptr, SIZE_MAX);
+  carve_moe(c, T, D, I, E, k);
+  c.take<__nv_bfloat16>(T * D);
+  return c.off;
+}
+
+int kw8_moe_block(const void* h, int64_t T, int64_t D, int64_t I, int64_t E, int32_t k,
+                  int64_t capacity, kw8_weight router, kw8_weight gate, kw8_weight up,
+                  kw8_weight down, const kw8_block_norms* norms, void* out, void* workspace,
+                  size_t workspace_bytes, kw8_stream_t stream) {
+  KW8_API_BEGIN
+  KW8_REQUIRE(h && out && h != out, KW8_ERR_INVALID_ARG, "null or aliased h/out");
+  int rc = check_moe_args(T, D, I, E, k, router, gate, up, down);
+  if (!rc) rc = check_norms(norms, D);
+  if (rc || T == 0) return rc;
+  Carver c(workspace, workspace_bytes);
+  MoeBuffers b = carve_moe(c, T, D, I, E, k);
+  __nv_bfloat16* xn = c.take<__nv_bfloat16>(T * D);
+  KW8_REQUIRE(workspace != nullptr && c.ok, KW8_ERR_WORKSPACE,
+              "MoE block workspace too small (%zu < %zu)", workspace_bytes, c.off);
+  rc = launch_rms_norm(h, T, D, norms->pre_scale, norms->scale_dtype, norms->kind, norms->eps, xn, stream);
+  if (!rc) rc = moe_layer_acc(xn, T, D, I, E, k, capacity, router, gate, up, down, b, stream);
+  if (rc) return rc;
+  return launch_block_finish(b.acc, 1, 0, T, D, norms->post_scale, norms->scale_dtype, norms->kind, norms->eps, h,
+                             out, stream);
+}
+
+size_t kw8_linear_workspace_size(int64_t T, int64_t K, int64_t N) {
+  Carver c(nullptr, SIZE_MAX);
+  carve_linear(c, T, K, N);
+  return c.off;
+}
+
+int kw8_linear(const void* x, const int32_t* rows, int64_t T, int64_t K, int64_t N, kw8_weight w,
+               int32_t out_dtype, void* out, void* workspace, size_t workspace_bytes,
+               kw8_stream_t stream) {
+  KW8_API_BEGIN
+  KW8_REQUIRE((x && out) || T == 0, KW8_ERR_INVALID_ARG, "null x/out");
+  KW8_REQUIRE(T >= 0 && K > 0 && N > 0, KW8_ERR_INVALID_ARG, "bad shape (T=%lld K=%lld N=%lld)",
+              (long long)T, (long long)K, (long long)N);
+  KW8_REQUIRE(out_dtype == KW8_DT_BF16 || out_dtype == KW8_DT_F32, KW8_ERR_INVALID_ARG, "bad out dtype");
+  int rc = check_weight(w, "weight");
+  if (rc || T == 0) return rc;
+  KW8_REQUIRE(T < (1ll << 31) && N < (1ll << 31), KW8_ERR_UNSUPPORTED, "shape out of range");
+  Carver c(workspace, workspace_bytes);
+  LinearBuffers b = carve_linear(c, T, K, N);
+  KW8_REQUIRE(workspace != nullptr && c.ok, KW8_ERR_WORKSPACE, "linear workspace too small (%zu < %zu)",
+              workspace_bytes, c.off);
+  return linear(x, rows, T, K, N, w, out_dtype == KW8_DT_F32, out, b, stream);
+}
+
+int kw8_embed_gather(const int32_t* tokens, int64_t n, kw8_weight table, int64_t V, int64_t D,
+                     int32_t out_dtype, void* out, kw8_stream_t stream) {
+  KW8_API_BEGIN
+  int rc = check_weight(table, "table");
+  if (rc) return rc;
+  return launch_embed_gather(tokens, n, table, V, D, out_dtype, out, stream);
+}
+
+int kw8_rms_norm(const void* x, int64_t T, int64_t D, const void* scale, int32_t scale_dtype,
+                 int32_t kind, float eps, void* out, kw8_stream_t stream) {
+  KW8_API_BEGIN
+  return launch_rms_norm(x, T, D, scale, scale_dtype, kind, eps, out, stream);
+}
+
+size_t kw8_dense_block_workspace_size(int64_t T, int64_t D, int64_t H) {
+  Carver c(nullptr, SIZE_MAX);
+  c.take<__nv_bfloat16>(T * D);
+  c.take<__nv_bfloat16>(T * H);
+  c.take<float>(std::max<int64_t>(dense_down_part_floats(T, D, H), T * D));
+  return c.off;
+}
+
+int kw8_dense_block(const void* h, int64_t T, int64_t D, int64_t H, kw8_weight gate, kw8_weight up,
+                    kw8_weight down, int32_t act, const kw8_block_norms* norms, void* out,
+                    void* workspace, size_t workspace_bytes, kw8_stream_t stream) {
+  KW8_API_BEGIN
+  KW8_REQUIRE(h && out && h != out, KW8_ERR_INVALID_ARG, "null or aliased h/out");
+  KW8_REQUIRE(T >= 0 && D > 0 && H > 0, KW8_ERR_INVALID_ARG, "bad shape");
+  KW8_REQUIRE(act == KW8_ACT_GELU_TANH || act == KW8_ACT_SILU, KW8_ERR_INVALID_ARG, "bad act");
+  int rc = check_weight(gate, "gate");
+  if (!rc) rc = check_weight(up, "up");
+  if (!rc) rc = check_weight(down, "down");
+  if (!rc) rc = check_norms(norms, D);
+  if (rc || T == 0) return rc;
+  KW8_REQUIRE(T < (1ll << 31), KW8_ERR_UNSUPPORTED, "too many tokens");
+  Carver c(workspace, workspace_bytes);
+  __nv_bfloat16* xn = c.take<__nv_bfloat16>(T * D);
+  __nv_bfloat16* hid = c.take<__nv_bfloat16>(T * H);
+  float* part = c.take<float>(std::max<int64_t>(dense_down_part_floats(T, D, H), T * D));
+  KW8_REQUIRE(workspace != nullptr && c.ok, KW8_ERR_WORKSPACE, "dense block workspace too small (%zu < %zu)",
+              workspace_bytes, c.off);
+  const int splits = dense_down_splits(T, D, H);
+  rc = launch_rms_norm(h, T, D, norms->pre_scale, norms->scale_dtype, norms->kind, norms->eps, xn, stream);
+  if (!rc) rc = dense_gate_up(xn, T, D, H, gate, up, act, hid, stream);
+  if (!rc) rc = dense_f32_parts(hid, T, H, D, down, splits, part, stream);
+  if (rc) return rc;
+  // One pass per row: the split sums, bf16, the post-FFN norm, the residual.
+  return launch_block_finish(part, splits, T * D, T, D, norms->post_scale, norms->scale_dtype, norms->kind,
+                             norms->eps, h, out, stream);
 }
 
 }  // extern "C"

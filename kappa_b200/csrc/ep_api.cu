@@ -213,11 +213,13 @@ int kw8_moe_ffn_ep(const void* x, int64_t T, int64_t D, int64_t I, int64_t E, in
     rc = expert_ffn(use_stream(rows_hint(recv_rows, e_loc)), b.ys_loc, nullptr, recv_rows, D, I, e_loc,
                     b.loc_off, gate_local, up_local, down_local, b.part, b.eb, stream, meta_u, meta_w);
     if (rc) return rc;
-    rc = launch_ep_return2(b.part, D, cnt, world, rank, E, peers->max_tokens, peers->ret, stream);
+    rc = launch_ep_return2(b.part, D, cnt, world, rank, E, peers->max_tokens, peers->ret, peers->ret_f32 != 0,
+                           stream);
     if (rc) return rc;
     rc = launch_ep_barrier(peers->flags, peers->own_flags, world, rank, 2, epoch, true, stream);
     if (rc) return rc;
-    return launch_ep_final2(peers->own_ret, b.tok_slot, T, world, peers->max_tokens, D, out, stream);
+    return launch_ep_final2(peers->own_ret, b.tok_slot, T, world, peers->max_tokens, D, peers->ret_f32 != 0, out,
+                            stream);
   }
   // Counts to every peer (phase 0), rows to their expert owners (phase 1).
   rc = launch_ep_counts(b.group_sizes, E, peers->counts, peers->flags, peers->own_flags, world, rank,

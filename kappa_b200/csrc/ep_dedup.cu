@@ -15,7 +15,8 @@
 // into one fp32 partial row per received token (the fused combine, rows
 // indexed by the records); each partial goes back to its source as bf16
 // (ret[r][slot] on the source), and the source sums its partials over the
-// ranks in rank order.
+// ranks in rank order.  The partials travel as fp32 (the sum is rounded
+// once, as on one GPU) or, to halve the return traffic, as bf16.
 #include "ep.cuh"
 
 namespace kw8 {
@@ -135,11 +136,12 @@ __global__ void __launch_bounds__(kDdThreads)
     part[i] = make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
-// Owner side: partial row u (source s, slot u - uoff(rank, s)) as bf16 into
-// source s's return buffer at [rank][slot].  A warp per row.
+// Owner side: partial row u (source s, slot u - uoff(rank, s)) into source
+// s's return buffer at [rank][slot]: fp32 as computed (ret_f32), or bf16.
+// A warp per row.
 __global__ void __launch_bounds__(kDdThreads)
     ep_return2_kernel(const float4* __restrict__ part, int D, const int32_t* __restrict__ counts, int world,
-                      int rank, int E, int64_t max_tokens, const uint64_t* __restrict__ peer_ret) {
+                      int rank, int E, int64_t max_tokens, const uint64_t* __restrict__ peer_ret, int ret_f32) {
   __shared__ int start[kEpMaxRanks + 1];  // first row of each source
   if (threadIdx.x == 0) {
     int acc = 0;
@@ -158,8 +160,13 @@ __global__ void __launch_bounds__(kDdThreads)
     int s = 0;
     while (s + 1 < world && start[s + 1] <= u) ++s;
     const float4* src = part + static_cast<int64_t>(u) * (D / 4);
-    uint4* dst = reinterpret_cast<uint4*>(peer_ret[s]) +
-                 (static_cast<int64_t>(rank) * max_tokens + (u - start[s])) * v8;
+    const int64_t drow = static_cast<int64_t>(rank) * max_tokens + (u - start[s]);
+    if (ret_f32) {
+      float4* dst = reinterpret_cast<float4*>(peer_ret[s]) + drow * (D / 4);
+      for (int c = lane; c < D / 4; c += 32) dst[c] = src[c];
+      continue;
+    }
+    uint4* dst = reinterpret_cast<uint4*>(peer_ret[s]) + drow * v8;
     for (int c = lane; c < v8; c += 32) {
       const float4 a = src[2 * c], b = src[2 * c + 1];
       const __nv_bfloat162 p0 = __floats2bfloat162_rn(a.x, a.y), p1 = __floats2bfloat162_rn(a.z, a.w);
@@ -176,10 +183,11 @@ __global__ void __launch_bounds__(kDdThreads)
 }
 
 // Source side: out[t] = sum over ranks r (in order) of ret[r][tok_slot[t][r]]
-// in fp32, then bf16 (zero for a token with no kept slot).  A warp per token.
+// (fp32 or bf16 partials) in fp32, then bf16 (zero for a token with no kept
+// slot).  A warp per token.
 __global__ void __launch_bounds__(kDdThreads)
-    ep_final2_kernel(const uint4* __restrict__ ret, const int32_t* __restrict__ tok_slot, int T, int world,
-                     int64_t max_tokens, int D, uint4* __restrict__ out) {
+    ep_final2_kernel(const void* __restrict__ ret, const int32_t* __restrict__ tok_slot, int T, int world,
+                     int64_t max_tokens, int D, int ret_f32, uint4* __restrict__ out) {
   const int lane = threadIdx.x & 31;
   const int wpb = blockDim.x >> 5;
   const int v8 = D / 8;
@@ -189,7 +197,15 @@ __global__ void __launch_bounds__(kDdThreads)
       for (int r = 0; r < world; ++r) {
         const int slot = tok_slot[static_cast<int64_t>(t) * world + r];
         if (slot < 0) continue;
-        const uint4 v = ret[(static_cast<int64_t>(r) * max_tokens + slot) * v8 + c];
+        const int64_t row = static_cast<int64_t>(r) * max_tokens + slot;
+        if (ret_f32) {
+          const float4* p = static_cast<const float4*>(ret) + row * (D / 4) + 2 * c;
+          const float4 a = p[0], b = p[1];
+          acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
+          acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
+          continue;
+        }
+        const uint4 v = static_cast<const uint4*>(ret)[row * v8 + c];
         const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -261,19 +277,19 @@ int launch_ep_gather2(const void* rows, const int32_t* meta, const int32_t* loc_
 }
 
 int launch_ep_return2(const float* part, int64_t D, const int32_t* counts, int world, int rank, int64_t E,
-                      int64_t max_tokens, const uint64_t* peer_ret, cudaStream_t stream) {
+                      int64_t max_tokens, const uint64_t* peer_ret, bool ret_f32, cudaStream_t stream) {
   ep_return2_kernel<<<ep_grid(static_cast<int64_t>(world) * max_tokens, kDdThreads / 32), kDdThreads, 0,
                       stream>>>(reinterpret_cast<const float4*>(part), static_cast<int>(D), counts, world, rank,
-                                static_cast<int>(E), max_tokens, peer_ret);
+                                static_cast<int>(E), max_tokens, peer_ret, ret_f32 ? 1 : 0);
   KW8_CHECK_LAUNCH();
   return KW8_OK;
 }
 
 int launch_ep_final2(const void* ret, const int32_t* tok_slot, int64_t T, int world, int64_t max_tokens,
-                     int64_t D, void* out, cudaStream_t stream) {
+                     int64_t D, bool ret_f32, void* out, cudaStream_t stream) {
   if (T <= 0) return KW8_OK;
   ep_final2_kernel<<<ep_grid(T, kDdThreads / 32), kDdThreads, 0, stream>>>(
-      static_cast<const uint4*>(ret), tok_slot, static_cast<int>(T), world, max_tokens, static_cast<int>(D),
+      ret, tok_slot, static_cast<int>(T), world, max_tokens, static_cast<int>(D), ret_f32 ? 1 : 0,
       static_cast<uint4*>(out));
   KW8_CHECK_LAUNCH();
   return KW8_OK;

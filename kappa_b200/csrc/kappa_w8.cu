@@ -6,6 +6,7 @@
 #include "gemm_tc.cu"
 #include "gemm_stream.cu"
 #include "moe.cu"
+#include "norm.cu"
 #include "api.cu"
 #include "noalloc.cu"
 #include "ep.cu"

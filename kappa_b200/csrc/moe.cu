@@ -478,11 +478,12 @@ __global__ void __launch_bounds__(kBlock, 1)
 }
 
 // ----------------------------------------------------------- gather ----
-// xs[p] = x[sorted_token[p]] for p < group_offsets[E]; 16-byte vectors.
+// xs[p] = x[sorted_token[p]] for p < min(*total_rows, max_rows) (all
+// max_rows rows when total_rows is null); 16-byte vectors.
 __global__ void gather_rows_kernel(const uint4* __restrict__ x, const int32_t* __restrict__ sorted_token,
                                    const int32_t* __restrict__ total_rows, int64_t max_rows,
                                    int vec_per_row, uint4* __restrict__ xs) {
-  const int64_t tr = *total_rows;
+  const int64_t tr = total_rows != nullptr ? *total_rows : max_rows;
   const int64_t rows = tr < max_rows ? tr : max_rows;
   const int64_t n = rows * vec_per_row;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
@@ -494,10 +495,11 @@ __global__ void gather_rows_kernel(const uint4* __restrict__ x, const int32_t* _
 }
 
 // ---------------------------------------------------------- combine ----
-// out[t][8c..8c+7] = bf16( Σ_j f32(w[t][j]) * f32(ys[inv_pos[t*k+j]][8c..]) ).
+// Σ_j f32(w[t][j]) * f32(ys[inv_pos[t*k+j]][8c..8c+7]) in slot order j, as
+// bf16 (out_f32 == 0) or fp32 (out_f32 == 1) into row t of out.
 __global__ void combine_kernel(const uint4* __restrict__ ys, const int32_t* __restrict__ inv_pos,
                                const __nv_bfloat16* __restrict__ w, int64_t T, int k,
-                               int vec_per_row, uint4* __restrict__ out) {
+                               int vec_per_row, int out_f32, void* __restrict__ out) {
   const int64_t n = T * vec_per_row;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -516,6 +518,12 @@ __global__ void combine_kernel(const uint4* __restrict__ ys, const int32_t* __re
         acc[2 * q + 1] = fmaf(wj, __uint_as_float(words[q] & 0xFFFF0000u), acc[2 * q + 1]);
       }
     }
+    if (out_f32) {
+      float4* o = static_cast<float4*>(out) + 2 * i;
+      o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+      continue;
+    }
     uint4 o;
     uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
@@ -523,7 +531,7 @@ __global__ void combine_kernel(const uint4* __restrict__ ys, const int32_t* __re
       const __nv_bfloat162 b = __floats2bfloat162_rn(acc[2 * q], acc[2 * q + 1]);
       ow[q] = *reinterpret_cast<const uint32_t*>(&b);
     }
-    out[i] = o;
+    static_cast<uint4*>(out)[i] = o;
   }
 }
 
@@ -674,13 +682,13 @@ int launch_gather(const void* x, const int32_t* sorted_token, const int32_t* tot
 }
 
 int launch_combine(const void* ys, const int32_t* inv_pos, const void* w, int64_t T, int k,
-                   int64_t D, void* out, cudaStream_t stream) {
+                   int64_t D, void* out, cudaStream_t stream, bool out_f32) {
   KW8_REQUIRE(D % 8 == 0, KW8_ERR_UNSUPPORTED, "D must be a multiple of 8");
   if (T <= 0) return KW8_OK;
   const int vec = static_cast<int>(D / 8);
   combine_kernel<<<grid_for(T * vec, 256, 148 * 16), 256, 0, stream>>>(
       static_cast<const uint4*>(ys), inv_pos, static_cast<const __nv_bfloat16*>(w), T, k, vec,
-      static_cast<uint4*>(out));
+      out_f32 ? 1 : 0, out);
   KW8_CHECK_LAUNCH();
   return KW8_OK;
 }

@@ -41,7 +41,8 @@ int launch_build_tiles(const int32_t* group_offsets, int64_t E, int nt, TileEntr
                        int32_t* num_tiles, cudaStream_t stream);
 int launch_gather(const void* x, const int32_t* sorted_token, const int32_t* total_rows,
                   int64_t max_rows, int64_t D, void* xs, cudaStream_t stream);
+// out [T][D]: bf16, or fp32 with out_f32 (the k rows summed in slot order).
 int launch_combine(const void* ys, const int32_t* inv_pos, const void* w, int64_t T, int k,
-                   int64_t D, void* out, cudaStream_t stream);
+                   int64_t D, void* out, cudaStream_t stream, bool out_f32 = false);
 
 }  // namespace kw8

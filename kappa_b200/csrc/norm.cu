@@ -1,0 +1,186 @@
+// RMSNorm (kappa/gemma3/norms.py:8-13 with Gemma's (1 + scale),
+// kappa/qwen3/norms.py:10-16 with Qwen's scale) and the residual epilogue of
+// the FFN sub-block (kappa/gemma3/block.py:73-82, kappa/qwen3/block.py:68-81).
+//
+// A CTA per row.  The row is read once into registers (8-wide vectors),
+// the sum of squares is reduced over the CTA in fp32, and the row is written
+// once.  Rounding follows kappa: the norm computes in fp32 and rounds its
+// output to the activation dtype once; the FFN output is rounded to bf16
+// before the post-FFN norm, and the residual add rounds once more.
+#include "norm.cuh"
+
+namespace kw8 {
+
+namespace {
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();  // red may still be read by an earlier call
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float s = 0.f;
+#pragma unroll
+  for (int w = 0; w < kNormThreads / 32; ++w) s += red[w];  // same order in every thread
+  return s;
+}
+
+__device__ __forceinline__ void bf16x8_to_f32(const uint4& v, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+__device__ __forceinline__ uint4 f32x8_to_bf16(const float (&f)[8]) {
+  uint4 o;
+  uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 b = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+    ow[i] = *reinterpret_cast<const uint32_t*>(&b);
+  }
+  return o;
+}
+
+// g[d] of the norm: 1 + scale (Gemma) or scale (Qwen), in fp32.
+__device__ __forceinline__ float norm_gain(const void* scale, int dtype, int kind, int64_t d) {
+  const float s = load_scale(scale, dtype, d);
+  return kind == KW8_NORM_GEMMA ? 1.0f + s : s;
+}
+
+// v (this thread's nv vectors of the row, fp32) <- (v * r) * g, r from the
+// row's mean square.
+__device__ __forceinline__ void rms_apply(float (&v)[kNormMaxVec][8], int nv, int64_t D,
+                                          const void* scale, int dtype, int kind, float eps,
+                                          float* red) {
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < kNormMaxVec; ++j)
+    if (j < nv)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss = fmaf(v[j][i], v[j][i], ss);
+  const float total = block_sum(ss, red);
+  const float r = rsqrtf(__fdiv_rn(total, static_cast<float>(D)) + eps);
+#pragma unroll
+  for (int j = 0; j < kNormMaxVec; ++j) {
+    if (j >= nv) continue;
+    const int64_t d0 = (static_cast<int64_t>(j) * kNormThreads + threadIdx.x) * 8;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[j][i] = __fmul_rn(__fmul_rn(v[j][i], r), norm_gain(scale, dtype, kind, d0 + i));
+  }
+}
+
+__global__ void __launch_bounds__(kNormThreads)
+    rms_norm_kernel(const uint4* __restrict__ x, int64_t D, const void* __restrict__ scale, int dtype,
+                    int kind, float eps, uint4* __restrict__ out) {
+  __shared__ float red[kNormThreads / 32];
+  const int64_t vec = D / 8;
+  const int nv = static_cast<int>((vec - threadIdx.x + kNormThreads - 1) / kNormThreads);
+  const uint4* xr = x + blockIdx.x * vec;
+  float v[kNormMaxVec][8];
+#pragma unroll
+  for (int j = 0; j < kNormMaxVec; ++j)
+    if (j < nv) bf16x8_to_f32(xr[j * kNormThreads + threadIdx.x], v[j]);
+  rms_apply(v, nv, D, scale, dtype, kind, eps, red);
+  uint4* orow = out + blockIdx.x * vec;
+#pragma unroll
+  for (int j = 0; j < kNormMaxVec; ++j)
+    if (j < nv) orow[j * kNormThreads + threadIdx.x] = f32x8_to_bf16(v[j]);
+}
+
+__global__ void __launch_bounds__(kNormThreads)
+    block_finish_kernel(const float4* __restrict__ part, int splits, int64_t stride4, int64_t D,
+                        const void* __restrict__ scale, int dtype, int kind, float eps,
+                        const uint4* __restrict__ h, uint4* __restrict__ out) {
+  __shared__ float red[kNormThreads / 32];
+  const int64_t vec = D / 8;
+  const int nv = static_cast<int>((vec - threadIdx.x + kNormThreads - 1) / kNormThreads);
+  float v[kNormMaxVec][8];
+#pragma unroll
+  for (int j = 0; j < kNormMaxVec; ++j) {
+    if (j >= nv) continue;
+    const int64_t e4 = (blockIdx.x * vec + j * kNormThreads + threadIdx.x) * 2;  // float4 index
+    float4 a = part[e4], b = part[e4 + 1];
+    for (int s = 1; s < splits; ++s) {
+      const float4 c = part[s * stride4 + e4], d = part[s * stride4 + e4 + 1];
+      a.x += c.x; a.y += c.y; a.z += c.z; a.w += c.w;
+      b.x += d.x; b.y += d.y; b.z += d.z; b.w += d.w;
+    }
+    const float f[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[j][i] = __bfloat162float(__float2bfloat16_rn(f[i]));  // the FFN output in bf16
+  }
+  if (scale != nullptr) {
+    rms_apply(v, nv, D, scale, dtype, kind, eps, red);
+#pragma unroll
+    for (int j = 0; j < kNormMaxVec; ++j)
+      if (j < nv)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[j][i] = __bfloat162float(__float2bfloat16_rn(v[j][i]));
+  }
+#pragma unroll
+  for (int j = 0; j < kNormMaxVec; ++j) {
+    if (j >= nv) continue;
+    const int64_t e = blockIdx.x * vec + j * kNormThreads + threadIdx.x;
+    if (h != nullptr) {
+      float hv[8];
+      bf16x8_to_f32(h[e], hv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[j][i] = __fadd_rn(hv[i], v[j][i]);
+    }
+    out[e] = f32x8_to_bf16(v[j]);
+  }
+}
+
+int check_norm(int64_t T, int64_t D, int scale_dtype, int kind, float eps) {
+  KW8_REQUIRE(T >= 0 && D >= 8 && D % 8 == 0 && D <= kNormMaxD, KW8_ERR_UNSUPPORTED,
+              "RMSNorm rows need D %% 8 == 0 and 8 <= D <= %lld (D=%lld)", (long long)kNormMaxD,
+              (long long)D);
+  KW8_REQUIRE(T < (1ll << 31), KW8_ERR_UNSUPPORTED, "too many rows");
+  KW8_REQUIRE(scale_dtype == KW8_DT_F32 || scale_dtype == KW8_DT_BF16, KW8_ERR_INVALID_ARG,
+              "norm scale dtype must be f32 or bf16");
+  KW8_REQUIRE(kind == KW8_NORM_GEMMA || kind == KW8_NORM_QWEN, KW8_ERR_INVALID_ARG, "unknown norm kind %d",
+              kind);
+  KW8_REQUIRE(eps >= 0.f, KW8_ERR_INVALID_ARG, "eps must be >= 0");
+  return KW8_OK;
+}
+
+}  // namespace
+
+int launch_rms_norm(const void* x, int64_t T, int64_t D, const void* scale, int scale_dtype, int kind,
+                    float eps, void* out, cudaStream_t stream) {
+  KW8_REQUIRE(x && scale && out, KW8_ERR_INVALID_ARG, "null pointer");
+  int rc = check_norm(T, D, scale_dtype, kind, eps);
+  if (rc) return rc;
+  KW8_REQUIRE(((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15) == 0,
+              KW8_ERR_UNSUPPORTED, "RMSNorm rows must be 16-byte aligned");
+  if (T == 0) return KW8_OK;
+  rms_norm_kernel<<<static_cast<unsigned>(T), kNormThreads, 0, stream>>>(
+      static_cast<const uint4*>(x), D, scale, scale_dtype, kind, eps, static_cast<uint4*>(out));
+  KW8_CHECK_LAUNCH();
+  return KW8_OK;
+}
+
+int launch_block_finish(const float* part, int splits, int64_t split_stride, int64_t T, int64_t D,
+                        const void* post_scale, int scale_dtype, int kind, float eps, const void* h,
+                        void* out, cudaStream_t stream) {
+  KW8_REQUIRE(part && out && splits >= 1, KW8_ERR_INVALID_ARG, "null pointer");
+  int rc = check_norm(T, D, scale_dtype, kind, eps);
+  if (rc) return rc;
+  KW8_REQUIRE(split_stride % 4 == 0 &&
+                  ((reinterpret_cast<uintptr_t>(part) | reinterpret_cast<uintptr_t>(out) |
+                    reinterpret_cast<uintptr_t>(h)) & 15) == 0,
+              KW8_ERR_UNSUPPORTED, "block epilogue rows must be 16-byte aligned");
+  if (T == 0) return KW8_OK;
+  block_finish_kernel<<<static_cast<unsigned>(T), kNormThreads, 0, stream>>>(
+      reinterpret_cast<const float4*>(part), splits, split_stride / 4, D, post_scale, scale_dtype, kind, eps,
+      static_cast<const uint4*>(h), static_cast<uint4*>(out));
+  KW8_CHECK_LAUNCH();
+  return KW8_OK;
+}
+
+}  // namespace kw8

@@ -109,7 +109,66 @@ __global__ void dequant_kernel(const int8_t* __restrict__ q, const void* __restr
   }
 }
 
+// gather_embed_tokens: out[i][d] = dt(q[row][d]) * dt(s) for row = tokens[i]
+// normalised like a JAX gather (negative ids count from the end, then the
+// id is clamped into [0, V)).  One rounding per product, as dequant_kernel.
+// A thread per 8 outputs (8 int8 in, 8 bf16 / fp32 out).
+__global__ void embed_gather_kernel(const int32_t* __restrict__ tokens, int64_t n,
+                                    const int8_t* __restrict__ q, const void* __restrict__ scale,
+                                    int scale_dtype, int per_channel, int64_t V, int64_t D,
+                                    int out_dtype, void* __restrict__ out) {
+  const int64_t vec = D / 8;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n * vec;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = i / vec, c = i - t * vec;
+    int64_t row = tokens[t];
+    if (row < 0) row += V;
+    row = row < 0 ? 0 : (row >= V ? V - 1 : row);
+    float s = load_scale(scale, scale_dtype, per_channel ? row : 0);
+    if (out_dtype == KW8_DT_BF16) s = __bfloat162float(__float2bfloat16_rn(s));
+    const uint2 w = *reinterpret_cast<const uint2*>(q + row * D + c * 8);
+    const uint32_t words[2] = {w.x, w.y};
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      v[j] = static_cast<float>(static_cast<int8_t>((words[j >> 2] >> (8 * (j & 3))) & 0xFFu)) * s;
+    if (out_dtype == KW8_DT_F32) {
+      float4* o = reinterpret_cast<float4*>(static_cast<float*>(out) + t * D + c * 8);
+      o[0] = make_float4(v[0], v[1], v[2], v[3]);
+      o[1] = make_float4(v[4], v[5], v[6], v[7]);
+    } else {
+      uint4 o;
+      uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const __nv_bfloat162 b = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+        ow[j] = *reinterpret_cast<const uint32_t*>(&b);
+      }
+      *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out) + t * D + c * 8) = o;
+    }
+  }
+}
+
 }  // namespace
+
+int launch_embed_gather(const int32_t* tokens, int64_t n, const kw8_weight& table, int64_t V,
+                        int64_t D, int out_dtype, void* out, cudaStream_t stream) {
+  KW8_REQUIRE(tokens && table.q && table.scale && out, KW8_ERR_INVALID_ARG, "null pointer");
+  KW8_REQUIRE(n >= 0 && V >= 1 && D >= 1, KW8_ERR_INVALID_ARG, "bad shape (n=%lld V=%lld D=%lld)",
+              (long long)n, (long long)V, (long long)D);
+  KW8_REQUIRE(out_dtype == KW8_DT_F32 || out_dtype == KW8_DT_BF16, KW8_ERR_INVALID_ARG,
+              "out dtype must be f32 or bf16");
+  KW8_REQUIRE(D % 8 == 0 && (reinterpret_cast<uintptr_t>(table.q) & 7) == 0 &&
+                  (reinterpret_cast<uintptr_t>(out) & 15) == 0,
+              KW8_ERR_UNSUPPORTED, "embedding rows need D %% 8 == 0 and aligned buffers");
+  if (n == 0) return KW8_OK;
+  int64_t blocks = (n * (D / 8) + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  embed_gather_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+      tokens, n, table.q, table.scale, table.scale_dtype, table.per_channel, V, D, out_dtype, out);
+  KW8_CHECK_LAUNCH();
+  return KW8_OK;
+}
 
 size_t quantize_workspace_size(int64_t outer, int64_t N) {
   return static_cast<size_t>(outer * N + 4) * sizeof(float);

@@ -30,6 +30,7 @@ __all__ = [
     "to_compute_dtype",
     "quantize_weight",
     "kmajor",
+    "gather_embed_tokens",
 ]
 
 
@@ -199,3 +200,30 @@ def to_compute_dtype(w: Weight, dtype: torch.dtype, *, in_axis: int = -2) -> tor
             _lib.load().kw8_dequantize(km.struct(), groups, N, K, _DT[dtype], out.data_ptr(), _lib.stream_of(out))
         )
     return out.transpose(-1, -2) if _norm_axis(in_axis, out.dim()) == -2 else out
+
+
+def gather_embed_tokens(tokens: torch.Tensor, embed: Weight, *, compute_dtype: torch.dtype) -> torch.Tensor:
+    """kappa/qwen3/quant.py:51-57 for a W8 table ``[vocab, model_dim]``.
+
+    Only the gathered rows are dequantised: ``values[t].astype(dt) *
+    scale.astype(dt)`` with one rounding per product (``kw8_embed_gather``).
+    Ids follow JAX's gather: negative ids count from the end, then ids are
+    clamped into ``[0, vocab)``.  A per-channel table has one scale per row.
+    """
+    if not is_q8_weight(embed):
+        raise TypeError("embed: kappa_b200 implements the W8 path; quantize the table first")
+    if compute_dtype not in _DT:
+        raise ValueError(f"gather_embed_tokens: unsupported compute dtype {compute_dtype}")
+    km = kmajor(embed, -1, "embed")
+    if km.q.dim() != 2:
+        raise ValueError(f"embed must be [vocab, model_dim], got {tuple(embed.values.shape)}")
+    V, D = (int(s) for s in km.q.shape)
+    _lib.require_cuda(tokens, "tokens")
+    t = tokens.to(torch.int32).contiguous()
+    out = torch.empty(tuple(tokens.shape) + (D,), dtype=compute_dtype, device=tokens.device)
+    _lib.check(
+        _lib.load().kw8_embed_gather(
+            t.data_ptr(), t.numel(), km.struct(), V, D, _DT[compute_dtype], out.data_ptr(), _lib.stream_of(t)
+        )
+    )
+    return out

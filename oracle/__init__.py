@@ -24,6 +24,17 @@ from oracle.kappa_ref import (  # noqa: F401
     Q8Weight,
     bf16_round,
     feed_forward,
+    gather_embed_tokens,
+    gemma_ffn_sub_block,
+    linear_f32,
+    logits_from_hidden,
+    logits_from_hidden_last_positions,
+    project_attn_out,
+    project_kv,
+    project_q,
+    qwen_dense_sub_block,
+    qwen_moe_sub_block_f32,
+    rms_norm,
     fixed_capacity_slots,
     fixed_capacity_value,
     moe_fixed_capacity,

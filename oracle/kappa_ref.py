@@ -395,3 +395,120 @@ def moe_reference_f32(x, router_w, ffn_gate, ffn_up, ffn_down, *, num_experts: i
     y = moe_ragged(x_flat, idx, w, ffn_gate, ffn_up, ffn_down, num_experts=num_experts, b=b, t=t, d=d,
                    capacity=capacity, combine_dtype=np.float32)
     return y, idx, w
+
+
+# --------------------------------------------------------------------------
+# Neighbours of the FFN: norms, attention projections, embedding, LM head
+# --------------------------------------------------------------------------
+
+
+def rms_norm(x, scale, *, gemma: bool, epsilon: float = 1e-6, out_dtype=None) -> np.ndarray:
+    """kappa/gemma3/norms.py:8-13 (``gemma=True``: ``* (1 + scale)``) and
+    kappa/qwen3/norms.py:10-16 (``gemma=False``: ``* scale``), in fp32,
+    rounded to ``out_dtype`` (x's dtype by default)."""
+    x = np.asarray(x)
+    out_dtype = np.dtype(out_dtype) if out_dtype is not None else x.dtype
+    xf = x.astype(np.float32)
+    var = np.mean(xf * xf, axis=-1, keepdims=True, dtype=np.float32).astype(np.float32)
+    r = (np.float32(1.0) / np.sqrt(var + np.float32(epsilon))).astype(np.float32)
+    s = np.asarray(scale).astype(np.float32)
+    g = (np.float32(1.0) + s) if gemma else s
+    return ((xf * r).astype(np.float32) * g).astype(np.float32).astype(out_dtype)
+
+
+def linear_f32(x2d, w_kmajor: Q8Weight) -> np.ndarray:
+    """The fp32 dequantise-then-dot reference of one W8 linear layer:
+    ``x [T, K] . dequant(w)^T`` with ``w`` K-major ``[N, K]`` (scale broadcast
+    over K), fp32 throughout."""
+    wf = to_compute_dtype(w_kmajor, F32)
+    return np.matmul(np.asarray(x2d).astype(np.float32), wf.T).astype(np.float32)
+
+
+def project_q(x, q_w, *, compute_dtype=BF16) -> np.ndarray:
+    """kappa/qwen3/linear.py:11-13: ``einsum("btd,ndh->btnh", x, dequant(q_w))``."""
+    dt = np.dtype(compute_dtype)
+    w = to_compute_dtype(q_w, dt).astype(np.float32)
+    return np.einsum("btd,ndh->btnh", np.asarray(x).astype(np.float32), w).astype(np.float32).astype(dt)
+
+
+def project_kv(x, k_w, v_w, *, compute_dtype=BF16):
+    """kappa/qwen3/linear.py:16-20."""
+    return project_q(x, k_w, compute_dtype=compute_dtype), project_q(x, v_w, compute_dtype=compute_dtype)
+
+
+def project_attn_out(encoded, o_w, *, compute_dtype=BF16) -> np.ndarray:
+    """kappa/qwen3/linear.py:23-25: ``einsum("btnh,nhd->btd", encoded, dequant(o_w))``."""
+    dt = np.dtype(compute_dtype)
+    w = to_compute_dtype(o_w, dt).astype(np.float32)
+    return np.einsum("btnh,nhd->btd", np.asarray(encoded).astype(np.float32), w).astype(np.float32).astype(dt)
+
+
+def gather_embed_tokens(tokens, embed: Q8Weight, *, compute_dtype) -> np.ndarray:
+    """kappa/qwen3/quant.py:51-57 for a W8 table ``[V, D]``: the gathered
+    int8 rows times the scale, one rounding per product.  Ids follow JAX's
+    gather (``embed.values[t]``): a negative id counts from the end, then
+    ids are clamped into [0, V)."""
+    dt = np.dtype(compute_dtype)
+    V = embed.values.shape[0]
+    t = np.asarray(tokens, dtype=np.int64)
+    t = np.where(t < 0, t + V, t)
+    t = np.clip(t, 0, V - 1)
+    rows = embed.values[t]
+    s = np.asarray(embed.scale)
+    if s.ndim == embed.values.ndim:  # one scale per row
+        s = s[t]
+    return rows.astype(dt) * s.astype(dt)
+
+
+def logits_from_hidden(x, lm_head: Q8Weight, *, compute_dtype=BF16) -> np.ndarray:
+    """kappa/qwen3/transformer.py:55-59: ``einsum("btd,vd->btv")`` in x's dtype."""
+    dt = np.dtype(compute_dtype)
+    w = to_compute_dtype(lm_head, dt).astype(np.float32)
+    return np.einsum("btd,vd->btv", np.asarray(x).astype(np.float32), w).astype(np.float32).astype(dt)
+
+
+def logits_from_hidden_last_positions(x, w: Q8Weight, last_idx, *, compute_dtype=BF16) -> np.ndarray:
+    """kappa/qwen3/transformer.py:68-75 (``x[rows, last_idx]`` with JAX's
+    negative-index and clamping rules)."""
+    x = np.asarray(x)
+    b, L = x.shape[:2]
+    li = np.asarray(last_idx, dtype=np.int64)
+    li = np.clip(np.where(li < 0, li + L, li), 0, L - 1)
+    h = x[np.arange(b), li]
+    dt = np.dtype(compute_dtype)
+    wf = to_compute_dtype(w, dt).astype(np.float32)
+    return np.einsum("bd,vd->bv", h.astype(np.float32), wf).astype(np.float32).astype(dt)
+
+
+def gemma_ffn_sub_block(h, pre_scale, gating_w, linear_w, post_scale=None, *, transpose_gating_einsum=True,
+                        compute_dtype=BF16, epsilon: float = 1e-6) -> np.ndarray:
+    """kappa/gemma3/block.py:73-82: ``h + rms_norm?(feed_forward(rms_norm(h, pre)))``
+    with bf16 results between the steps (``compute_dtype`` as feed_forward)."""
+    h = np.asarray(h)
+    xn = rms_norm(h, pre_scale, gemma=True, epsilon=epsilon)
+    out = feed_forward(xn, gating_w, linear_w, transpose_gating_einsum=transpose_gating_einsum,
+                       compute_dtype=compute_dtype).astype(np.float32).astype(BF16)
+    if post_scale is not None:
+        out = rms_norm(out, post_scale, gemma=True, epsilon=epsilon)
+    return (h.astype(np.float32) + out.astype(np.float32)).astype(BF16)
+
+
+def qwen_dense_sub_block(h, pre_scale, gate_w, up_w, down_w, *, compute_dtype=BF16, epsilon: float = 1e-6):
+    """kappa/qwen3/block.py:68-81 for a dense block: ``h + swiglu_ffn(rms_norm(h))``."""
+    h = np.asarray(h)
+    xn = rms_norm(h, pre_scale, gemma=False, epsilon=epsilon)
+    out = swiglu_ffn(xn, gate_w, up_w, down_w, compute_dtype=compute_dtype).astype(np.float32).astype(BF16)
+    return (h.astype(np.float32) + out.astype(np.float32)).astype(BF16)
+
+
+def qwen_moe_sub_block_f32(h, pre_scale, router_w, ffn_gate, ffn_up, ffn_down, *, num_experts: int, k: int,
+                           epsilon: float = 1e-6, idx=None, w=None):
+    """kappa/qwen3/block.py:68-81 for an MoE block with the fp32 reference of
+    the MoE layer (moe_reference_f32): the normed input is bf16, the layer
+    output is rounded to bf16, then ``h +`` in bf16.  Returns (out, idx, w)."""
+    h = np.asarray(h)
+    xn = rms_norm(h, pre_scale, gemma=False, epsilon=epsilon)
+    y, idx, w = moe_reference_f32(xn, router_w, ffn_gate, ffn_up, ffn_down, num_experts=num_experts, k=k,
+                                  idx=idx, w=w)
+    out = (h.astype(np.float32) + y.astype(BF16).astype(np.float32)).astype(BF16)
+    return out, idx, w, xn

@@ -252,6 +252,21 @@ def test_qwen_swiglu_ffn(path):
     parity(y, O.swiglu_ffn(x, *o), tol=KAPPA_BF16_TOL)
 
 
+@pytest.mark.parametrize("T", [7, 100])
+def test_qwen3_4b_swiglu_ffn(T):
+    """Qwen3-4B dense MLP shape (kappa/qwen3/architecture.py:82-83): D=2560,
+    I=9728 (a multiple of 16 but not of 128: the down projection's last k
+    stage is partial), kappa's per-tensor bf16 scales."""
+    rng = np.random.default_rng(T)
+    D, I = 2560, 9728
+    x = normal(rng, (1, T, D)).astype(O.BF16)
+    ws = [normal(rng, s, 0.02) for s in ((D, I), (D, I), (I, D))]
+    g = [_gpu_q(w, False, scale_dtype=torch.bfloat16) for w in ws]
+    o = [_oracle_q(w, False, scale_dtype=O.BF16) for w in ws]
+    y = to_np(swiglu_ffn(to_dev(x), *g))
+    parity(y, O.swiglu_ffn(x, *o, compute_dtype=np.float32))
+
+
 # ------------------------------------------------------------------- MoE ----
 
 

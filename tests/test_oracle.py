@@ -152,3 +152,31 @@ def test_regression_vectors():
     np.testing.assert_array_equal(idx, z["moe_idx"])
     y = O.moe_ragged(x_flat, idx, w, qg, qu, qd, num_experts=E, b=b, t=t, d=d)
     np.testing.assert_array_equal(y.view(np.uint16), z["moe_y"])
+
+
+def test_gather_embed_index_rules():
+    """gather_embed_tokens follows JAX's gather: negative ids count from the
+    end, out-of-range ids clamp (kappa/qwen3/quant.py:51-57 indexes
+    ``embed.values[t]``)."""
+    V, D = 6, 4
+    vals = (np.arange(V * D, dtype=np.int64) % 200 - 100).astype(np.int8).reshape(V, D)
+    w = O.Q8Weight(vals, np.asarray(0.5, dtype=O.BF16))
+    tokens = np.array([0, 5, -1, -6, -7, 6, 100], dtype=np.int32)
+    got = O.gather_embed_tokens(tokens, w, compute_dtype=np.float32)
+    rows = [0, 5, 5, 0, 0, 5, 5]
+    np.testing.assert_array_equal(got, vals[rows].astype(np.float32) * 0.5)
+
+
+def test_rms_norm_matches_its_formula():
+    """kappa's two RMSNorm flavours against a float64 evaluation (within one
+    bf16 step), and Gemma's (1 + scale) against Qwen's scale."""
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((5, 64)).astype(np.float32).astype(O.BF16)
+    s = (rng.standard_normal(64) * 0.3).astype(np.float32)
+    x64 = x.astype(np.float64)
+    r = 1.0 / np.sqrt(np.mean(x64 * x64, axis=-1, keepdims=True) + 1e-6)
+    for gemma, g in ((True, 1.0 + s.astype(np.float64)), (False, s.astype(np.float64))):
+        got = O.rms_norm(x, s, gemma=gemma).astype(np.float32)
+        want = x64 * r * g
+        assert np.all(np.abs(got - want) <= 2.0 ** -7 * np.abs(want) + 1e-30)
+    np.testing.assert_array_equal(O.rms_norm(x, s, gemma=True), O.rms_norm(x, 1.0 + s, gemma=False))
