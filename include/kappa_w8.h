@@ -388,6 +388,11 @@ typedef struct kw8_ep_peers {
   void* own_ret;
   int32_t ret_f32; /* partial sums in ret as fp32 (ret rows of 4*D bytes)
                       instead of bf16 (2*D bytes)                            */
+  /* Exchange buffer of the one-shot sums (kw8_moe_ffn_ep_decode,
+   * kw8_dense_ffn_tp): fp32 [2][world][red_rows][D] in every rank.         */
+  const uint64_t* red;
+  float* own_red;
+  int64_t red_rows;
 } kw8_ep_peers;
 
 /* The expert-parallel MoE layer over this rank's T <= max_tokens tokens in
@@ -409,6 +414,35 @@ int kw8_moe_ffn_ep(const void* x, int64_t T, int64_t D, int64_t I, int64_t E, in
                    kw8_weight up_local, kw8_weight down_local, void* out,
                    const kw8_ep_peers* peers, uint32_t epoch, void* workspace,
                    size_t workspace_bytes, kw8_stream_t stream);
+
+/* The expert-parallel MoE layer for a batch that every rank holds (decode,
+ * kappa's moe_swiglu_ffn at small B*T), in one call: every rank routes all
+ * T <= red_rows tokens (the same fp32 logits and top-k everywhere), runs
+ * its own E/world experts' rows with the fused weighted combine into an
+ * fp32 partial [T][D], stores that partial into every rank's exchange
+ * buffer (peers->red, slot [epoch & 1][rank]), passes flag phase 1 of
+ * `epoch`, and sums the world partials in rank order into out (bf16; every
+ * rank gets the same bits).  Needs peers->red and peers->flags only.  No
+ * counterpart in kappa, which replicates every expert.                     */
+size_t kw8_moe_ffn_ep_decode_workspace_size(int64_t T, int64_t D, int64_t I, int64_t E, int32_t k);
+int kw8_moe_ffn_ep_decode(const void* x, int64_t T, int64_t D, int64_t I, int64_t E, int32_t k,
+                          int64_t capacity, kw8_weight router, kw8_weight gate_local,
+                          kw8_weight up_local, kw8_weight down_local, void* out,
+                          const kw8_ep_peers* peers, uint32_t epoch, void* workspace,
+                          size_t workspace_bytes, kw8_stream_t stream);
+
+/* Tensor-parallel dense FFN (the column/row split of kappa/qwen3/sharding.py:
+ * 127-132, which kappa leaves to GSPMD) in one call: this rank's gate/up
+ * shards ([H_local][D] each) and down shard ([D][H_local]) give an fp32
+ * partial of the layer output; the partials are summed over the group like
+ * kw8_moe_ffn_ep_decode's (peers->red, phase 1 of `epoch`) into out (bf16,
+ * the same bits on every rank).  x [T][D] bf16 (the same on every rank),
+ * T <= red_rows.                                                            */
+size_t kw8_dense_ffn_tp_workspace_size(int64_t T, int64_t D, int64_t H_local);
+int kw8_dense_ffn_tp(const void* x, int64_t T, int64_t D, int64_t H_local, kw8_weight gate,
+                     kw8_weight up, kw8_weight down, int32_t act, void* out,
+                     const kw8_ep_peers* peers, uint32_t epoch, void* workspace,
+                     size_t workspace_bytes, kw8_stream_t stream);
 
 /* Phase `phase` (0..2) of the group barrier: with `signal` this rank first
  * marks the phase done at every peer; then it waits (bounded) until every

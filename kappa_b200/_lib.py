@@ -95,6 +95,9 @@ class KW8EpPeers(ctypes.Structure):
         ("own_meta", ctypes.c_void_p),
         ("own_ret", ctypes.c_void_p),
         ("ret_f32", ctypes.c_int32),
+        ("red", ctypes.c_void_p),
+        ("own_red", ctypes.c_void_p),
+        ("red_rows", ctypes.c_int64),
     ]
 
 
@@ -153,6 +156,18 @@ SIGNATURES: dict[str, tuple] = {
         ctypes.c_int,
         [_vp, _i64, _i64, _i64, _i64, _i32, _i64, KW8Weight, KW8Weight, KW8Weight, KW8Weight, _vp,
          ctypes.POINTER(KW8EpPeers), ctypes.c_uint32, _vp, _sz, _vp],
+    ),
+    "kw8_moe_ffn_ep_decode_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i32]),
+    "kw8_moe_ffn_ep_decode": (
+        ctypes.c_int,
+        [_vp, _i64, _i64, _i64, _i64, _i32, _i64, KW8Weight, KW8Weight, KW8Weight, KW8Weight, _vp,
+         ctypes.POINTER(KW8EpPeers), ctypes.c_uint32, _vp, _sz, _vp],
+    ),
+    "kw8_dense_ffn_tp_workspace_size": (_sz, [_i64, _i64, _i64]),
+    "kw8_dense_ffn_tp": (
+        ctypes.c_int,
+        [_vp, _i64, _i64, _i64, KW8Weight, KW8Weight, KW8Weight, _i32, _vp, ctypes.POINTER(KW8EpPeers),
+         ctypes.c_uint32, _vp, _sz, _vp],
     ),
     "kw8_ep_barrier": (ctypes.c_int, [ctypes.POINTER(KW8EpPeers), _i32, ctypes.c_uint32, _i32, _vp]),
     "kw8_moe_permute_ws": (ctypes.c_int, [_vp, _i64, _i32, _i64, _i64, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]),

@@ -282,17 +282,21 @@ int expert_ffn(bool streamed, const void* x, const int32_t* row_index, int64_t r
                int64_t I, int64_t E, const int32_t* group_offsets, const kw8_weight& gate,
                const kw8_weight& up, const kw8_weight& down, void* ys, const ExpertBuffers& b,
                cudaStream_t stream, const int32_t* row_token = nullptr,
-               const float* row_weight = nullptr, const int32_t* active = nullptr) {
+               const float* row_weight = nullptr, const int32_t* active = nullptr,
+               int64_t tile_rows = -1) {
+  // tile_rows: the rows the E groups hold together, for the tile choice,
+  // when `rows` (the extent of the row buffers) counts other groups' rows too.
+  const int64_t hint = tile_rows >= 0 ? tile_rows : rows;
   const int mode = row_token != nullptr ? EPI_COMBINE_F32 : EPI_PLAIN_BF16;
   if (streamed) {
-    const int nt = stream_nt(rows_hint(rows, E));
+    const int nt = stream_nt(rows_hint(hint, E));
     StreamArgs g = stream_args(gate, &up);
     g.group_offsets = group_offsets;
     g.active_groups = active;
     g.row_index = row_index;
     g.out = b.h;
     g.ld_out = I;
-    int rc = launch_gemm_stream(EPI_PAIR_SILU, gate.q, up.q, E, I, D, x, D, rows, nt, g, stream);
+    int rc = launch_gemm_stream(EPI_PAIR_SILU, gate.q, up.q, E, I, D, x, D, hint, nt, g, stream);
     if (rc) return rc;
     StreamArgs d = stream_args(down, nullptr);
     d.group_offsets = group_offsets;
@@ -302,10 +306,10 @@ int expert_ffn(bool streamed, const void* x, const int32_t* row_index, int64_t r
     d.row_token = row_token;
     d.row_weight = row_weight;
     d.kz_max = kStreamMaxKz;  // used by the combine mode only (its atomics add the K ranges)
-    return launch_gemm_stream(mode, down.q, nullptr, E, D, I, b.h, I, rows, nt, d, stream);
+    return launch_gemm_stream(mode, down.q, nullptr, E, D, I, b.h, I, hint, nt, d, stream);
   }
   KW8_REQUIRE(row_index == nullptr, KW8_ERR_INVALID_ARG, "tensor-core path takes gathered rows");
-  const int nt = pick_nt(rows, E);
+  const int nt = pick_nt(hint, E);
   int rc = launch_build_tiles(group_offsets, E, nt, b.tiles, b.num_tiles, stream);
   if (rc) return rc;
   GemmArgs g = base_args(gate, &up);
@@ -611,7 +615,7 @@ extern "C" {
 
 const char* kw8_last_error(void) { return kw8::last_error(); }
 
-int32_t kw8_abi_version(void) { return 1; }
+int32_t kw8_abi_version(void) { return 2; }
 
 int kw8_device_status(int32_t* status_out, kw8_stream_t stream) {
   KW8_API_BEGIN

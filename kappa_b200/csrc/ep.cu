@@ -181,6 +181,50 @@ __global__ void ep_counts_kernel(const int32_t* __restrict__ sizes, int E, const
   __syncthreads();
 }
 
+// ------------------------------------------- one-shot partial-sum exchange --
+// A group whose ranks each hold an fp32 partial [T][D] of the same output
+// (tensor-parallel dense FFN, expert-parallel decode) sums it over NVLink:
+// every rank stores its partial (the sum of its `splits` K-split slices)
+// into slot [parity][rank] of every rank's exchange buffer, the group passes
+// one flag phase, and every rank adds the world slots in rank order (the
+// same order everywhere, so every rank gets the same bits).  parity =
+// epoch & 1: a rank can start call e + 1 while a slower one still reads the
+// slots of call e, but not call e + 2 (its phase waits for every rank's
+// call e + 1), so two slot sets suffice.
+__global__ void __launch_bounds__(kEpThreads)
+    ep_push_partials_kernel(const float4* __restrict__ part, int splits, int64_t split4, int64_t n4,
+                            const uint64_t* __restrict__ peer_red, int world, int64_t dst_off4) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float4 v = part[i];
+    for (int sp = 1; sp < splits; ++sp) {
+      const float4 b = part[sp * split4 + i];
+      v.x += b.x; v.y += b.y; v.z += b.z; v.w += b.w;
+    }
+    for (int r = 0; r < world; ++r) reinterpret_cast<float4*>(peer_red[r])[dst_off4 + i] = v;
+  }
+  __threadfence_system();
+}
+
+__global__ void __launch_bounds__(kEpThreads)
+    ep_sum_partials_kernel(const float4* __restrict__ slots, int world, int64_t n4, int64_t slot4,
+                           uint2* __restrict__ out) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float4 a = slots[i];
+    for (int r = 1; r < world; ++r) {
+      const float4 b = slots[r * slot4 + i];
+      a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+    }
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(a.x, a.y), hi = __floats2bfloat162_rn(a.z, a.w);
+    out[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+  }
+}
+
+int ep_grid_blocks(int64_t n) {
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((n + kEpThreads - 1) / kEpThreads, 148 * 8)));
+}
+
 int check_ep(int64_t D, int world, int rank, int64_t E) {
   KW8_REQUIRE(world >= 1 && world <= kEpMaxRanks && rank >= 0 && rank < world, KW8_ERR_INVALID_ARG,
               "bad rank %d of %d", rank, world);
@@ -249,6 +293,34 @@ int launch_ep_counts(const int32_t* sizes, int64_t E, const uint64_t* counts, co
   if (rc) return rc;
   ep_counts_kernel<<<1, 256, 0, stream>>>(sizes, static_cast<int>(E), counts, flags, own_flags, world, rank,
                                          epoch);
+  KW8_CHECK_LAUNCH();
+  return KW8_OK;
+}
+
+int launch_ep_allreduce(const float* part, int splits, int64_t split_stride, int64_t T, int64_t D,
+                        const uint64_t* peer_red, float* own_red, int64_t red_rows, const uint64_t* flags,
+                        uint32_t* own_flags, int world, int rank, uint32_t epoch, void* out, cudaStream_t stream) {
+  KW8_REQUIRE(world >= 1 && world <= kEpMaxRanks && rank >= 0 && rank < world, KW8_ERR_INVALID_ARG,
+              "bad rank %d of %d", rank, world);
+  KW8_REQUIRE(T >= 0 && T <= red_rows && D % 4 == 0 && split_stride % 4 == 0 && splits >= 1,
+              KW8_ERR_UNSUPPORTED, "partial sums of %lld rows exceed the exchange buffer (%lld rows)",
+              (long long)T, (long long)red_rows);
+  KW8_REQUIRE(((reinterpret_cast<uintptr_t>(part) | reinterpret_cast<uintptr_t>(own_red)) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(out) & 7) == 0,
+              KW8_ERR_UNSUPPORTED, "partial sums need 16-byte aligned rows");
+  const int64_t n4 = T * D / 4;
+  const int64_t slot4 = red_rows * D / 4;  // one rank's slot
+  const int64_t parity4 = static_cast<int64_t>(epoch & 1u) * world * slot4;
+  if (n4 > 0) {
+    ep_push_partials_kernel<<<ep_grid_blocks(n4), kEpThreads, 0, stream>>>(
+        reinterpret_cast<const float4*>(part), splits, split_stride / 4, n4, peer_red, world,
+        parity4 + rank * slot4);
+    KW8_CHECK_LAUNCH();
+  }
+  int rc = launch_ep_barrier(flags, own_flags, world, rank, 1, epoch, true, stream);
+  if (rc || n4 == 0) return rc;
+  ep_sum_partials_kernel<<<ep_grid_blocks(n4), kEpThreads, 0, stream>>>(
+      reinterpret_cast<const float4*>(own_red) + parity4, world, n4, slot4, static_cast<uint2*>(out));
   KW8_CHECK_LAUNCH();
   return KW8_OK;
 }

@@ -51,6 +51,17 @@ EpBuffers carve_ep(Carver& c, int64_t max_tokens, int64_t D, int64_t I, int64_t 
   return b;
 }
 
+// The members every group call needs: rank, world, flags and (for the
+// one-shot sums) the exchange buffer.
+int check_group(const kw8_ep_peers* p) {
+  KW8_REQUIRE(p != nullptr, KW8_ERR_INVALID_ARG, "null peers");
+  KW8_REQUIRE(p->world >= 1 && p->world <= kEpMaxRanks && p->rank >= 0 && p->rank < p->world,
+              KW8_ERR_INVALID_ARG, "bad rank %d of %d", p->rank, p->world);
+  KW8_REQUIRE(p->flags && p->own_flags && p->red && p->own_red && p->red_rows >= 0, KW8_ERR_INVALID_ARG,
+              "incomplete peers (flags and the exchange buffer are required)");
+  return KW8_OK;
+}
+
 int check_peers(const kw8_ep_peers* p) {
   KW8_REQUIRE(p != nullptr, KW8_ERR_INVALID_ARG, "null peers");
   KW8_REQUIRE(p->world >= 1 && p->world <= kEpMaxRanks && p->rank >= 0 && p->rank < p->world,
@@ -246,6 +257,108 @@ int kw8_moe_ffn_ep(const void* x, int64_t T, int64_t D, int64_t I, int64_t E, in
   rc = launch_ep_barrier(peers->flags, peers->own_flags, world, rank, 2, epoch, true, stream);
   if (rc) return rc;
   return launch_combine(peers->own_out, b.inv_pos, b.w, T, k, D, out, stream);
+}
+
+size_t kw8_moe_ffn_ep_decode_workspace_size(int64_t T, int64_t D, int64_t I, int64_t E, int32_t k) {
+  Carver c(nullptr, SIZE_MAX);
+  carve_moe(c, T, D, I, E, k);
+  return c.off;
+}
+
+int kw8_moe_ffn_ep_decode(const void* x, int64_t T, int64_t D, int64_t I, int64_t E, int32_t k,
+                          int64_t capacity, kw8_weight router, kw8_weight gate_local,
+                          kw8_weight up_local, kw8_weight down_local, void* out,
+                          const kw8_ep_peers* peers, uint32_t epoch, void* workspace,
+                          size_t workspace_bytes, kw8_stream_t stream_in) {
+  KW8_API_BEGIN
+  int rc = check_group(peers);
+  if (rc) return rc;
+  const int world = peers->world, rank = peers->rank;
+  KW8_REQUIRE((x && out) || T == 0, KW8_ERR_INVALID_ARG, "null x/out");
+  rc = check_ep(D, world, rank, E);
+  if (!rc) rc = check_moe_args(T, D, I, E, k, router, gate_local, up_local, down_local);
+  if (rc) return rc;
+  KW8_REQUIRE(T <= peers->red_rows, KW8_ERR_UNSUPPORTED, "T=%lld exceeds the group's exchange rows (%lld)",
+              (long long)T, (long long)peers->red_rows);
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_in);
+  Carver c(workspace, workspace_bytes);
+  MoeBuffers b = carve_moe(c, T, D, I, E, k);
+  KW8_REQUIRE(workspace != nullptr && c.ok, KW8_ERR_WORKSPACE, "EP decode workspace too small (%zu < %zu)",
+              workspace_bytes, c.off);
+  const int64_t e_loc = E / world;
+  const int64_t m = T * k;
+  if (T > 0) {
+    // Every rank routes every token: the same logits, top-k and permutation.
+    float* part = router_part_floats(T, D, E) > 0 ? b.router_part : nullptr;
+    if (route_tail_small_ok(T, E, k)) {
+      rc = router_logits(x, T, D, E, router, b.logits, stream, part);
+      if (!rc)
+        rc = launch_route_tail_small(b.logits, T, E, k, capacity, b.idx, b.w, b.sorted_token, b.inv_pos,
+                                     b.group_sizes, b.group_offsets, b.sorted_w, b.active, b.acc, D, stream);
+    } else {
+      rc = kw8::route(x, T, D, E, k, router, b.logits, b.idx, b.w, stream, part, b.acc, D);
+      if (!rc)
+        rc = launch_permute_multi(b.idx, T, k, E, capacity, b.perm_hist, b.sorted_token, b.inv_pos,
+                                  b.group_sizes, b.group_offsets, stream, b.w, b.sorted_w, b.active);
+    }
+    if (rc) return rc;
+    // This rank's experts: their rows are a contiguous range of the sorted
+    // order (offsets e_loc * rank .. e_loc * (rank + 1)); the fused combine
+    // adds their weighted outputs into the fp32 partial b.acc.
+    const bool streamed = use_stream(rows_hint(m, E));
+    if (!streamed) {
+      rc = launch_gather(x, b.sorted_token, b.group_offsets + E, m, D, b.xs, stream);
+      if (rc) return rc;
+    }
+    ExpertBuffers eb{b.tiles, b.num_tiles, b.h};
+    const int64_t m_loc = std::max<int64_t>(1, m * e_loc / E);  // expected local rows (tile choice)
+    rc = expert_ffn(streamed, streamed ? x : b.xs, streamed ? b.sorted_token : nullptr, m, D, I, e_loc,
+                    b.group_offsets + rank * e_loc, gate_local, up_local, down_local, b.acc, eb, stream,
+                    b.sorted_token, b.sorted_w, nullptr, m_loc);
+    if (rc) return rc;
+  }
+  return launch_ep_allreduce(b.acc, 1, 0, T, D, peers->red, peers->own_red, peers->red_rows, peers->flags,
+                             peers->own_flags, world, rank, epoch, out, stream);
+}
+
+size_t kw8_dense_ffn_tp_workspace_size(int64_t T, int64_t D, int64_t H_local) {
+  Carver c(nullptr, SIZE_MAX);
+  c.take<__nv_bfloat16>(T * H_local);
+  c.take<float>(std::max<int64_t>(dense_down_part_floats(T, D, H_local), T * D));
+  return c.off;
+}
+
+int kw8_dense_ffn_tp(const void* x, int64_t T, int64_t D, int64_t H_local, kw8_weight gate,
+                     kw8_weight up, kw8_weight down, int32_t act, void* out,
+                     const kw8_ep_peers* peers, uint32_t epoch, void* workspace,
+                     size_t workspace_bytes, kw8_stream_t stream_in) {
+  KW8_API_BEGIN
+  int rc = check_group(peers);
+  if (rc) return rc;
+  KW8_REQUIRE((x && out) || T == 0, KW8_ERR_INVALID_ARG, "null x/out");
+  KW8_REQUIRE(T >= 0 && D > 0 && D % 8 == 0 && H_local > 0, KW8_ERR_INVALID_ARG, "bad shape");
+  KW8_REQUIRE(act == KW8_ACT_GELU_TANH || act == KW8_ACT_SILU, KW8_ERR_INVALID_ARG, "bad act");
+  rc = check_weight(gate, "gate");
+  if (!rc) rc = check_weight(up, "up");
+  if (!rc) rc = check_weight(down, "down");
+  if (rc) return rc;
+  KW8_REQUIRE(T <= peers->red_rows, KW8_ERR_UNSUPPORTED, "T=%lld exceeds the group's exchange rows (%lld)",
+              (long long)T, (long long)peers->red_rows);
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_in);
+  Carver c(workspace, workspace_bytes);
+  __nv_bfloat16* hid = c.take<__nv_bfloat16>(T * H_local);
+  float* part = c.take<float>(std::max<int64_t>(dense_down_part_floats(T, D, H_local), T * D));
+  KW8_REQUIRE(workspace != nullptr && c.ok, KW8_ERR_WORKSPACE, "TP workspace too small (%zu < %zu)",
+              workspace_bytes, c.off);
+  const int splits = T > 0 ? dense_down_splits(T, D, H_local) : 1;
+  if (T > 0) {
+    rc = dense_gate_up(x, T, D, H_local, gate, up, act, hid, stream);
+    if (!rc) rc = dense_f32_parts(hid, T, H_local, D, down, splits, part, stream);
+    if (rc) return rc;
+  }
+  // The K-split slices of this rank's partial are summed while they are pushed.
+  return launch_ep_allreduce(part, splits, T * D, T, D, peers->red, peers->own_red, peers->red_rows,
+                             peers->flags, peers->own_flags, peers->world, peers->rank, epoch, out, stream);
 }
 
 int kw8_ep_barrier(const kw8_ep_peers* peers, int32_t phase, uint32_t epoch, int32_t signal,

@@ -54,6 +54,7 @@ __all__ = [
     "feed_forward_tp",
     "moe_swiglu_ffn_ep",
     "EPContext",
+    "TPContext",
     "moe_swiglu_ffn_ep_decode",
     "MoEOps",
     "KernelMoEOps",
@@ -133,19 +134,53 @@ def _allreduce_to_bf16(partial: torch.Tensor, group) -> torch.Tensor:
     return partial.to(torch.bfloat16)
 
 
-def swiglu_ffn_tp(x: torch.Tensor, gate_shard: Weight, up_shard: Weight, down_shard: Weight, *, group=None):
-    """Tensor-parallel kappa/qwen3/ffn.py:swiglu_ffn over this rank's shards."""
+def _dense_tp_call(x: torch.Tensor, gate, up, down, hidden: int, act: int, ctx: "TPContext", keep) -> torch.Tensor:
+    """One ``kw8_dense_ffn_tp`` call: this rank's shards, partials summed over NVLink."""
+    from kappa_b200 import _dense
+
+    b, t, d = x.shape
+    T = b * t
+    if d != ctx.d or T > ctx.max_tokens:
+        raise ValueError(f"TPContext holds {ctx.max_tokens} rows of {ctx.d}, got {T} rows of {d}")
+    _dense.check_x(x, d)
+    xc = x.contiguous()
+    lib = _lib.load()
+    out = torch.empty((b, t, d), dtype=torch.bfloat16, device=x.device)
+    ws = torch.empty(int(lib.kw8_dense_ffn_tp_workspace_size(T, d, hidden)), dtype=torch.uint8, device=x.device)
+    _lib.check(lib.kw8_dense_ffn_tp(xc.data_ptr(), T, d, hidden, gate, up, down, act, out.data_ptr(),
+                                    ctypes.byref(ctx.peers), ctx.next_epoch(), ws.data_ptr(), ws.numel(),
+                                    _lib.stream_of(x)))
+    del keep
+    return out
+
+
+def swiglu_ffn_tp(x: torch.Tensor, gate_shard: Weight, up_shard: Weight, down_shard: Weight, *, group=None,
+                  ctx: "TPContext | None" = None):
+    """Tensor-parallel kappa/qwen3/ffn.py:swiglu_ffn over this rank's shards.
+
+    With ``ctx`` (a :class:`TPContext`) the layer is one library call that
+    sums the ranks' fp32 partials over NVLink; without, an NCCL all-reduce.
+    """
     from kappa_b200.qwen3.ffn import swiglu_ffn
 
+    if ctx is not None:
+        g, u, dn = (kmajor(w, -2, n) for w, n in ((gate_shard, "gate_w"), (up_shard, "up_w"), (down_shard, "down_w")))
+        return _dense_tp_call(x, g.struct(), u.struct(), dn.struct(), int(g.q.shape[-2]), _lib.ACT_SILU, ctx,
+                              (g, u, dn))
     partial = swiglu_ffn(x, gate_shard, up_shard, down_shard, out_dtype=torch.float32)
     return _allreduce_to_bf16(partial, group)
 
 
 def feed_forward_tp(x: torch.Tensor, gating_shard: Weight, linear_shard: Weight, *, transpose_gating_einsum: bool,
-                    group=None):
-    """Tensor-parallel kappa/gemma3/ffn.py:feed_forward over this rank's shards."""
+                    group=None, ctx: "TPContext | None" = None):
+    """Tensor-parallel kappa/gemma3/ffn.py:feed_forward over this rank's shards (``ctx``: see swiglu_ffn_tp)."""
     from kappa_b200.gemma3.ffn import feed_forward
 
+    if ctx is not None:
+        g = kmajor(gating_shard, -1 if transpose_gating_einsum else -2, "gating_w")
+        lw = kmajor(linear_shard, -2, "linear_w")
+        hidden = int(g.q.shape[1])
+        return _dense_tp_call(x, g.struct(0), g.struct(hidden), lw.struct(), hidden, _lib.ACT_GELU_TANH, ctx, (g, lw))
     partial = feed_forward(x, gating_shard, linear_shard, transpose_gating_einsum=transpose_gating_einsum,
                            out_dtype=torch.float32)
     return _allreduce_to_bf16(partial, group)
@@ -231,43 +266,29 @@ def _moe_args(cfg, x: torch.Tensor):
     return b, t, d, capacity
 
 
-class EPContext:
-    """Buffers of the NVLink expert-parallel path for one process group.
+def _as_i64(v):
+    return [int(a) - (1 << 64) if int(a) >= (1 << 63) else int(a) for a in v]
 
-    Each rank allocates a receive buffer for every row the other ranks could
-    send it (``world * max_tokens * k`` rows of ``d``) and a return buffer
-    for its own routed rows, shares both with CUDA IPC and maps the other
-    ranks' buffers.  Collective: every rank constructs it with the same
-    arguments and calls :meth:`close` (also collective) when done.
-    """
 
-    def __init__(self, *, max_tokens: int, d: int, k: int, hidden: int, num_experts: int, group=None,
-                 dedup: bool = True):
+class _SharedBuffers:
+    """Device buffers every rank of a group allocates (zero-filled, CUDA IPC)
+    and maps from every other rank.  ``peer_ptrs[b]`` is a device int64
+    tensor of the ``world`` addresses of buffer ``b`` as this rank sees them;
+    ``own[b]`` is this rank's own address.  Collective construction and
+    :meth:`close`."""
+
+    def __init__(self, sizes, group, device):
         self.group = group
         self.world, self.rank = _world(group)
-        if num_experts % self.world:
-            raise ValueError(f"{num_experts} experts do not split over {self.world} ranks")
-        self.max_tokens, self.d, self.k, self.hidden, self.num_experts = max_tokens, d, k, hidden, num_experts
-        self.device = torch.device("cuda", torch.cuda.current_device())
         lib = _lib.load()
         hsize = int(lib.kw8_ipc_handle_size())
-        self.recv_rows = self.world * max_tokens * k
-        self.out_rows = max_tokens * k
-        # Shared buffers (zero-filled): receive rows, return rows, counts
-        # [2][world][E + world] int32, phase flags [3][world] uint32, and for
-        # the deduplicated step: token rows [world * max_tokens][d], pair
-        # records (int32 row + fp32 weight per received pair), partial sums
-        # [world][max_tokens][d].
-        pairs = self.world * max_tokens * k
-        sizes = (self.recv_rows * d * 2, self.out_rows * d * 2, 2 * self.world * (num_experts + self.world) * 4,
-                 3 * self.world * 4, self.world * max_tokens * d * 2, pairs * 8, self.world * max_tokens * d * 2)
-        self._own = []
+        self.own = []
         handles = []
         for nbytes in sizes:
             ptr = ctypes.c_void_p()
             h = ctypes.create_string_buffer(hsize)
-            _lib.check(lib.kw8_ipc_alloc(nbytes, ctypes.byref(ptr), h))
-            self._own.append(ptr.value)
+            _lib.check(lib.kw8_ipc_alloc(max(int(nbytes), 16), ctypes.byref(ptr), h))
+            self.own.append(ptr.value)
             handles.append(h.raw)
         allh = [None] * self.world
         dist.all_gather_object(allh, handles, group=group)
@@ -276,20 +297,70 @@ class EPContext:
         for r, hs in enumerate(allh):
             for b in range(len(sizes)):
                 if r == self.rank:
-                    peers[b].append(self._own[b])
+                    peers[b].append(self.own[b])
                 else:
                     ptr = ctypes.c_void_p()
                     _lib.check(lib.kw8_ipc_open(ctypes.create_string_buffer(hs[b], hsize), ctypes.byref(ptr)))
                     self._opened.append(ptr.value)
                     peers[b].append(ptr.value)
+        self.peer_ptrs = [torch.tensor(_as_i64(v), dtype=torch.int64, device=device) for v in peers]
+        self.closed = False
 
-        def as_i64(v):
-            return [int(a) - (1 << 64) if int(a) >= (1 << 63) else int(a) for a in v]
+    def close(self, device):
+        if self.closed:
+            return
+        lib = _lib.load()
+        torch.cuda.synchronize(device)
+        dist.barrier(group=self.group)
+        for p in self._opened:
+            lib.kw8_ipc_close(ctypes.c_void_p(p))
+        dist.barrier(group=self.group)
+        for p in self.own:
+            lib.kw8_ipc_free(ctypes.c_void_p(p))
+        self.closed = True
 
+
+class EPContext:
+    """Buffers of the NVLink expert-parallel path for one process group.
+
+    Each rank allocates a receive buffer for every row the other ranks could
+    send it (``world * max_tokens * k`` rows of ``d``) and a return buffer
+    for its own routed rows, shares both with CUDA IPC and maps the other
+    ranks' buffers; the decode step (``moe_swiglu_ffn_ep_decode``) sums its
+    partials through an exchange buffer of ``decode_tokens`` rows.
+    Collective: every rank constructs it with the same arguments and calls
+    :meth:`close` (also collective) when done.
+    """
+
+    def __init__(self, *, max_tokens: int, d: int, k: int, hidden: int, num_experts: int, group=None,
+                 dedup: bool = True, return_fp32: bool = True, decode_tokens: int = 256):
+        self.group = group
+        self.world, self.rank = _world(group)
+        if num_experts % self.world:
+            raise ValueError(f"{num_experts} experts do not split over {self.world} ranks")
+        self.max_tokens, self.d, self.k, self.hidden, self.num_experts = max_tokens, d, k, hidden, num_experts
+        self.decode_tokens = decode_tokens
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        lib = _lib.load()
+        self.recv_rows = self.world * max_tokens * k
+        self.out_rows = max_tokens * k
+        # Shared buffers (zero-filled): receive rows, return rows, counts
+        # [2][world][E + world] int32, phase flags [3][world] uint32, and for
+        # the deduplicated step: token rows [world * max_tokens][d], pair
+        # records (int32 row + fp32 weight per received pair), partial sums
+        # [world][max_tokens][d], fp32 (return_fp32: the source rounds each
+        # output once, as one GPU does) or bf16 (half the return traffic);
+        # and the decode exchange buffer [2][world][decode_tokens][d] fp32.
+        pairs = self.world * max_tokens * k
+        ret_bytes = 4 if return_fp32 else 2
+        sizes = (self.recv_rows * d * 2, self.out_rows * d * 2, 2 * self.world * (num_experts + self.world) * 4,
+                 3 * self.world * 4, self.world * max_tokens * d * 2, pairs * 8,
+                 self.world * max_tokens * d * ret_bytes, 2 * self.world * decode_tokens * d * 4)
+        self._bufs = _SharedBuffers(sizes, group, self.device)
         (self.peer_recv, self.peer_out, self.peer_counts, self.peer_flags, self.peer_rows, self.peer_meta,
-         self.peer_ret) = (torch.tensor(as_i64(v), dtype=torch.int64, device=self.device) for v in peers)
+         self.peer_ret, self.peer_red) = self._bufs.peer_ptrs
         (self.recv_ptr, self.out_ptr, self.counts_ptr, self.flags_ptr, self.rows_ptr, self.meta_ptr,
-         self.ret_ptr) = self._own
+         self.ret_ptr, self.red_ptr) = self._bufs.own
         self.dedup = dedup
         self.peers = _lib.KW8EpPeers(
             self.world, self.rank, max_tokens, self.peer_recv.data_ptr(), self.peer_out.data_ptr(),
@@ -297,10 +368,14 @@ class EPContext:
             self.counts_ptr, self.flags_ptr,
             self.peer_rows.data_ptr() if dedup else None, self.peer_meta.data_ptr() if dedup else None,
             self.peer_ret.data_ptr() if dedup else None, self.rows_ptr if dedup else None,
-            self.meta_ptr if dedup else None, self.ret_ptr if dedup else None)
-        self.epoch = 0  # calls of the fused layer so far (the group's phase tag)
+            self.meta_ptr if dedup else None, self.ret_ptr if dedup else None, int(bool(return_fp32)),
+            self.peer_red.data_ptr(), self.red_ptr, decode_tokens)
+        self.epoch = 0  # calls of the fused steps so far (the group's phase tag)
         self.ep_ws = torch.empty(
             int(lib.kw8_moe_ffn_ep_workspace_size(max_tokens, d, hidden, num_experts, k, self.world)),
+            dtype=torch.uint8, device=self.device)
+        self.dec_ws = torch.empty(
+            int(lib.kw8_moe_ffn_ep_decode_workspace_size(decode_tokens, d, hidden, num_experts, k)),
             dtype=torch.uint8, device=self.device)
         # Staged path (kw8_ep_dispatch / kw8_ep_return + collectives).
         self.ys_loc = torch.empty((self.recv_rows, d), dtype=torch.bfloat16, device=self.device)
@@ -310,10 +385,17 @@ class EPContext:
         self.loc_off = torch.empty(e_loc + 1, dtype=torch.int32, device=self.device)
         self.counts = torch.empty((self.world, num_experts), dtype=torch.int32, device=self.device)
         self.flag = torch.zeros(1, dtype=torch.float32, device=self.device)
-        self.closed = False
         # Every rank's buffers (flags included) are zero before anyone signals.
         torch.cuda.synchronize(self.device)
         dist.barrier(group=group)
+
+    @property
+    def closed(self) -> bool:
+        return self._bufs.closed
+
+    def next_epoch(self) -> int:
+        self.epoch += 1
+        return self.epoch & 0xFFFFFFFF
 
     def sync(self):
         """Orders the phases across ranks on the current stream (a one-element all-reduce)."""
@@ -321,17 +403,37 @@ class EPContext:
 
     def close(self):
         """Collective: unmaps the other ranks' buffers, then frees this rank's."""
-        if self.closed:
-            return
-        lib = _lib.load()
+        self._bufs.close(self.device)
+
+
+class TPContext:
+    """The exchange buffer and phase flags of one-call tensor-parallel FFNs
+    (``kw8_dense_ffn_tp``) for a process group: every rank's fp32 partial of
+    up to ``max_tokens`` rows of ``d`` goes to every rank over NVLink.
+    Collective construction and :meth:`close`."""
+
+    def __init__(self, *, max_tokens: int, d: int, group=None):
+        self.group = group
+        self.world, self.rank = _world(group)
+        self.max_tokens, self.d = max_tokens, d
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        self._bufs = _SharedBuffers((3 * self.world * 4, 2 * self.world * max_tokens * d * 4), group, self.device)
+        self.peer_flags, self.peer_red = self._bufs.peer_ptrs
+        self.flags_ptr, self.red_ptr = self._bufs.own
+        self.peers = _lib.KW8EpPeers(
+            self.world, self.rank, max_tokens, None, None, None, self.peer_flags.data_ptr(), None, None, None,
+            self.flags_ptr, None, None, None, None, None, None, 0, self.peer_red.data_ptr(), self.red_ptr,
+            max_tokens)
+        self.epoch = 0
         torch.cuda.synchronize(self.device)
-        dist.barrier(group=self.group)
-        for p in self._opened:
-            lib.kw8_ipc_close(ctypes.c_void_p(p))
-        dist.barrier(group=self.group)
-        for p in self._own:
-            lib.kw8_ipc_free(ctypes.c_void_p(p))
-        self.closed = True
+        dist.barrier(group=group)
+
+    def next_epoch(self) -> int:
+        self.epoch += 1
+        return self.epoch & 0xFFFFFFFF
+
+    def close(self):
+        self._bufs.close(self.device)
 
 
 def _moe_ep_p2p(x, router_w, gate_local, up_local, down_local, *, cfg, ctx: EPContext, capacity,
@@ -357,10 +459,9 @@ def _moe_ep_p2p(x, router_w, gate_local, up_local, down_local, *, cfg, ctx: EPCo
         # round trip and no collective library.
         r = kmajor(router_w, -2, "router_w")
         out = torch.empty((b, t, d), dtype=torch.bfloat16, device=x.device)
-        ctx.epoch += 1
         _lib.check(lib.kw8_moe_ffn_ep(
             xc.data_ptr(), T, d, i, e, k, -1 if capacity is None else int(capacity), r.struct(), g.struct(),
-            u.struct(), dn.struct(), out.data_ptr(), ctypes.byref(ctx.peers), ctx.epoch & 0xFFFFFFFF,
+            u.struct(), dn.struct(), out.data_ptr(), ctypes.byref(ctx.peers), ctx.next_epoch(),
             ctx.ep_ws.data_ptr(), ctx.ep_ws.numel(), stream))
         del r, g, u, dn
         return out
@@ -438,12 +539,38 @@ def moe_swiglu_ffn_ep(x: torch.Tensor, router_w: Weight, gate_local: Weight, up_
 
 
 def moe_swiglu_ffn_ep_decode(x: torch.Tensor, router_w: Weight, gate_local: Weight, up_local: Weight,
-                             down_local: Weight, *, cfg, group=None, ops: MoEOps | None = None) -> torch.Tensor:
+                             down_local: Weight, *, cfg, group=None, ops: MoEOps | None = None,
+                             ctx: EPContext | None = None) -> torch.Tensor:
     """Expert-parallel MoE layer for small, replicated batches (decode).
 
     Every rank passes the same ``x``; each adds its local experts' weighted
-    outputs into an fp32 partial and one all-reduce sums them.
+    outputs into an fp32 partial and the partials are summed over the group.
+    With ``ctx`` (an :class:`EPContext`) the whole step is one library call
+    (``kw8_moe_ffn_ep_decode``: the partials cross NVLink with peer stores
+    and a flag phase, no host synchronisation); otherwise the staged steps
+    of ``ops`` and an NCCL all-reduce (this form also runs on CPU ranks).
     """
+    if ctx is not None and ops is None:
+        b, t, d, capacity = _moe_args(cfg, x)
+        e, k = cfg.num_experts, cfg.num_experts_per_tok
+        T = b * t
+        if T > ctx.decode_tokens or d != ctx.d or e != ctx.num_experts:
+            raise ValueError("EPContext was made for other shapes")
+        e_loc = e // ctx.world
+        g, u, dn = (kmajor(w, -2, n) for w, n in ((gate_local, "ffn_gate"), (up_local, "ffn_up"),
+                                                   (down_local, "ffn_down")))
+        if int(g.q.shape[0]) != e_loc:
+            raise ValueError("local expert weights do not match the EPContext")
+        r = kmajor(router_w, -2, "router_w")
+        lib = _lib.load()
+        xc = x.contiguous()
+        out = torch.empty((b, t, d), dtype=torch.bfloat16, device=x.device)
+        _lib.check(lib.kw8_moe_ffn_ep_decode(
+            xc.data_ptr(), T, d, int(g.q.shape[-2]), e, k, -1 if capacity is None else int(capacity), r.struct(),
+            g.struct(), u.struct(), dn.struct(), out.data_ptr(), ctypes.byref(ctx.peers), ctx.next_epoch(),
+            ctx.dec_ws.data_ptr(), ctx.dec_ws.numel(), _lib.stream_of(x)))
+        del r, g, u, dn
+        return out
     ops = ops or KernelMoEOps()
     world, rank = _world(group)
     e, k = cfg.num_experts, cfg.num_experts_per_tok

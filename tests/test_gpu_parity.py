@@ -455,7 +455,7 @@ def test_moe_errors_match_kappa():
                                                       moe_impl="fixed_capacity", moe_capacity_factor=0.0))
 
 
-def _ep_single_rank_peers(dev, Tm, D, E, k, dedup):
+def _ep_single_rank_peers(dev, Tm, D, E, k, dedup, ret_f32=True, red_rows=0):
     """A one-rank expert-parallel group: its own buffers are the peers'."""
     world = 1
     bufs = {
@@ -465,7 +465,8 @@ def _ep_single_rank_peers(dev, Tm, D, E, k, dedup):
         "flags": torch.zeros(3 * world, dtype=torch.int32, device=dev),
         "rows": torch.zeros((world * Tm, D), dtype=torch.bfloat16, device=dev),
         "meta": torch.zeros(2 * world * Tm * k, dtype=torch.int32, device=dev),
-        "ret": torch.zeros((world * Tm, D), dtype=torch.bfloat16, device=dev),
+        "ret": torch.zeros((world * Tm, D), dtype=torch.float32 if ret_f32 else torch.bfloat16, device=dev),
+        "red": torch.zeros((2, world, max(red_rows, 1), D), dtype=torch.float32, device=dev),
     }
     arr = {n: torch.tensor([t.data_ptr()], dtype=torch.int64, device=dev) for n, t in bufs.items()}
     p = _lib.KW8EpPeers(
@@ -474,16 +475,18 @@ def _ep_single_rank_peers(dev, Tm, D, E, k, dedup):
         bufs["flags"].data_ptr(),
         arr["rows"].data_ptr() if dedup else None, arr["meta"].data_ptr() if dedup else None,
         arr["ret"].data_ptr() if dedup else None, bufs["rows"].data_ptr() if dedup else None,
-        bufs["meta"].data_ptr() if dedup else None, bufs["ret"].data_ptr() if dedup else None)
+        bufs["meta"].data_ptr() if dedup else None, bufs["ret"].data_ptr() if dedup else None, int(ret_f32),
+        arr["red"].data_ptr(), bufs["red"].data_ptr(), red_rows)
     return p, (bufs, arr)
 
 
-@pytest.mark.parametrize("dedup", [True, False])
-def test_moe_ep_single_rank(dedup):
+@pytest.mark.parametrize("dedup,ret_f32", [(True, True), (True, False), (False, True)])
+def test_moe_ep_single_rank(dedup, ret_f32):
     """kw8_moe_ffn_ep on a group of one rank: every step of the expert-parallel
     call (counts exchange, row and record dispatch, phase flags, local
     experts, return, combine) runs on one GPU against the fp32 reference, for
-    two calls in a row (epochs 1 and 2, both count copies)."""
+    two calls in a row (epochs 1 and 2, both count copies).  The partial sums
+    return as fp32 (or as bf16, one more rounding)."""
     import ctypes
 
     from kappa_b200.qwen3.quant import kmajor
@@ -491,7 +494,7 @@ def test_moe_ep_single_rank(dedup):
     T, D, I, E, k = 200, 256, 128, 16, 4
     x, g, o = _moe_case(T, D, I, E, k, True, seed=31)
     dev = torch.device("cuda", 0)
-    peers, keep = _ep_single_rank_peers(dev, T, D, E, k, dedup)
+    peers, keep = _ep_single_rank_peers(dev, T, D, E, k, dedup, ret_f32)
     lib = _lib.load()
     ws = torch.empty(int(lib.kw8_moe_ffn_ep_workspace_size(T, D, I, E, k, 1)), dtype=torch.uint8, device=dev)
     km = [kmajor(w, -2) for w in g]
@@ -503,6 +506,73 @@ def test_moe_ep_single_rank(dedup):
                                       ctypes.byref(peers), epoch, ws.data_ptr(), ws.numel(), stream))
         assert _lib.device_status(out) == 0
         _moe_check(x, g, o, E, k, out.reshape(1, T, D))
+    del keep
+
+
+@pytest.mark.parametrize("B", [1, 8, 64, 256])
+def test_moe_ep_decode_single_rank(B):
+    """kw8_moe_ffn_ep_decode on a group of one rank: routing of the
+    replicated batch, the local experts' fused combine, the push of the fp32
+    partial into the exchange slot, the flag phase and the rank-order sum, for
+    three calls in a row (both slot parities), against the fp32 reference."""
+    import ctypes
+
+    from kappa_b200.qwen3.quant import kmajor
+
+    D, I, E, k = 512, 256, 32, 8
+    x, g, o = _moe_case(B, D, I, E, k, True, seed=B + 5)
+    dev = torch.device("cuda", 0)
+    peers, keep = _ep_single_rank_peers(dev, B, D, E, k, True, True, red_rows=256)
+    lib = _lib.load()
+    ws = torch.empty(int(lib.kw8_moe_ffn_ep_decode_workspace_size(B, D, I, E, k)), dtype=torch.uint8, device=dev)
+    km = [kmajor(w, -2) for w in g]
+    xd = to_dev(x).reshape(B, D)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    outs = []
+    for epoch in (1, 2, 3):
+        out = torch.empty_like(xd)
+        _lib.check(lib.kw8_moe_ffn_ep_decode(xd.data_ptr(), B, D, I, E, k, -1, *[w.struct() for w in km],
+                                             out.data_ptr(), ctypes.byref(peers), epoch, ws.data_ptr(), ws.numel(),
+                                             stream))
+        assert _lib.device_status(out) == 0
+        _moe_check(x, g, o, E, k, out.reshape(1, B, D))
+        outs.append(out)
+    del keep
+
+
+@pytest.mark.parametrize("T,act", [(16, 0), (300, 1)])
+def test_dense_ffn_tp_single_rank(T, act):
+    """kw8_dense_ffn_tp on a group of one rank (the whole hidden axis is the
+    rank's shard): the fp32 partial's push, flag phase and sum equal the
+    dense FFN."""
+    import ctypes
+
+    from kappa_b200.qwen3.quant import kmajor
+
+    D, H = 512, 1024
+    rng = np.random.default_rng(T)
+    x = normal(rng, (1, T, D)).astype(O.BF16)
+    gating, linear = normal(rng, (2, H, D), 0.02), normal(rng, (H, D), 0.02)
+    gt, lw = _gpu_q(gating, True, -1), _gpu_q(linear, True, -2)
+    dev = torch.device("cuda", 0)
+    peers, keep = _ep_single_rank_peers(dev, 1, D, 4, 1, False, True, red_rows=512)
+    g, l2 = kmajor(gt, -1), kmajor(lw, -2)
+    lib = _lib.load()
+    ws = torch.empty(int(lib.kw8_dense_ffn_tp_workspace_size(T, D, H)), dtype=torch.uint8, device=dev)
+    xd = to_dev(x).reshape(T, D)
+    out = torch.empty_like(xd)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    _lib.check(lib.kw8_dense_ffn_tp(xd.data_ptr(), T, D, H, g.struct(0), g.struct(H), l2.struct(), act,
+                                    out.data_ptr(), ctypes.byref(peers), 1, ws.data_ptr(), ws.numel(), stream))
+    assert _lib.device_status(out) == 0
+    ogt, olw = _oracle_q(gating, True, -1), _oracle_q(linear, True, -2)
+    if act == 0:
+        ref = O.feed_forward(x, ogt, olw, transpose_gating_einsum=True, compute_dtype=np.float32)
+    else:
+        ref = O.swiglu_ffn(x, O.Q8Weight(np.swapaxes(ogt.values[0], 0, 1), np.swapaxes(ogt.scale[0], 0, 1)),
+                           O.Q8Weight(np.swapaxes(ogt.values[1], 0, 1), np.swapaxes(ogt.scale[1], 0, 1)), olw,
+                           compute_dtype=np.float32)
+    parity(to_np(out).reshape(1, T, D), ref)
     del keep
 
 
