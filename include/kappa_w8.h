@@ -90,7 +90,14 @@ int kw8_device_status(int32_t* status_out, kw8_stream_t stream);
  *   option 0 (GEMM path): 0 automatic, 1 tensor-core GEMM, 2 weight-
  *            streaming GEMM (the decode kernel: few rows per group);
  *   option 1 (token tile of the tensor-core GEMM): 0 automatic, or a
- *            multiple of 16 in [16, 256].                                   */
+ *            multiple of 16 in [16, 256];
+ *   option 2 (MoE combine): 0 the fused fp32 combine of the down GEMM's
+ *            epilogue (its additions run in arrival order), 1 a fixed
+ *            order: the expert outputs are stored as bf16 rows and every
+ *            token's k rows are summed in slot order (bit-identical runs);
+ *   option 3 (tensor-core GEMM over SM pairs, cta_group::2 with M = 256):
+ *            0 automatic (the one-CTA kernel, faster where measured),
+ *            1 never, 2 for every launch whose tile allows it.             */
 int kw8_set_option(int32_t option, int64_t value);
 
 /* ------------------------------------------------------- quantisation -- */

@@ -40,6 +40,7 @@ NORM_QWEN = 1  # x * rsqrt(mean(x^2) + eps) * scale
 OPT_GEMM_PATH = 0  # 0 auto, 1 tensor core, 2 weight streaming (decode kernel)
 OPT_TOKEN_TILE = 1  # 0 auto, 16..256
 OPT_DETERMINISTIC = 2  # 1: the MoE combine sums each token's k rows in a fixed order
+OPT_TC_PAIR = 3  # tensor-core GEMM over SM pairs: 0 auto (one-CTA), 1 never, 2 whenever the tile allows
 
 
 class KW8Error(RuntimeError):

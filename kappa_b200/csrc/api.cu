@@ -635,6 +635,11 @@ int kw8_set_option(int32_t option, int64_t value) {
     g_opt_token_tile.store(static_cast<int>(value));
     return KW8_OK;
   }
+  if (option == 3) {
+    KW8_REQUIRE(value >= 0 && value <= 2, KW8_ERR_INVALID_ARG, "CTA-pair GEMM must be 0, 1 or 2");
+    g_opt_tc_pair.store(static_cast<int>(value));
+    return KW8_OK;
+  }
   if (option == 2) {
     KW8_REQUIRE(value == 0 || value == 1, KW8_ERR_INVALID_ARG, "deterministic must be 0 or 1");
     g_opt_deterministic.store(static_cast<int>(value));

@@ -62,16 +62,18 @@ __device__ __forceinline__ void transpose4x4(float (&a)[4], int lane) {
 }
 
 // Epilogue of one tile for one warp: TMEM lane quarter q, 32-column chunks
-// c0, c0 + cstep, ... of the accumulator at acc_lane_base.
+// c0, c0 + cstep, ... of the accumulator at acc_lane_base.  The tile's 128
+// TMEM lanes hold output features fbase.. (64 paired gate/up features, or
+// 128 features).
 template <int kMode>
 __device__ __forceinline__ void epilogue_tile(const GemmArgs& p, const TileInfo& ti,
                                               uint32_t acc_lane_base, int q, int lane,
-                                              int c0, int cstep) {
+                                              int c0, int cstep, int fbase_tile) {
   constexpr bool kPair = epi_is_pair(kMode);
   const int nrows = ti.nrows;
   const int nchunks = (nrows + 31) >> 5;
   if constexpr (kPair) {
-    const int f = ti.mt * 64 + q * 16 + (lane & 15);
+    const int f = fbase_tile + q * 16 + (lane & 15);
     const bool fvalid = f < p.N_out;
     const int64_t sidx = static_cast<int64_t>(ti.group) * p.N_out + (fvalid ? f : 0);
     const float s = (lane < 16)
@@ -108,7 +110,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& p, const TileInfo&
       }
     }
   } else if constexpr (kMode == EPI_COMBINE_F32) {
-    const int fbase = ti.mt * 128 + q * 32;
+    const int fbase = fbase_tile + q * 32;
     const int f = fbase + lane;
     const bool fvalid = f < p.N_out;
     const int64_t sidx = static_cast<int64_t>(ti.group) * p.N_out + (fvalid ? f : 0);
@@ -149,7 +151,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& p, const TileInfo&
       }
     }
   } else {
-    const int f = ti.mt * 128 + q * 32 + lane;
+    const int f = fbase_tile + q * 32 + lane;
     const bool fvalid = f < p.N_out;
     const int64_t sidx = static_cast<int64_t>(ti.group) * p.N_out + (fvalid ? f : 0);
     const float s = scale_at(p.scale_a, p.scale_a_dtype, p.scale_a_pc, sidx);
@@ -392,7 +394,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         break;
       tc_fence_after();
       epilogue_tile<kMode>(p, ti, lane_base + static_cast<uint32_t>(ab) * acc_cols, q, lane, ch,
-                           kTcEpiWarps / 4);
+                           kTcEpiWarps / 4, ti.mt * (kPair ? 64 : 128));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[ab]);
@@ -509,6 +511,22 @@ int launch_gemm_tc(int mode, const int8_t* wa, const int8_t* wb, int64_t groups,
   GemmArgs args = args_in;
   args.K = static_cast<int>(K);
   args.N_out = static_cast<int>(N_out);
+  if (mode == EPI_COMBINE_F32) {
+    KW8_REQUIRE(args.row_token && args.row_weight, KW8_ERR_INVALID_ARG, "combine needs row maps");
+    KW8_REQUIRE(N_out % 4 == 0 && args.ld_out % 4 == 0 && (reinterpret_cast<uintptr_t>(args.out) & 15) == 0,
+                KW8_ERR_UNSUPPORTED, "fused combine needs D %% 4 == 0 and a 16-byte aligned output");
+  }
+  if (args.k_splits > 1) {
+    const int64_t kt = (K + kTcBK - 1) / kTcBK;
+    KW8_REQUIRE(mode == EPI_PLAIN_F32 && args.k_splits == valid_k_splits(args.k_splits, kt) &&
+                    args.split_stride > 0,
+                KW8_ERR_INVALID_ARG, "split K needs fp32 output, non-empty ranges and a stride");
+  }
+  if (gemm_tc_pair_ok(mode, N_out, args.nt, g_opt_tc_pair.load())) {
+    // Feature tiles of 256 rows over an SM pair (gemm_tc2.cu).
+    const int64_t max_entries = args.tiles == nullptr ? 0 : groups + (x_rows + args.nt - 1) / args.nt;
+    return launch_gemm_tc2(mode, wa, wb, groups, N_out, K, x, x_rows, ldx, args, max_entries, stream);
+  }
   const TcPlan pl = tc_plan(args.nt);
   KW8_REQUIRE(pl.stages >= 2 && pl.stages <= kTcMaxStages &&
                   pl.nbuf * pl.acc_cols + pl.stages * kTcASlotCols <= static_cast<int>(kTcTmemCols) &&

@@ -43,6 +43,8 @@
 // 16), so the epilogue pairs gate and up with one warp shuffle.
 #pragma once
 
+#include <atomic>
+
 #include "common.cuh"
 
 namespace kw8 {
@@ -152,6 +154,14 @@ inline int valid_k_splits(int want, int64_t k_tiles) {
 // fp32 or bf16; n a multiple of 4.
 int launch_reduce_splits(const float* part, int splits, int64_t stride, int64_t n, void* out,
                          bool out_bf16, cudaStream_t stream);
+
+// CTA-pair kernel (gemm_tc2.cu): whether a launch takes it (force: 0
+// automatic, 1 never, 2 whenever the tile allows), and its launcher.
+inline std::atomic<int> g_opt_tc_pair{0};
+bool gemm_tc_pair_ok(int mode, int64_t N_out, int nt, int force);
+int launch_gemm_tc2(int mode, const int8_t* wa, const int8_t* wb, int64_t groups, int64_t N_out, int64_t K,
+                    const void* x, int64_t x_rows, int64_t ldx, const GemmArgs& args_in, int64_t max_entries,
+                    cudaStream_t stream);
 
 int launch_gemm_tc(int mode, const int8_t* wa, const int8_t* wb, int64_t groups,
                    int64_t N_out, int64_t K, const void* x, int64_t x_rows,

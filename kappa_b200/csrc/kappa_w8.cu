@@ -4,6 +4,7 @@
 #include "host.cu"
 #include "quant.cu"
 #include "gemm_tc.cu"
+#include "gemm_tc2.cu"
 #include "gemm_stream.cu"
 #include "moe.cu"
 #include "norm.cu"

@@ -35,13 +35,16 @@ GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 KAPPA_BF16_TOL = 3e-2
 
 
+_OPTS = (_lib.OPT_GEMM_PATH, _lib.OPT_TOKEN_TILE, _lib.OPT_DETERMINISTIC, _lib.OPT_TC_PAIR)
+
+
 @pytest.fixture(autouse=True)
 def _reset_options():
-    _lib.set_option(_lib.OPT_GEMM_PATH, 0)
-    _lib.set_option(_lib.OPT_TOKEN_TILE, 0)
+    for opt in _OPTS:
+        _lib.set_option(opt, 0)
     yield
-    _lib.set_option(_lib.OPT_GEMM_PATH, 0)
-    _lib.set_option(_lib.OPT_TOKEN_TILE, 0)
+    for opt in _OPTS:
+        _lib.set_option(opt, 0)
     if torch.cuda.is_available():
         dummy = torch.zeros(1, device="cuda")
         assert _lib.device_status(dummy) == 0, "a kernel reported a device-side error"
@@ -384,6 +387,37 @@ def test_moe_token_tiles_agree():
     for nt in (16, 48, 128, 192):
         _lib.set_option(_lib.OPT_TOKEN_TILE, nt)
         _moe_check(x, g, o, E, k, M.moe_swiglu_ffn(to_dev(x), *g, cfg=cfg))
+
+
+@pytest.mark.parametrize("nt", [0, 16, 48, 160, 192, 256])
+def test_tc_pair_kernel_matches_single_cta(nt):
+    """The CTA-pair tensor-core GEMM (M = 256 over two SMs) and the one-CTA
+    kernel give the same MoE layer and dense FFN: every epilogue mode, token
+    tiles from 32 to 256 (ragged tails, odd group sizes), K not a multiple of
+    128, and the split-K dense down projection."""
+    _lib.set_option(_lib.OPT_GEMM_PATH, 1)
+    _lib.set_option(_lib.OPT_TOKEN_TILE, nt)
+    T, D, I, E, k = 700, 208, 336, 16, 4
+    x, g, o = _moe_case(T, D, I, E, k, True, seed=nt + 1)
+    cfg = MoEConfig(use_moe=True, num_experts=E, num_experts_per_tok=k, moe_impl="ragged_jax",
+                    moe_ragged_decode_token_threshold=0)
+    ys = {}
+    for force in (1, 2):
+        _lib.set_option(_lib.OPT_TC_PAIR, force)
+        ys[force] = M.moe_swiglu_ffn(to_dev(x), *g, cfg=cfg)
+        _moe_check(x, g, o, E, k, ys[force])
+    parity(to_np(ys[2]), to_np(ys[1]), tol=2e-2)
+    # dense: gate/up pair mode, plain bf16 down, and the split-K fp32 down
+    rng = np.random.default_rng(nt)
+    for Tn, Dn, Hn in ((96, 512, 2048), (40, 2560, 10240)):
+        xd = normal(rng, (1, Tn, Dn)).astype(O.BF16)
+        gating, linear = normal(rng, (2, Hn, Dn), 0.02), normal(rng, (Hn, Dn), 0.02)
+        gt, lw = _gpu_q(gating, True, -1), _gpu_q(linear, True, -2)
+        ref = O.feed_forward(xd, _oracle_q(gating, True, -1), _oracle_q(linear, True, -2),
+                             transpose_gating_einsum=True, compute_dtype=np.float32)
+        for force in (1, 2):
+            _lib.set_option(_lib.OPT_TC_PAIR, force)
+            parity(to_np(feed_forward(to_dev(xd), gt, lw, transpose_gating_einsum=True)), ref)
 
 
 _FULL = {}
