@@ -60,14 +60,27 @@ typedef enum kw8_act {
  * g = scale     (Qwen3,  kappa/qwen3/norms.py:10-16).                       */
 typedef enum kw8_norm_kind { KW8_NORM_GEMMA = 0, KW8_NORM_QWEN = 1 } kw8_norm_kind;
 
+/* Storage of the int8 values of a W8 weight.
+ *   KW8_LAYOUT_KMAJOR: [groups][N][K], K contiguous (row stride K).
+ *   KW8_LAYOUT_TILED : pre-packed by kw8_pack_weight:
+ *     [groups][ceil(N/16)][2*ceil(K/128)][1024 bytes]; block (g, f, s)
+ *     holds rows 16f..16f+15 and k = 64s..64s+63, the 16 k of chunk c
+ *     (c = 0..3) of row 16f + 8h + r (h = 0..1, r = 0..7) at byte
+ *     512h + 16(8c + r); zeros past N and K.  Each kernel reads it in
+ *     whole contiguous pieces (512 B per warp load in the decode kernel,
+ *     one 16 KB box per tensor-core stage).                               */
+typedef enum kw8_layout { KW8_LAYOUT_KMAJOR = 0, KW8_LAYOUT_TILED = 1 } kw8_layout;
+
 /* One W8 weight: int8 values plus either one scale for the whole tensor
  * (kappa's Q8Weight, kappa/qwen3/quant.py:15-19) or one scale per output
  * channel (per expert when stacked): [groups][N] scales.                    */
 typedef struct kw8_weight {
-  const int8_t* q;     /* [groups][N][K] int8, K contiguous                 */
+  const int8_t* q;     /* the int8 values in `layout`                       */
   const void* scale;   /* 1 value, or [groups][N] values                    */
   int32_t scale_dtype; /* kw8_dtype of `scale`                              */
   int32_t per_channel; /* 0: one scale; 1: [groups][N] scales               */
+  int32_t layout;      /* kw8_layout of `q`                                 */
+  int32_t reserved;    /* 0                                                 */
 } kw8_weight;
 
 /* ---------------------------------------------------------------- misc -- */
@@ -97,7 +110,10 @@ int kw8_device_status(int32_t* status_out, kw8_stream_t stream);
  *            token's k rows are summed in slot order (bit-identical runs);
  *   option 3 (tensor-core GEMM over SM pairs, cta_group::2 with M = 256):
  *            0 automatic (the one-CTA kernel, faster where measured),
- *            1 never, 2 for every launch whose tile allows it.             */
+ *            1 never, 2 for every launch whose tile allows it;
+ *   option 4 (phase timing of kw8_moe_ffn_ep's deduplicated step): 1
+ *            records CUDA events at its phase boundaries (see
+ *            kw8_ep_phase_times), 0 none.                                    */
 int kw8_set_option(int32_t option, int64_t value);
 
 /* ------------------------------------------------------- quantisation -- */
@@ -129,6 +145,17 @@ int kw8_quantize(const void* w, int32_t w_dtype, int64_t outer, int64_t K,
  * out is [groups][N][K] in out_dtype.                                       */
 int kw8_dequantize(kw8_weight w, int64_t groups, int64_t N, int64_t K,
                    int32_t out_dtype, void* out, kw8_stream_t stream);
+
+/* Pre-packed weights: the load-time step that kappa's quantize_qwen3_params
+ * (kappa/qwen3/weights.py:143-170) would end with, so that every kernel
+ * reads whole contiguous pieces of the weights.  q [groups][N][K] int8
+ * (K % 16 == 0) -> tiled (kw8_packed_weight_bytes bytes, 16-byte aligned),
+ * and back.  The values are the same bits; scales are unchanged.          */
+size_t kw8_packed_weight_bytes(int64_t groups, int64_t N, int64_t K);
+int kw8_pack_weight(const int8_t* q, int64_t groups, int64_t N, int64_t K, void* tiled,
+                    kw8_stream_t stream);
+int kw8_unpack_weight(const void* tiled, int64_t groups, int64_t N, int64_t K, int8_t* q,
+                      kw8_stream_t stream);
 
 /* ----------------------------------------------------------- dense FFN -- */
 
@@ -429,7 +456,8 @@ int kw8_moe_ffn_ep(const void* x, int64_t T, int64_t D, int64_t I, int64_t E, in
  * fp32 partial [T][D], stores that partial into every rank's exchange
  * buffer (peers->red, slot [epoch & 1][rank]), passes flag phase 1 of
  * `epoch`, and sums the world partials in rank order into out (bf16; every
- * rank gets the same bits).  Needs peers->red and peers->flags only.  No
+ * rank gets the same bits).  Needs peers->red and peers->flags only
+ * (epoch 0: the device-side call count of kw8_dense_ffn_tp).  No
  * counterpart in kappa, which replicates every expert.                     */
 size_t kw8_moe_ffn_ep_decode_workspace_size(int64_t T, int64_t D, int64_t I, int64_t E, int32_t k);
 int kw8_moe_ffn_ep_decode(const void* x, int64_t T, int64_t D, int64_t I, int64_t E, int32_t k,
@@ -444,12 +472,27 @@ int kw8_moe_ffn_ep_decode(const void* x, int64_t T, int64_t D, int64_t I, int64_
  * partial of the layer output; the partials are summed over the group like
  * kw8_moe_ffn_ep_decode's (peers->red, phase 1 of `epoch`) into out (bf16,
  * the same bits on every rank).  x [T][D] bf16 (the same on every rank),
- * T <= red_rows.                                                            */
+ * T <= red_rows.
+ * epoch: as for kw8_moe_ffn_ep, or 0: the group keeps the call count in
+ * device memory (word 3 * world of each rank's flags, which must then hold
+ * 3 * world + 1 words, zero before the first call), so a sequence of calls
+ * captured in a CUDA graph takes a new tag at every replay.  Every call of
+ * a group uses one of the two forms.                                        */
 size_t kw8_dense_ffn_tp_workspace_size(int64_t T, int64_t D, int64_t H_local);
 int kw8_dense_ffn_tp(const void* x, int64_t T, int64_t D, int64_t H_local, kw8_weight gate,
                      kw8_weight up, kw8_weight down, int32_t act, void* out,
                      const kw8_ep_peers* peers, uint32_t epoch, void* workspace,
                      size_t workspace_bytes, kw8_stream_t stream);
+
+/* Milliseconds of the phases of the last timed kw8_moe_ffn_ep call on the
+ * current device (option 4 set; deduplicated step), synchronising on it:
+ * [0] route + permute, [1] slots + counts exchange (phase 0), [2] rows and
+ * pair records to their owners, [3] wait for every peer's rows (phase 1),
+ * [4] local offsets + gather of the received pairs, [5] expert FFN with the
+ * fused combine, [6] partial sums back to their sources, [7] wait for every
+ * peer's sums (phase 2), [8] final sum.  n <= 9 values are written.  No
+ * counterpart in kappa.                                                    */
+int kw8_ep_phase_times(float* ms_out, int32_t n);
 
 /* Phase `phase` (0..2) of the group barrier: with `signal` this rank first
  * marks the phase done at every peer; then it waits (bounded) until every

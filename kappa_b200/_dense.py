@@ -65,8 +65,12 @@ def linear(
     """
     if out_dtype not in (torch.bfloat16, torch.float32):
         raise ValueError(f"out_dtype must be bfloat16 or float32, got {out_dtype}")
-    K = int(w.q.shape[-1])
-    N = w.q.numel() // K
+    K = int(w.shape[-1])
+    if w.layout == _lib.LAYOUT_TILED and len(w.shape) > 2 and int(w.shape[-2]) % 16:
+        raise ValueError("a stacked tiled weight is one linear layer only when its rows per group are a multiple of 16")
+    N = 1
+    for d in w.shape[:-1]:
+        N *= int(d)
     xc = x2d.contiguous()
     if xc.dim() != 2 or int(xc.shape[1]) != K:
         raise ValueError(f"x rows have {tuple(xc.shape)[1:]} features, the weight takes {K}")

@@ -32,6 +32,10 @@ DT_BF16 = 1
 ACT_GELU_TANH = 0
 ACT_SILU = 1
 
+# kw8_layout
+LAYOUT_KMAJOR = 0
+LAYOUT_TILED = 1
+
 # kw8_norm_kind
 NORM_GEMMA = 0  # x * rsqrt(mean(x^2) + eps) * (1 + scale)
 NORM_QWEN = 1  # x * rsqrt(mean(x^2) + eps) * scale
@@ -41,6 +45,7 @@ OPT_GEMM_PATH = 0  # 0 auto, 1 tensor core, 2 weight streaming (decode kernel)
 OPT_TOKEN_TILE = 1  # 0 auto, 16..256
 OPT_DETERMINISTIC = 2  # 1: the MoE combine sums each token's k rows in a fixed order
 OPT_TC_PAIR = 3  # tensor-core GEMM over SM pairs: 0 auto (one-CTA), 1 never, 2 whenever the tile allows
+OPT_EP_TIMING = 4  # 1: CUDA events at the phase boundaries of kw8_moe_ffn_ep (kw8_ep_phase_times)
 
 
 class KW8Error(RuntimeError):
@@ -59,6 +64,8 @@ class KW8Weight(ctypes.Structure):
         ("scale", ctypes.c_void_p),
         ("scale_dtype", ctypes.c_int32),
         ("per_channel", ctypes.c_int32),
+        ("layout", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
     ]
 
 
@@ -119,6 +126,9 @@ SIGNATURES: dict[str, tuple] = {
         [_vp, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _vp, _vp, _vp, _sz, _vp],
     ),
     "kw8_dequantize": (ctypes.c_int, [KW8Weight, _i64, _i64, _i64, _i32, _vp, _vp]),
+    "kw8_packed_weight_bytes": (_sz, [_i64, _i64, _i64]),
+    "kw8_pack_weight": (ctypes.c_int, [_vp, _i64, _i64, _i64, _vp, _vp]),
+    "kw8_unpack_weight": (ctypes.c_int, [_vp, _i64, _i64, _i64, _vp, _vp]),
     "kw8_dense_ffn_workspace_size": (_sz, [_i64, _i64, _i64]),
     "kw8_dense_ffn": (
         ctypes.c_int,
@@ -170,6 +180,7 @@ SIGNATURES: dict[str, tuple] = {
         [_vp, _i64, _i64, _i64, KW8Weight, KW8Weight, KW8Weight, _i32, _vp, ctypes.POINTER(KW8EpPeers),
          ctypes.c_uint32, _vp, _sz, _vp],
     ),
+    "kw8_ep_phase_times": (ctypes.c_int, [_vp, _i32]),
     "kw8_ep_barrier": (ctypes.c_int, [ctypes.POINTER(KW8EpPeers), _i32, ctypes.c_uint32, _i32, _vp]),
     "kw8_moe_permute_ws": (ctypes.c_int, [_vp, _i64, _i32, _i64, _i64, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
     "kw8_moe_expert_ffn_workspace_size": (_sz, [_i64, _i64, _i64, _i64]),

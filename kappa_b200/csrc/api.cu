@@ -172,11 +172,22 @@ int check_weight(const kw8_weight& w, const char* name) {
               "%s: scale dtype must be f32 or bf16", name);
   KW8_REQUIRE(w.per_channel == 0 || w.per_channel == 1, KW8_ERR_INVALID_ARG,
               "%s: per_channel must be 0 or 1", name);
+  KW8_REQUIRE(w.layout == KW8_LAYOUT_KMAJOR || w.layout == KW8_LAYOUT_TILED, KW8_ERR_INVALID_ARG,
+              "%s: unknown layout %d", name, w.layout);
+  KW8_REQUIRE(w.layout == KW8_LAYOUT_KMAJOR || (reinterpret_cast<uintptr_t>(w.q) & 15) == 0,
+              KW8_ERR_UNSUPPORTED, "%s: tiled weights must be 16-byte aligned", name);
+  return KW8_OK;
+}
+
+// Paired gate/up weights are read by one kernel: one layout for both.
+int check_same_layout(const kw8_weight& a, const kw8_weight& b) {
+  KW8_REQUIRE(a.layout == b.layout, KW8_ERR_INVALID_ARG, "gate and up weights must share one layout");
   return KW8_OK;
 }
 
 GemmArgs base_args(const kw8_weight& a, const kw8_weight* b) {
   GemmArgs g{};
+  g.a_tiled = a.layout == KW8_LAYOUT_TILED ? 1 : 0;
   g.scale_a = a.scale;
   g.scale_a_dtype = a.scale_dtype;
   g.scale_a_pc = a.per_channel;
@@ -194,6 +205,7 @@ GemmArgs base_args(const kw8_weight& a, const kw8_weight* b) {
 
 StreamArgs stream_args(const kw8_weight& a, const kw8_weight* b) {
   StreamArgs g{};
+  g.w_tiled = a.layout == KW8_LAYOUT_TILED ? 1 : 0;
   g.scale_a = a.scale;
   g.scale_a_dtype = a.scale_dtype;
   g.scale_a_pc = a.per_channel;
@@ -288,6 +300,7 @@ int expert_ffn(bool streamed, const void* x, const int32_t* row_index, int64_t r
   // when `rows` (the extent of the row buffers) counts other groups' rows too.
   const int64_t hint = tile_rows >= 0 ? tile_rows : rows;
   const int mode = row_token != nullptr ? EPI_COMBINE_F32 : EPI_PLAIN_BF16;
+  if (int rc = check_same_layout(gate, up)) return rc;
   if (streamed) {
     const int nt = stream_nt(rows_hint(hint, E));
     StreamArgs g = stream_args(gate, &up);
@@ -418,6 +431,7 @@ int64_t dense_down_part_floats(int64_t T, int64_t D, int64_t H) {
 // Gate/up GEMM with the activation epilogue: h [T][H] bf16.
 int dense_gate_up(const void* x, int64_t T, int64_t D, int64_t H, const kw8_weight& gate,
                   const kw8_weight& up, int act, __nv_bfloat16* h, cudaStream_t stream) {
+  if (int rc = check_same_layout(gate, up)) return rc;
   const int epi_pair = act == KW8_ACT_GELU_TANH ? EPI_PAIR_GELU : EPI_PAIR_SILU;
   if (use_stream(static_cast<double>(T))) {
     StreamArgs g = stream_args(gate, &up);
@@ -615,7 +629,7 @@ extern "C" {
 
 const char* kw8_last_error(void) { return kw8::last_error(); }
 
-int32_t kw8_abi_version(void) { return 2; }
+int32_t kw8_abi_version(void) { return 3; }
 
 int kw8_device_status(int32_t* status_out, kw8_stream_t stream) {
   KW8_API_BEGIN
@@ -633,6 +647,11 @@ int kw8_set_option(int32_t option, int64_t value) {
     KW8_REQUIRE(value == 0 || (value >= 16 && value <= kTcMaxNT && value % 16 == 0),
                 KW8_ERR_INVALID_ARG, "token tile must be 0 or a multiple of 16 in [16, 256]");
     g_opt_token_tile.store(static_cast<int>(value));
+    return KW8_OK;
+  }
+  if (option == 4) {
+    KW8_REQUIRE(value == 0 || value == 1, KW8_ERR_INVALID_ARG, "EP phase timing must be 0 or 1");
+    g_opt_ep_timing.store(static_cast<int>(value));
     return KW8_OK;
   }
   if (option == 3) {
@@ -667,7 +686,25 @@ int kw8_dequantize(kw8_weight w, int64_t groups, int64_t N, int64_t K, int32_t o
   KW8_API_BEGIN
   int rc = check_weight(w, "weight");
   if (rc) return rc;
+  KW8_REQUIRE(w.layout == KW8_LAYOUT_KMAJOR, KW8_ERR_UNSUPPORTED,
+              "dequantize takes K-major values (kw8_unpack_weight a tiled weight first)");
   return launch_dequantize(w, groups, N, K, out_dtype, out, stream);
+}
+
+size_t kw8_packed_weight_bytes(int64_t groups, int64_t N, int64_t K) {
+  if (groups <= 0 || N <= 0 || K <= 0) return 0;
+  return static_cast<size_t>(tiled_bytes(groups, N, K));
+}
+
+int kw8_pack_weight(const int8_t* q, int64_t groups, int64_t N, int64_t K, void* tiled, kw8_stream_t stream) {
+  KW8_API_BEGIN
+  return launch_pack(q, groups, N, K, tiled, stream);
+}
+
+int kw8_unpack_weight(const void* tiled, int64_t groups, int64_t N, int64_t K, int8_t* q,
+                      kw8_stream_t stream) {
+  KW8_API_BEGIN
+  return launch_unpack(tiled, groups, N, K, q, stream);
 }
 
 size_t kw8_dense_ffn_workspace_size(int64_t T, int64_t D, int64_t H) {
@@ -909,6 +946,7 @@ int kw8_embed_gather(const int32_t* tokens, int64_t n, kw8_weight table, int64_t
   KW8_API_BEGIN
   int rc = check_weight(table, "table");
   if (rc) return rc;
+  KW8_REQUIRE(table.layout == KW8_LAYOUT_KMAJOR, KW8_ERR_UNSUPPORTED, "embedding tables are gathered K-major");
   return launch_embed_gather(tokens, n, table, V, D, out_dtype, out, stream);
 }
 

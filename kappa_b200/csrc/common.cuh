@@ -12,6 +12,7 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <string>
 
@@ -59,6 +60,10 @@ __device__ __forceinline__ uint64_t global_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+
+// Process-wide option (kw8_set_option 4): time the phases of
+// kw8_moe_ffn_ep with CUDA events (read back with kw8_ep_phase_times).
+inline std::atomic<int> g_opt_ep_timing{0};
 
 // ----------------------------------------------------------- small utils --
 
@@ -254,6 +259,16 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst,
       : "memory");
 }
 
+// 3-D tiled TMA load (no multicast): box at coordinates (c0, c1, c2).
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
+                                            int32_t c0, int32_t c1, int32_t c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_"
+      "tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05 --
 
 __device__ __forceinline__ void tc_fence_before() {
@@ -417,5 +432,11 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
                  int esize, uint64_t rows, uint64_t cols, uint64_t pitch_bytes,
                  uint32_t box_cols, uint32_t box_rows,
                  CUtensorMapSwizzle swizzle);
+
+// Tensor map of a pre-packed (tiled) int8 weight with `tile_rows` feature
+// tiles of `steps` 1 KB blocks each, viewed as [tile_rows][steps * 4][256 B];
+// box: 2 steps (one 128-k stage) of `box_tiles` feature tiles.
+int make_tmap_tiled(CUtensorMap* map, const void* base, uint64_t tile_rows, uint64_t steps,
+                    uint32_t box_tiles);
 
 }  // namespace kw8

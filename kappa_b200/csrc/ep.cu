@@ -191,9 +191,19 @@ __global__ void ep_counts_kernel(const int32_t* __restrict__ sizes, int E, const
 // epoch & 1: a rank can start call e + 1 while a slower one still reads the
 // slots of call e, but not call e + 2 (its phase waits for every rank's
 // call e + 1), so two slot sets suffice.
+// Call tag of a one-shot sum: the host's `epoch`, or (epoch == 0) the
+// group's device-side counter at ctr (the last finished call) plus one, so
+// that a call captured in a CUDA graph gets a new tag at every replay.
+__device__ __forceinline__ uint32_t call_epoch(uint32_t epoch, const uint32_t* ctr) {
+  return epoch != 0 ? epoch : *reinterpret_cast<const volatile uint32_t*>(ctr) + 1u;
+}
+
 __global__ void __launch_bounds__(kEpThreads)
     ep_push_partials_kernel(const float4* __restrict__ part, int splits, int64_t split4, int64_t n4,
-                            const uint64_t* __restrict__ peer_red, int world, int64_t dst_off4) {
+                            const uint64_t* __restrict__ peer_red, int world, int rank, int64_t slot4,
+                            uint32_t epoch, const uint32_t* ctr) {
+  const uint32_t e = call_epoch(epoch, ctr);
+  const int64_t dst_off4 = static_cast<int64_t>(e & 1u) * world * slot4 + rank * slot4;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     float4 v = part[i];
@@ -206,9 +216,27 @@ __global__ void __launch_bounds__(kEpThreads)
   __threadfence_system();
 }
 
+// Phase 1 of the call's tag: mark it at every rank, wait for every rank;
+// with a device counter, then advance it (one thread, after every wait).
+__global__ void ep_exchange_barrier_kernel(const uint64_t* __restrict__ flags, uint32_t* own_flags, int world,
+                                           int rank, uint32_t epoch, uint32_t* ctr) {
+  const int lane = threadIdx.x;
+  const uint32_t e = call_epoch(epoch, ctr);
+  if (lane < world) {
+    __threadfence_system();
+    flag_release(reinterpret_cast<uint32_t*>(flags[lane]) + world + rank, e);
+  }
+  if (lane < world) flag_wait(own_flags + world + lane, e);
+  __syncwarp();
+  if (epoch == 0 && lane == 0) *reinterpret_cast<volatile uint32_t*>(ctr) = e;
+}
+
 __global__ void __launch_bounds__(kEpThreads)
-    ep_sum_partials_kernel(const float4* __restrict__ slots, int world, int64_t n4, int64_t slot4,
-                           uint2* __restrict__ out) {
+    ep_sum_partials_kernel(const float4* __restrict__ red, int world, int64_t n4, int64_t slot4, uint32_t epoch,
+                           const uint32_t* ctr, uint2* __restrict__ out) {
+  // After the barrier the counter holds this call's tag (epoch == 0).
+  const uint32_t e = epoch != 0 ? epoch : *reinterpret_cast<const volatile uint32_t*>(ctr);
+  const float4* slots = red + static_cast<int64_t>(e & 1u) * world * slot4;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     float4 a = slots[i];
@@ -310,17 +338,16 @@ int launch_ep_allreduce(const float* part, int splits, int64_t split_stride, int
               KW8_ERR_UNSUPPORTED, "partial sums need 16-byte aligned rows");
   const int64_t n4 = T * D / 4;
   const int64_t slot4 = red_rows * D / 4;  // one rank's slot
-  const int64_t parity4 = static_cast<int64_t>(epoch & 1u) * world * slot4;
-  if (n4 > 0) {
-    ep_push_partials_kernel<<<ep_grid_blocks(n4), kEpThreads, 0, stream>>>(
-        reinterpret_cast<const float4*>(part), splits, split_stride / 4, n4, peer_red, world,
-        parity4 + rank * slot4);
-    KW8_CHECK_LAUNCH();
-  }
-  int rc = launch_ep_barrier(flags, own_flags, world, rank, 1, epoch, true, stream);
-  if (rc || n4 == 0) return rc;
+  uint32_t* ctr = own_flags + 3 * world;   // device call counter (epoch == 0)
+  // Every rank takes every phase, also with no rows (the others wait on it).
+  ep_push_partials_kernel<<<ep_grid_blocks(std::max<int64_t>(n4, 1)), kEpThreads, 0, stream>>>(
+      reinterpret_cast<const float4*>(part), splits, split_stride / 4, n4, peer_red, world, rank, slot4, epoch, ctr);
+  KW8_CHECK_LAUNCH();
+  ep_exchange_barrier_kernel<<<1, 32, 0, stream>>>(flags, own_flags, world, rank, epoch, ctr);
+  KW8_CHECK_LAUNCH();
+  if (n4 == 0) return KW8_OK;
   ep_sum_partials_kernel<<<ep_grid_blocks(n4), kEpThreads, 0, stream>>>(
-      reinterpret_cast<const float4*>(own_red) + parity4, world, n4, slot4, static_cast<uint2*>(out));
+      reinterpret_cast<const float4*>(own_red), world, n4, slot4, epoch, ctr, static_cast<uint2*>(out));
   KW8_CHECK_LAUNCH();
   return KW8_OK;
 }

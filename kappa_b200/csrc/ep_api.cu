@@ -62,6 +62,36 @@ int check_group(const kw8_ep_peers* p) {
   return KW8_OK;
 }
 
+// Phase timing of kw8_moe_ffn_ep (option 4): CUDA events recorded on the
+// call's stream at the phase boundaries of the last call on each device.
+constexpr int kEpPhases = 9;
+cudaEvent_t g_ep_events[64][kEpPhases + 1] = {};
+bool g_ep_recorded[64] = {};
+
+struct PhaseClock {
+  int dev = -1;
+  cudaStream_t stream;
+  explicit PhaseClock(cudaStream_t s) : stream(s) {
+    if (!g_opt_ep_timing.load()) return;
+    int d = 0;
+    if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= 64) return;
+    for (int i = 0; i <= kEpPhases; ++i)
+      if (g_ep_events[d][i] == nullptr && cudaEventCreate(&g_ep_events[d][i]) != cudaSuccess) return;
+    dev = d;
+    g_ep_recorded[d] = false;
+    mark(0);
+  }
+  void mark(int i) {
+    if (dev >= 0) cudaEventRecord(g_ep_events[dev][i], stream);
+  }
+  void done() {
+    if (dev >= 0) {
+      mark(kEpPhases);
+      g_ep_recorded[dev] = true;
+    }
+  }
+};
+
 int check_peers(const kw8_ep_peers* p) {
   KW8_REQUIRE(p != nullptr, KW8_ERR_INVALID_ARG, "null peers");
   KW8_REQUIRE(p->world >= 1 && p->world <= kEpMaxRanks && p->rank >= 0 && p->rank < p->world,
@@ -184,6 +214,7 @@ int kw8_moe_ffn_ep(const void* x, int64_t T, int64_t D, int64_t I, int64_t E, in
   cudaStream_t stream = static_cast<cudaStream_t>(stream_in);
   const int64_t e_loc = E / world;
   const int64_t recv_rows = static_cast<int64_t>(world) * peers->max_tokens * k;
+  PhaseClock clock(stream);
   // Route and permute this rank's tokens (a rank without tokens still takes
   // part: its counts are zero).
   if (T > 0) {
@@ -195,6 +226,7 @@ int kw8_moe_ffn_ep(const void* x, int64_t T, int64_t D, int64_t I, int64_t E, in
                             b.group_sizes, b.group_offsets, stream, dedup ? b.w : nullptr,
                             dedup ? b.sorted_w : nullptr);
   if (rc) return rc;
+  clock.mark(1);
   if (dedup) {
     // Each token once per owning rank (ep_dedup.cu).
     KW8_REQUIRE(peers->meta && peers->ret && peers->own_rows && peers->own_meta && peers->own_ret &&
@@ -206,12 +238,15 @@ int kw8_moe_ffn_ep(const void* x, int64_t T, int64_t D, int64_t I, int64_t E, in
     rc = launch_ep_counts2(b.group_sizes, b.u_cnt, E, peers->counts, peers->flags, peers->own_flags, world,
                            rank, epoch, stream);
     if (rc) return rc;
+    clock.mark(2);
     const int32_t* cnt = peers->own_counts + static_cast<int64_t>(epoch & 1u) * world * (E + world);
     rc = launch_ep_dispatch2(x, T, k, D, b.sorted_token, b.group_offsets, b.sorted_w, b.tok_slot, cnt, world,
                              rank, E, pair_cap, peers->rows, peers->meta, stream);
     if (rc) return rc;
+    clock.mark(3);
     rc = launch_ep_barrier(peers->flags, peers->own_flags, world, rank, 1, epoch, true, stream);
     if (rc) return rc;
+    clock.mark(4);
     rc = launch_ep_local_offsets(cnt, world, rank, E, b.loc_off, stream, E + world);
     if (rc) return rc;
     const int32_t* meta_u = static_cast<const int32_t*>(peers->own_meta);
@@ -219,18 +254,24 @@ int kw8_moe_ffn_ep(const void* x, int64_t T, int64_t D, int64_t I, int64_t E, in
     rc = launch_ep_gather2(peers->own_rows, meta_u, b.loc_off, e_loc, cnt, world, rank, E, D, recv_rows,
                            b.ys_loc, b.part, stream);
     if (rc) return rc;
+    clock.mark(5);
     // The down projection adds w * y of every pair into its token's fp32
     // partial row (rows indexed by the pair records).
     rc = expert_ffn(use_stream(rows_hint(recv_rows, e_loc)), b.ys_loc, nullptr, recv_rows, D, I, e_loc,
                     b.loc_off, gate_local, up_local, down_local, b.part, b.eb, stream, meta_u, meta_w);
     if (rc) return rc;
+    clock.mark(6);
     rc = launch_ep_return2(b.part, D, cnt, world, rank, E, peers->max_tokens, peers->ret, peers->ret_f32 != 0,
                            stream);
     if (rc) return rc;
+    clock.mark(7);
     rc = launch_ep_barrier(peers->flags, peers->own_flags, world, rank, 2, epoch, true, stream);
     if (rc) return rc;
-    return launch_ep_final2(peers->own_ret, b.tok_slot, T, world, peers->max_tokens, D, peers->ret_f32 != 0, out,
-                            stream);
+    clock.mark(8);
+    rc = launch_ep_final2(peers->own_ret, b.tok_slot, T, world, peers->max_tokens, D, peers->ret_f32 != 0, out,
+                          stream);
+    if (!rc) clock.done();
+    return rc;
   }
   // Counts to every peer (phase 0), rows to their expert owners (phase 1).
   rc = launch_ep_counts(b.group_sizes, E, peers->counts, peers->flags, peers->own_flags, world, rank,
@@ -359,6 +400,19 @@ int kw8_dense_ffn_tp(const void* x, int64_t T, int64_t D, int64_t H_local, kw8_w
   // The K-split slices of this rank's partial are summed while they are pushed.
   return launch_ep_allreduce(part, splits, T * D, T, D, peers->red, peers->own_red, peers->red_rows,
                              peers->flags, peers->own_flags, peers->world, peers->rank, epoch, out, stream);
+}
+
+int kw8_ep_phase_times(float* ms_out, int32_t n) {
+  KW8_API_BEGIN
+  int dev = 0;
+  KW8_CUDA_TRY(cudaGetDevice(&dev));
+  KW8_REQUIRE(ms_out && n >= 1 && dev >= 0 && dev < 64, KW8_ERR_INVALID_ARG, "bad arguments");
+  KW8_REQUIRE(g_ep_recorded[dev], KW8_ERR_INVALID_ARG,
+              "no timed kw8_moe_ffn_ep call on this device (set option 4 and take the deduplicated step)");
+  KW8_CUDA_TRY(cudaEventSynchronize(g_ep_events[dev][kEpPhases]));
+  for (int i = 0; i < n && i < kEpPhases; ++i)
+    KW8_CUDA_TRY(cudaEventElapsedTime(&ms_out[i], g_ep_events[dev][i], g_ep_events[dev][i + 1]));
+  return KW8_OK;
 }
 
 int kw8_ep_barrier(const kw8_ep_peers* peers, int32_t phase, uint32_t epoch, int32_t signal,

@@ -60,7 +60,7 @@ __device__ __forceinline__ void widen16(const uint4& v, uint32_t (&a)[8]) {
   i8x4_to_bf16x4(v.w, a[6], a[7]);
 }
 
-template <int kMode, int kNT>
+template <int kMode, int kNT, bool kTiled>
 __global__ void __launch_bounds__(kStThreads,
                                   stream_smem_bytes(epi_is_pair(kMode), kNT) <= 113 * 1024 ? 2 : 1)
     w8_stream_kernel(const int8_t* __restrict__ wa, const int8_t* __restrict__ wb,
@@ -112,11 +112,28 @@ __global__ void __launch_bounds__(kStThreads,
   const int64_t fr0 = wbase + min(f0 + g, p.N_out - 1);
   const int64_t fr1 = wbase + min(f0 + g + 8, p.N_out - 1);
   const int8_t* w_rows[kMats][2];
-  w_rows[0][0] = wa + fr0 * p.K;
-  w_rows[0][1] = wa + fr1 * p.K;
-  if constexpr (kPair) {
-    w_rows[1][0] = wb + fr0 * p.K;
-    w_rows[1][1] = wb + fr1 * p.K;
+  if constexpr (kTiled) {
+    // Block (group, ftile, step 0) of the tiled layout; lane (g, c) copies
+    // its 16 bytes of row g at 16 (8 c + g) and of row g + 8 at 512 + that
+    // (zeros past N and K are stored, so no fill is needed).  A step is
+    // 1 KB further on: "k" below counts bytes of blocks, 64 per 1 KB.
+    const int64_t blk_off =
+        tile_ok ? (static_cast<int64_t>(group) * p.tile_ftiles + ftile) * p.tile_steps * kTiledBlock : 0;
+    const int8_t* blk0 = wa + blk_off;
+    w_rows[0][0] = blk0 + 16 * (8 * c + g);
+    w_rows[0][1] = blk0 + 512 + 16 * (8 * c + g);
+    if constexpr (kPair) {
+      const int8_t* blk1 = wb + (blk0 - wa);
+      w_rows[1][0] = blk1 + 16 * (8 * c + g);
+      w_rows[1][1] = blk1 + 512 + 16 * (8 * c + g);
+    }
+  } else {
+    w_rows[0][0] = wa + fr0 * p.K;
+    w_rows[0][1] = wa + fr1 * p.K;
+    if constexpr (kPair) {
+      w_rows[1][0] = wb + fr0 * p.K;
+      w_rows[1][1] = wb + fr1 * p.K;
+    }
   }
 
   float s_a[2], s_b[2] = {0.f, 0.f};
@@ -152,7 +169,10 @@ __global__ void __launch_bounds__(kStThreads,
       // The last step of K is partial when K % 64 != 0: its lanes past K
       // zero-fill from a clamped (valid) address.
       const int tail_j = (p.K % kStStepK != 0 && s_hi == nsteps) ? n - 1 : -1;
-      const uint32_t wn0 = ok0 ? 16u : 0u, wn1 = ok1 ? 16u : 0u;
+      // Tiled weights store zeros past N: every row copies.
+      const uint32_t wn0 = (kTiled || ok0) ? 16u : 0u, wn1 = (kTiled || ok1) ? 16u : 0u;
+      // Bytes between consecutive steps of a weight row, and the first.
+      constexpr int kWStep = kTiled ? kTiledBlock : kStStepK;
       uint32_t xn[kNTiles];
 #pragma unroll
       for (int t = 0; t < kNTiles; ++t) xn[t] = x_ok[t] ? 16u : 0u;
@@ -161,10 +181,11 @@ __global__ void __launch_bounds__(kStThreads,
       const int k_first = s_lo * kStStepK + c * 16;
       const int8_t* wp[kMats][2];
       const __nv_bfloat16* xp[kNTiles];
+      const int64_t w_first = kTiled ? static_cast<int64_t>(s_lo) * kTiledBlock : k_first;
 #pragma unroll
       for (int m = 0; m < kMats; ++m) {
-        wp[m][0] = w_rows[m][0] + k_first;
-        wp[m][1] = w_rows[m][1] + k_first;
+        wp[m][0] = w_rows[m][0] + w_first;
+        wp[m][1] = w_rows[m][1] + w_first;
       }
 #pragma unroll
       for (int t = 0; t < kNTiles; ++t) xp[t] = x_rows[t] + k_first;
@@ -175,8 +196,8 @@ __global__ void __launch_bounds__(kStThreads,
         if (j != tail_j) {
 #pragma unroll
           for (int m = 0; m < kMats; ++m) {
-            cp_async_cg16(dst + (2 * m) * 32, wp[m][0] + off * kStStepK, wn0);
-            cp_async_cg16(dst + (2 * m + 1) * 32, wp[m][1] + off * kStStepK, wn1);
+            cp_async_cg16(dst + (2 * m) * 32, wp[m][0] + off * kWStep, wn0);
+            cp_async_cg16(dst + (2 * m + 1) * 32, wp[m][1] + off * kWStep, wn1);
           }
 #pragma unroll
           for (int t = 0; t < kNTiles; ++t) {
@@ -192,8 +213,13 @@ __global__ void __launch_bounds__(kStThreads,
           const int o = off * kStStepK - back;
 #pragma unroll
           for (int m = 0; m < kMats; ++m) {
-            cp_async_cg16(dst + (2 * m) * 32, wp[m][0] + o, kok ? wn0 : 0u);
-            cp_async_cg16(dst + (2 * m + 1) * 32, wp[m][1] + o, kok ? wn1 : 0u);
+            if constexpr (kTiled) {  // the block holds zeros past K
+              cp_async_cg16(dst + (2 * m) * 32, wp[m][0] + off * kWStep, wn0);
+              cp_async_cg16(dst + (2 * m + 1) * 32, wp[m][1] + off * kWStep, wn1);
+            } else {
+              cp_async_cg16(dst + (2 * m) * 32, wp[m][0] + o, kok ? wn0 : 0u);
+              cp_async_cg16(dst + (2 * m + 1) * 32, wp[m][1] + o, kok ? wn1 : 0u);
+            }
           }
 #pragma unroll
           for (int t = 0; t < kNTiles; ++t) {
@@ -242,8 +268,8 @@ __global__ void __launch_bounds__(kStThreads,
         }
 #pragma unroll
         for (int m = 0; m < kMats; ++m) {
-          wp[m][0] += kStages * kStStepK;
-          wp[m][1] += kStages * kStStepK;
+          wp[m][0] += kStages * kWStep;
+          wp[m][1] += kStages * kWStep;
         }
 #pragma unroll
         for (int t = 0; t < kNTiles; ++t) xp[t] += kStages * kStStepK;
@@ -309,7 +335,7 @@ __global__ void __launch_bounds__(kStThreads,
   }
 }
 
-template <int kMode, int kNT>
+template <int kMode, int kNT, bool kTiled>
 int launch_stream_nt(dim3 grid, const int8_t* wa, const int8_t* wb, const void* x, int64_t ldx,
                      const StreamArgs& a, cudaStream_t stream) {
   constexpr int smem = stream_smem_bytes(epi_is_pair(kMode), kNT);
@@ -318,27 +344,34 @@ int launch_stream_nt(dim3 grid, const int8_t* wa, const int8_t* wb, const void* 
   int dev = 0;
   KW8_CUDA_TRY(cudaGetDevice(&dev));
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    KW8_CUDA_TRY(cudaFuncSetAttribute(w8_stream_kernel<kMode, kNT>,
+    KW8_CUDA_TRY(cudaFuncSetAttribute(w8_stream_kernel<kMode, kNT, kTiled>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     attr_set[dev] = true;
   }
-  w8_stream_kernel<kMode, kNT><<<grid, kStThreads, smem, stream>>>(
+  w8_stream_kernel<kMode, kNT, kTiled><<<grid, kStThreads, smem, stream>>>(
       wa, wb, static_cast<const __nv_bfloat16*>(x), ldx, a);
   KW8_CHECK_LAUNCH();
   return KW8_OK;
 }
 
+template <int kMode, bool kTiled>
+int launch_stream_tiled(int nt, dim3 grid, const int8_t* wa, const int8_t* wb, const void* x, int64_t ldx,
+                        const StreamArgs& a, cudaStream_t stream) {
+  switch (nt) {
+    case 8:
+      return launch_stream_nt<kMode, 8, kTiled>(grid, wa, wb, x, ldx, a, stream);
+    case 16:
+      return launch_stream_nt<kMode, 16, kTiled>(grid, wa, wb, x, ldx, a, stream);
+    default:
+      return launch_stream_nt<kMode, 32, kTiled>(grid, wa, wb, x, ldx, a, stream);
+  }
+}
+
 template <int kMode>
 int launch_stream_mode(int nt, dim3 grid, const int8_t* wa, const int8_t* wb, const void* x,
                        int64_t ldx, const StreamArgs& a, cudaStream_t stream) {
-  switch (nt) {
-    case 8:
-      return launch_stream_nt<kMode, 8>(grid, wa, wb, x, ldx, a, stream);
-    case 16:
-      return launch_stream_nt<kMode, 16>(grid, wa, wb, x, ldx, a, stream);
-    default:
-      return launch_stream_nt<kMode, 32>(grid, wa, wb, x, ldx, a, stream);
-  }
+  if (a.w_tiled) return launch_stream_tiled<kMode, true>(nt, grid, wa, wb, x, ldx, a, stream);
+  return launch_stream_tiled<kMode, false>(nt, grid, wa, wb, x, ldx, a, stream);
 }
 
 }  // namespace
@@ -399,6 +432,10 @@ int launch_gemm_stream(int mode, const int8_t* wa, const int8_t* wb, int64_t gro
   StreamArgs a = args_in;
   a.K = static_cast<int>(K);
   a.N_out = static_cast<int>(N_out);
+  if (a.w_tiled) {
+    a.tile_ftiles = static_cast<int>(tiled_ftiles(N_out));
+    a.tile_steps = static_cast<int>(tiled_steps(K));
+  }
   if (a.group_offsets == nullptr && a.dense_rows <= 0) return KW8_OK;
 
   const StreamPlan plan = stream_plan(mode, nt, a.group_offsets != nullptr, a.active_groups != nullptr,

@@ -61,6 +61,10 @@ struct StreamArgs {
   // split_stride floats, the caller sums them; other modes: 1).
   int kz_max;
   int64_t split_stride;
+  // Weights pre-packed in the tiled layout (kw8_pack_weight): tile_steps
+  // 1 KB blocks per 16-row feature tile, tile_ftiles tiles per group.
+  int w_tiled;
+  int tile_steps, tile_ftiles;
   // Filled in by the launcher (stream_plan).
   int ks;  // warps of a CTA splitting its K range (1, 2, 4 or 8)
   int kz;  // CTAs splitting K

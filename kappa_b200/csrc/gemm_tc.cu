@@ -266,7 +266,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           else
             mbar_arrive(&full[stage]);
           if (part == 0) {
-            if (kPair) {
+            if (p.a_tiled) {
+              // One box = the stage's 8 (paired: 4 + 4) feature tiles x 2 steps.
+              const int z = ti.group * p.tile_ftiles + ti.mt * (kPair ? 4 : 8);
+              tma_load_3d(dst, &map_a0, &full[stage], 0, kt * 8, z);
+              if (kPair) tma_load_3d(dst + kTcATileBytes / 2, &map_a1, &full[stage], 0, kt * 8, z);
+            } else if (kPair) {
               tma_load_2d(dst, &map_a0, &full[stage], kt * kTcBK, a_row);
               tma_load_2d(dst + kTcATileBytes / 2, &map_a1, &full[stage], kt * kTcBK, a_row);
             } else {
@@ -359,10 +364,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           break;
         }
         const uint8_t* a_src = smem + stage * stage_bytes + src_row * kTcBK;
+        // Tiled weights: row r's chunk c of step kh at (r/16) * 2 KB + kh * 1 KB
+        // + 512 ((r % 16) / 8) + 16 (8 c + r % 8).
+        const uint8_t* t_src = smem + stage * stage_bytes + (src_row >> 4) * 2048 + kh * 1024 +
+                               ((src_row >> 3) & 1) * 512 + (src_row & 7) * 16;
         uint32_t v[32];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          const uint4 w = *reinterpret_cast<const uint4*>(a_src + (((kh * 4 + c) ^ swz) << 4));
+          const uint4 w = p.a_tiled ? *reinterpret_cast<const uint4*>(t_src + c * 128)
+                                    : *reinterpret_cast<const uint4*>(a_src + (((kh * 4 + c) ^ swz) << 4));
           i8x4_to_bf16x4(w.x, v[c * 8 + 0], v[c * 8 + 1]);
           i8x4_to_bf16x4(w.y, v[c * 8 + 2], v[c * 8 + 3]);
           i8x4_to_bf16x4(w.z, v[c * 8 + 4], v[c * 8 + 5]);
@@ -522,7 +532,7 @@ int launch_gemm_tc(int mode, const int8_t* wa, const int8_t* wb, int64_t groups,
                     args.split_stride > 0,
                 KW8_ERR_INVALID_ARG, "split K needs fp32 output, non-empty ranges and a stride");
   }
-  if (gemm_tc_pair_ok(mode, N_out, args.nt, g_opt_tc_pair.load())) {
+  if (!args.a_tiled && gemm_tc_pair_ok(mode, N_out, args.nt, g_opt_tc_pair.load())) {
     // Feature tiles of 256 rows over an SM pair (gemm_tc2.cu).
     const int64_t max_entries = args.tiles == nullptr ? 0 : groups + (x_rows + args.nt - 1) / args.nt;
     return launch_gemm_tc2(mode, wa, wb, groups, N_out, K, x, x_rows, ldx, args, max_entries, stream);
@@ -541,18 +551,28 @@ int launch_gemm_tc(int mode, const int8_t* wa, const int8_t* wb, int64_t groups,
 
   CUtensorMap map_a0, map_a1, map_b;
   const uint32_t a_box_rows = pair ? 64 : 128;
-  int rc = make_tmap_2d(&map_a0, wa, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1,
-                        static_cast<uint64_t>(groups * N_out), static_cast<uint64_t>(K),
-                        static_cast<uint64_t>(K), kTcBK, a_box_rows,
-                        CU_TENSOR_MAP_SWIZZLE_128B);
-  if (rc) return rc;
-  if (pair) {
-    rc = make_tmap_2d(&map_a1, wb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1,
-                      static_cast<uint64_t>(groups * N_out), static_cast<uint64_t>(K),
-                      static_cast<uint64_t>(K), kTcBK, a_box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
+  int rc;
+  if (args.a_tiled) {
+    args.tile_ftiles = static_cast<int>(tiled_ftiles(N_out));
+    args.tile_steps = static_cast<int>(tiled_steps(K));
+    const uint64_t tile_rows = static_cast<uint64_t>(groups) * args.tile_ftiles;
+    rc = make_tmap_tiled(&map_a0, wa, tile_rows, args.tile_steps, a_box_rows / 16);
+    if (!rc && pair) rc = make_tmap_tiled(&map_a1, wb, tile_rows, args.tile_steps, a_box_rows / 16);
     if (rc) return rc;
+    if (!pair) map_a1 = map_a0;
   } else {
-    map_a1 = map_a0;
+    rc = make_tmap_2d(&map_a0, wa, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, static_cast<uint64_t>(groups * N_out),
+                      static_cast<uint64_t>(K), static_cast<uint64_t>(K), kTcBK, a_box_rows,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    if (pair) {
+      rc = make_tmap_2d(&map_a1, wb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, static_cast<uint64_t>(groups * N_out),
+                        static_cast<uint64_t>(K), static_cast<uint64_t>(K), kTcBK, a_box_rows,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+      if (rc) return rc;
+    } else {
+      map_a1 = map_a0;
+    }
   }
   rc = make_tmap_2d(&map_b, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
                     static_cast<uint64_t>(x_rows), static_cast<uint64_t>(K),

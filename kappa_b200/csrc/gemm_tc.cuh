@@ -46,6 +46,7 @@
 #include <atomic>
 
 #include "common.cuh"
+#include "pack.cuh"
 
 namespace kw8 {
 
@@ -93,6 +94,11 @@ struct GemmArgs {
   // EPI_COMBINE_F32 only: token and routing weight of every sorted row.
   const int32_t* row_token;
   const float* row_weight;
+  // Weights pre-packed in the tiled layout (kw8_pack_weight) instead of
+  // K-major rows: tile_steps 1 KB blocks per 16-row feature tile.
+  int a_tiled;
+  int tile_steps;
+  int tile_ftiles;  // feature tiles per group
   // Split K (EPI_PLAIN_F32 only): each tile's k tiles are cut into
   // k_splits near-equal ranges run by different CTAs; range s writes its
   // partial sums to out + s * split_stride floats (0 or 1: no split).

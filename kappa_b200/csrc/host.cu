@@ -76,6 +76,27 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
   return KW8_OK;
 }
 
+int make_tmap_tiled(CUtensorMap* map, const void* base, uint64_t tile_rows, uint64_t steps,
+                    uint32_t box_tiles) {
+  EncodeTiledFn fn = encode_fn();
+  KW8_REQUIRE(fn != nullptr, KW8_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  KW8_REQUIRE((reinterpret_cast<uintptr_t>(base) & 15) == 0, KW8_ERR_UNSUPPORTED,
+              "TMA base address must be 16-byte aligned");
+  KW8_REQUIRE(box_tiles >= 1 && box_tiles <= 256 && steps % 2 == 0 && tile_rows >= 1, KW8_ERR_INVALID_ARG,
+              "bad tiled TMA box");
+  // [tile_rows][steps * 4][256 bytes]; a box is [box_tiles][8][256]: the
+  // two 1 KB blocks of one 128-k stage of box_tiles feature tiles.
+  const cuuint64_t dims[3] = {256, steps * 4, tile_rows};
+  const cuuint64_t strides[2] = {256, steps * 1024};
+  const cuuint32_t box[3] = {256, 8, box_tiles};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  KW8_REQUIRE(r == CUDA_SUCCESS, KW8_ERR_CUDA, "cuTensorMapEncodeTiled (tiled weights) failed (%d)", (int)r);
+  return KW8_OK;
+}
+
 int read_device_status(int32_t* out, cudaStream_t stream) {
   KW8_REQUIRE(out != nullptr, KW8_ERR_INVALID_ARG, "null status pointer");
   KW8_CUDA_TRY(cudaStreamSynchronize(stream));

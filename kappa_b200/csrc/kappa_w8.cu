@@ -2,6 +2,7 @@
 // status word and are compiled together so no relocatable device code is
 // needed.
 #include "host.cu"
+#include "pack.cu"
 #include "quant.cu"
 #include "gemm_tc.cu"
 #include "gemm_tc2.cu"

@@ -29,10 +29,10 @@ def ffn_sub_block(
     """``h + post_norm(feed_forward(rms_norm(h, pre)))``; ``post_ffw_norm_scale=None`` skips the post-norm."""
     g = kmajor(gating_weights, -1 if transpose_gating_einsum else -2, "gating_weights")
     lw = kmajor(output_weights, -2, "output_weights")
-    if g.q.dim() != 3 or g.q.shape[0] != 2:
+    if len(g.shape) != 3 or g.shape[0] != 2:
         raise ValueError(f"gating_weights must be [2, ., .], got {tuple(gating_weights.values.shape)}")
-    hidden, embed = int(g.q.shape[1]), int(g.q.shape[2])
-    if tuple(lw.q.shape) != (embed, hidden):
+    hidden, embed = int(g.shape[1]), int(g.shape[2])
+    if tuple(lw.shape) != (embed, hidden):
         raise ValueError(f"output_weights shape {tuple(output_weights.values.shape)} != ({hidden}, {embed})")
     _dense.check_x(h, embed)
     return _norm.dense_block(h, g.struct(0), g.struct(hidden), lw.struct(), hidden=hidden, act=_lib.ACT_GELU_TANH,

@@ -30,10 +30,10 @@ def feed_forward(
     """
     g = kmajor(gating_w, -1 if transpose_gating_einsum else -2, "gating_w")
     lw = kmajor(linear_w, -2, "linear_w")
-    if g.q.dim() != 3 or g.q.shape[0] != 2:
+    if len(g.shape) != 3 or g.shape[0] != 2:
         raise ValueError(f"gating_w must be [2, ., .], got {tuple(gating_w.values.shape)}")
-    hidden, embed = int(g.q.shape[1]), int(g.q.shape[2])
-    if tuple(lw.q.shape) != (embed, hidden):
+    hidden, embed = int(g.shape[1]), int(g.shape[2])
+    if tuple(lw.shape) != (embed, hidden):
         raise ValueError(f"linear_w shape {tuple(linear_w.values.shape)} != ({hidden}, {embed})")
     _dense.check_x(x, embed)
     return _dense.dense_ffn(

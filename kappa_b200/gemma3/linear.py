@@ -12,7 +12,7 @@ import torch
 
 from kappa_b200 import _dense
 from kappa_b200.qwen3.linear import project_attn_out, project_q
-from kappa_b200.qwen3.quant import KMajor, Weight, kmajor
+from kappa_b200.qwen3.quant import Weight, kmajor
 
 __all__ = ["project_q", "project_kv", "project_attn_out"]
 
@@ -20,16 +20,11 @@ __all__ = ["project_q", "project_kv", "project_attn_out"]
 def project_kv(x: torch.Tensor, kv_w: Weight) -> tuple[torch.Tensor, torch.Tensor]:
     """kappa/gemma3/linear.py:15-19: ``kv_w`` ``[2, num_kv, D, head_dim]`` -> k, v ``[B, T, num_kv, head_dim]``."""
     km = kmajor(kv_w, -2, "kv_w")
-    if km.q.dim() != 4 or int(km.q.shape[0]) != 2:
+    if len(km.shape) != 4 or int(km.shape[0]) != 2:
         raise ValueError(f"kv_w must be [2, num_kv, model_dim, head_dim], got {tuple(kv_w.values.shape)}")
-    _, nkv, h, d = (int(s) for s in km.q.shape)
+    _, nkv, h, d = (int(s) for s in km.shape)
     _dense.check_x(x, d)
     b, t = int(x.shape[0]), int(x.shape[1])
-    half = nkv * h
     x2 = x.reshape(b * t, d)
-    k, v = (
-        _dense.linear(x2, KMajor(q=km.q[j], scale=km.scale[j * half:(j + 1) * half] if km.per_channel else km.scale,
-                                 per_channel=km.per_channel)).reshape(b, t, nkv, h)
-        for j in (0, 1)
-    )
+    k, v = (_dense.linear(x2, km.group(j)).reshape(b, t, nkv, h) for j in (0, 1))
     return k, v

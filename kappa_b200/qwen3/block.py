@@ -36,8 +36,8 @@ def ffn_sub_block(h: torch.Tensor, pre_ffn_norm: torch.Tensor, ffn, *, cfg=None,
     g = kmajor(ffn.gate_proj, -2, "gate_proj")
     u = kmajor(ffn.up_proj, -2, "up_proj")
     dn = kmajor(ffn.down_proj, -2, "down_proj")
-    inter, dim = int(g.q.shape[-2]), int(g.q.shape[-1])
-    if dim != d or tuple(u.q.shape) != (inter, dim) or tuple(dn.q.shape) != (dim, inter) or g.q.dim() != 2:
+    inter, dim = int(g.shape[-2]), int(g.shape[-1])
+    if dim != d or tuple(u.shape) != (inter, dim) or tuple(dn.shape) != (dim, inter) or len(g.shape) != 2:
         raise ValueError("ffn_sub_block: weight shapes do not match [D, I], [D, I], [I, D]")
     return _norm.dense_block(h, g.struct(), u.struct(), dn.struct(), hidden=inter, act=_lib.ACT_SILU,
                              pre=pre_ffn_norm, post=None, kind=_lib.NORM_QWEN, epsilon=epsilon, keep=(g, u, dn))

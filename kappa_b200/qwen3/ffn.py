@@ -20,8 +20,8 @@ def swiglu_ffn(
     g = kmajor(gate_w, -2, "gate_w")
     u = kmajor(up_w, -2, "up_w")
     dn = kmajor(down_w, -2, "down_w")
-    inter, dim = int(g.q.shape[-2]), int(g.q.shape[-1])
-    if tuple(u.q.shape) != (inter, dim) or tuple(dn.q.shape) != (dim, inter) or g.q.dim() != 2:
+    inter, dim = int(g.shape[-2]), int(g.shape[-1])
+    if tuple(u.shape) != (inter, dim) or tuple(dn.shape) != (dim, inter) or len(g.shape) != 2:
         raise ValueError("swiglu_ffn: weight shapes do not match [D, I], [D, I], [I, D]")
     _dense.check_x(x, dim)
     return _dense.dense_ffn(

@@ -58,7 +58,7 @@ def _effective_moe_impl(cfg, *, total_tokens: int) -> str:
 
 def _router(router_w: Weight, d: int, num_experts: int) -> KMajor:
     r = kmajor(router_w, -2, "router_w")
-    if tuple(r.q.shape) != (num_experts, d):
+    if tuple(r.shape) != (num_experts, d):
         raise ValueError(f"router_w shape {tuple(router_w.values.shape)} != ({d}, {num_experts})")
     return r
 
@@ -67,10 +67,10 @@ def _experts(ffn_gate: Weight, ffn_up: Weight, ffn_down: Weight, d: int):
     g = kmajor(ffn_gate, -2, "ffn_gate")
     u = kmajor(ffn_up, -2, "ffn_up")
     dn = kmajor(ffn_down, -2, "ffn_down")
-    if g.q.dim() != 3:
+    if len(g.shape) != 3:
         raise ValueError("expert weights must be [E, D, I] / [E, I, D]")
-    e, i, dd = (int(s) for s in g.q.shape)
-    if dd != d or tuple(u.q.shape) != (e, i, d) or tuple(dn.q.shape) != (e, d, i):
+    e, i, dd = (int(s) for s in g.shape)
+    if dd != d or tuple(u.shape) != (e, i, d) or tuple(dn.shape) != (e, d, i):
         raise ValueError(
             f"expert weight shapes {tuple(ffn_gate.values.shape)}, {tuple(ffn_up.values.shape)}, "
             f"{tuple(ffn_down.values.shape)} do not match [E, {d}, I], [E, {d}, I], [E, I, {d}]"

@@ -25,9 +25,9 @@ __all__ = ["project_q", "project_kv", "project_attn_out", "quantize_attn_out", "
 def _project_heads(x: torch.Tensor, w: Weight, name: str) -> torch.Tensor:
     """``einsum("btd,ndh->btnh", x, w)`` for a W8 ``w`` ``[n, d, h]``."""
     km = kmajor(w, -2, name)
-    if km.q.dim() != 3:
+    if len(km.shape) != 3:
         raise ValueError(f"{name} must be [heads, model_dim, head_dim], got {tuple(w.values.shape)}")
-    n, h, d = (int(s) for s in km.q.shape)
+    n, h, d = (int(s) for s in km.shape)
     _dense.check_x(x, d)
     b, t = int(x.shape[0]), int(x.shape[1])
     return _dense.linear(x.reshape(b * t, d), km).reshape(b, t, n, h)
@@ -68,7 +68,7 @@ def attn_out_kmajor(o_w: Weight) -> KMajor:
 def project_attn_out(encoded: torch.Tensor, o_w: Weight) -> torch.Tensor:
     """kappa/qwen3/linear.py:23-25: ``einsum("btnh,nhd->btd", encoded, o_w)``."""
     km = attn_out_kmajor(o_w)
-    d, nh = (int(s) for s in km.q.shape)
+    d, nh = (int(s) for s in km.shape)
     if encoded.dim() != 4 or int(encoded.shape[2]) * int(encoded.shape[3]) != nh:
         raise ValueError(f"encoded {tuple(encoded.shape)} does not match o_w {tuple(o_w.values.shape)}")
     b, t = int(encoded.shape[0]), int(encoded.shape[1])

@@ -31,6 +31,9 @@ __all__ = [
     "quantize_weight",
     "kmajor",
     "gather_embed_tokens",
+    "Q8Tiled",
+    "pack_weight",
+    "unpack_weight",
 ]
 
 
@@ -119,28 +122,81 @@ def quantize_weight(
 
 
 class KMajor(NamedTuple):
-    """A W8 weight as the kernels take it: [.., N, K] int8 + flat scales."""
+    """A W8 weight as the kernels take it: int8 values K-major ``[.., N, K]``
+    (or pre-packed, ``layout == LAYOUT_TILED``) + flat scales."""
 
-    q: torch.Tensor  # [..., N, K] contiguous int8
+    q: torch.Tensor  # [..., N, K] contiguous int8, or the tiled uint8 buffer
     scale: torch.Tensor  # flat: 1 value or prod(lead) * N values
     per_channel: bool
+    shape: tuple = ()  # the K-major logical shape [..., N, K]
+    layout: int = _lib.LAYOUT_KMAJOR
 
     def struct(self, offset_rows: int = 0) -> _lib.KW8Weight:
         """kw8_weight for rows [offset_rows, ...) of the [-1, K] view."""
-        K = self.q.shape[-1]
-        q_ptr = self.q.data_ptr() + offset_rows * K
+        K = int(self.shape[-1])
+        if self.layout == _lib.LAYOUT_TILED:
+            if offset_rows % 16 or (offset_rows and int(self.shape[-2]) % 16):
+                raise ValueError("tiled weights split only at 16-row tile boundaries")
+            steps = (K + 127) // 128 * 2
+            q_ptr = self.q.data_ptr() + (offset_rows // 16) * steps * 1024
+        else:
+            q_ptr = self.q.data_ptr() + offset_rows * K
         s_ptr = self.scale.data_ptr()
         if self.per_channel:
             s_ptr += offset_rows * self.scale.element_size()
-        return _lib.KW8Weight(q_ptr, s_ptr, _DT[self.scale.dtype], int(self.per_channel))
+        return _lib.KW8Weight(q_ptr, s_ptr, _DT[self.scale.dtype], int(self.per_channel), int(self.layout), 0)
+
+    def group(self, j: int, count: int = 1) -> "KMajor":
+        """Leading-axis groups [j, j + count) (weights stacked on axis 0)."""
+        per = 1
+        for d in self.shape[1:-2]:
+            per *= int(d)
+        rows = per * int(self.shape[-2])
+        scale = self.scale[j * rows:(j + count) * rows] if self.per_channel else self.scale
+        shape = (count,) + tuple(self.shape[1:]) if count != 1 else tuple(self.shape[1:])
+        if self.layout == _lib.LAYOUT_TILED:
+            q = self.q[j * per:(j + count) * per]
+        else:
+            q = self.q[j:j + count] if count != 1 else self.q[j]
+        return KMajor(q=q, scale=scale, per_channel=self.per_channel, shape=shape, layout=self.layout)
+
+
+class Q8Tiled(NamedTuple):
+    """A W8 weight pre-packed for the kernels (``pack_weight``): the same int8
+    values and scale as the ``Q8Weight`` it came from, stored in the tiled
+    layout (``kw8_pack_weight``) that every kernel reads in whole contiguous
+    pieces.  ``kshape`` is the K-major logical shape ``[.., N, K]`` and
+    ``in_axis`` the contraction axis of kappa's logical shape."""
+
+    tiled: torch.Tensor  # uint8 [groups, ceil(N / 16), steps, 1024]
+    scale: torch.Tensor
+    kshape: tuple
+    in_axis: int
+
+    @property
+    def values_shape(self) -> tuple:
+        s = tuple(self.kshape)
+        return s[:-2] + (s[-1], s[-2]) if self.in_axis == -2 else s
 
 
 _warned_layout = False
 
 
 def kmajor(w: Weight, in_axis: int, name: str = "weight") -> KMajor:
-    """View a W8 weight K-major; copies only if ``values`` is stored otherwise."""
+    """View a W8 weight K-major; copies only if ``values`` is stored otherwise.
+
+    A ``Q8Tiled`` weight is passed through in its packed layout.
+    """
     global _warned_layout
+    if isinstance(w, Q8Tiled):
+        if _norm_axis(in_axis, len(w.kshape)) != w.in_axis:
+            raise ValueError(f"{name}: packed with contraction axis {w.in_axis}, used with {in_axis}")
+        _lib.require_cuda(w.tiled, name)
+        s = w.scale
+        per_channel = s.numel() > 1
+        s = s.contiguous().reshape(-1) if per_channel else s.reshape(1).contiguous()
+        return KMajor(q=w.tiled, scale=s, per_channel=per_channel, shape=tuple(int(d) for d in w.kshape),
+                      layout=_lib.LAYOUT_TILED)
     if not is_q8_weight(w):
         raise TypeError(
             f"{name}: kappa_b200 implements the W8 path; quantize the weight with "
@@ -177,7 +233,7 @@ def kmajor(w: Weight, in_axis: int, name: str = "weight") -> KMajor:
         s = s2.contiguous().reshape(-1)
     else:
         s = s.reshape(1).contiguous()
-    return KMajor(q=q, scale=s, per_channel=per_channel)
+    return KMajor(q=q, scale=s, per_channel=per_channel, shape=tuple(int(d) for d in q.shape))
 
 
 def to_compute_dtype(w: Weight, dtype: torch.dtype, *, in_axis: int = -2) -> torch.Tensor:
@@ -186,6 +242,8 @@ def to_compute_dtype(w: Weight, dtype: torch.dtype, *, in_axis: int = -2) -> tor
     W8 weights are dequantised by the ``kw8_dequantize`` kernel (one rounding
     per product, as kappa); full-precision weights are cast.
     """
+    if isinstance(w, Q8Tiled):
+        return to_compute_dtype(unpack_weight(w), dtype, in_axis=w.in_axis)
     if not is_q8_weight(w):
         return w.to(dtype)
     if dtype not in _DT:
@@ -227,3 +285,42 @@ def gather_embed_tokens(tokens: torch.Tensor, embed: Weight, *, compute_dtype: t
         )
     )
     return out
+
+
+def pack_weight(w: Weight, *, in_axis: int = -2) -> Q8Tiled:
+    """Pre-pack a W8 weight into the tiled layout (``kw8_pack_weight``).
+
+    The load-time step after ``quantize_weight`` (kappa quantises its whole
+    parameter tree at load, kappa/qwen3/weights.py:143-170): the values and
+    scales are unchanged, only their storage order differs, so every kernel
+    reads whole contiguous pieces of the weights (512 bytes per warp load in
+    the decode kernel).  ``in_axis`` is the contraction axis as for
+    ``kmajor``.  Every FFN, MoE, linear and block function of this package
+    accepts the result wherever it takes a ``Q8Weight``.
+    """
+    km = kmajor(w, in_axis)
+    if km.layout == _lib.LAYOUT_TILED:
+        return w
+    K, N = int(km.shape[-1]), int(km.shape[-2])
+    groups = km.q.numel() // (N * K)
+    lib = _lib.load()
+    nbytes = int(lib.kw8_packed_weight_bytes(groups, N, K))
+    steps = (K + 127) // 128 * 2
+    tiled = torch.empty((groups, (N + 15) // 16, steps, 1024), dtype=torch.uint8, device=km.q.device)
+    assert tiled.numel() == nbytes
+    _lib.check(lib.kw8_pack_weight(km.q.data_ptr(), groups, N, K, tiled.data_ptr(), _lib.stream_of(km.q)))
+    return Q8Tiled(tiled=tiled, scale=w.scale, kshape=tuple(km.shape), in_axis=_norm_axis(in_axis, len(km.shape)))
+
+
+def unpack_weight(w: Q8Tiled) -> Q8Weight:
+    """The ``Q8Weight`` a ``Q8Tiled`` was packed from (values K-major in memory,
+    kappa's logical shape), bit for bit."""
+    kshape = tuple(w.kshape)
+    K, N = kshape[-1], kshape[-2]
+    groups = 1
+    for d in kshape[:-2]:
+        groups *= int(d)
+    q = torch.empty(kshape, dtype=torch.int8, device=w.tiled.device)
+    _lib.check(_lib.load().kw8_unpack_weight(w.tiled.data_ptr(), groups, N, K, q.data_ptr(), _lib.stream_of(q)))
+    values = q.transpose(-1, -2) if w.in_axis == -2 else q
+    return Q8Weight(values=values, scale=w.scale)

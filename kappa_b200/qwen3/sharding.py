@@ -119,9 +119,18 @@ def shard_gemma_mlp(gating_w: Weight, linear_w: Weight, rank: int, world: int, *
 
 
 def shard_experts(ffn_gate: Weight, ffn_up: Weight, ffn_down: Weight, rank: int, world: int):
-    """Expert-parallel shards: experts ``[r*E/R, (r+1)*E/R)`` of ``[E, ...]`` weights and scales."""
+    """Expert-parallel shards: experts ``[r*E/R, (r+1)*E/R)`` of ``[E, ...]`` weights and scales
+    (``Q8Weight`` or pre-packed ``Q8Tiled``, whose groups are the experts)."""
+    from kappa_b200.qwen3.quant import Q8Tiled
+
     out = []
     for w in (ffn_gate, ffn_up, ffn_down):
+        if isinstance(w, Q8Tiled):
+            sl = _span(int(w.kshape[0]), rank, world, "experts")
+            scale = w.scale[sl] if w.scale.dim() == len(w.kshape) else w.scale
+            out.append(Q8Tiled(tiled=w.tiled[sl], scale=scale, kshape=(sl.stop - sl.start,) + tuple(w.kshape[1:]),
+                               in_axis=w.in_axis))
+            continue
         q = _q8(w, "expert weight")
         sl = _span(int(q.values.shape[0]), rank, world, "experts")
         scale = q.scale[sl] if q.scale.dim() == q.values.dim() else q.scale
@@ -147,9 +156,9 @@ def _dense_tp_call(x: torch.Tensor, gate, up, down, hidden: int, act: int, ctx: 
     lib = _lib.load()
     out = torch.empty((b, t, d), dtype=torch.bfloat16, device=x.device)
     ws = torch.empty(int(lib.kw8_dense_ffn_tp_workspace_size(T, d, hidden)), dtype=torch.uint8, device=x.device)
+    # epoch 0: the device-side call count (calls may be captured in a CUDA graph)
     _lib.check(lib.kw8_dense_ffn_tp(xc.data_ptr(), T, d, hidden, gate, up, down, act, out.data_ptr(),
-                                    ctypes.byref(ctx.peers), ctx.next_epoch(), ws.data_ptr(), ws.numel(),
-                                    _lib.stream_of(x)))
+                                    ctypes.byref(ctx.peers), 0, ws.data_ptr(), ws.numel(), _lib.stream_of(x)))
     del keep
     return out
 
@@ -165,7 +174,7 @@ def swiglu_ffn_tp(x: torch.Tensor, gate_shard: Weight, up_shard: Weight, down_sh
 
     if ctx is not None:
         g, u, dn = (kmajor(w, -2, n) for w, n in ((gate_shard, "gate_w"), (up_shard, "up_w"), (down_shard, "down_w")))
-        return _dense_tp_call(x, g.struct(), u.struct(), dn.struct(), int(g.q.shape[-2]), _lib.ACT_SILU, ctx,
+        return _dense_tp_call(x, g.struct(), u.struct(), dn.struct(), int(g.shape[-2]), _lib.ACT_SILU, ctx,
                               (g, u, dn))
     partial = swiglu_ffn(x, gate_shard, up_shard, down_shard, out_dtype=torch.float32)
     return _allreduce_to_bf16(partial, group)
@@ -179,7 +188,7 @@ def feed_forward_tp(x: torch.Tensor, gating_shard: Weight, linear_shard: Weight,
     if ctx is not None:
         g = kmajor(gating_shard, -1 if transpose_gating_einsum else -2, "gating_w")
         lw = kmajor(linear_shard, -2, "linear_w")
-        hidden = int(g.q.shape[1])
+        hidden = int(g.shape[1])
         return _dense_tp_call(x, g.struct(0), g.struct(hidden), lw.struct(), hidden, _lib.ACT_GELU_TANH, ctx, (g, lw))
     partial = feed_forward(x, gating_shard, linear_shard, transpose_gating_einsum=transpose_gating_einsum,
                            out_dtype=torch.float32)
@@ -354,7 +363,7 @@ class EPContext:
         pairs = self.world * max_tokens * k
         ret_bytes = 4 if return_fp32 else 2
         sizes = (self.recv_rows * d * 2, self.out_rows * d * 2, 2 * self.world * (num_experts + self.world) * 4,
-                 3 * self.world * 4, self.world * max_tokens * d * 2, pairs * 8,
+                 (3 * self.world + 1) * 4, self.world * max_tokens * d * 2, pairs * 8,
                  self.world * max_tokens * d * ret_bytes, 2 * self.world * decode_tokens * d * 4)
         self._bufs = _SharedBuffers(sizes, group, self.device)
         (self.peer_recv, self.peer_out, self.peer_counts, self.peer_flags, self.peer_rows, self.peer_meta,
@@ -417,20 +426,17 @@ class TPContext:
         self.world, self.rank = _world(group)
         self.max_tokens, self.d = max_tokens, d
         self.device = torch.device("cuda", torch.cuda.current_device())
-        self._bufs = _SharedBuffers((3 * self.world * 4, 2 * self.world * max_tokens * d * 4), group, self.device)
+        # flags [3][world] + the device call counter; exchange slots [2][world][max_tokens][d] fp32
+        self._bufs = _SharedBuffers(((3 * self.world + 1) * 4, 2 * self.world * max_tokens * d * 4), group,
+                                    self.device)
         self.peer_flags, self.peer_red = self._bufs.peer_ptrs
         self.flags_ptr, self.red_ptr = self._bufs.own
         self.peers = _lib.KW8EpPeers(
             self.world, self.rank, max_tokens, None, None, None, self.peer_flags.data_ptr(), None, None, None,
             self.flags_ptr, None, None, None, None, None, None, 0, self.peer_red.data_ptr(), self.red_ptr,
             max_tokens)
-        self.epoch = 0
         torch.cuda.synchronize(self.device)
         dist.barrier(group=group)
-
-    def next_epoch(self) -> int:
-        self.epoch += 1
-        return self.epoch & 0xFFFFFFFF
 
     def close(self):
         self._bufs.close(self.device)
@@ -449,8 +455,8 @@ def _moe_ep_p2p(x, router_w, gate_local, up_local, down_local, *, cfg, ctx: EPCo
     e_loc = e // ctx.world
     g, u, dn = (kmajor(w, -2, n) for w, n in ((gate_local, "ffn_gate"), (up_local, "ffn_up"),
                                                (down_local, "ffn_down")))
-    i = int(g.q.shape[-2])
-    if int(g.q.shape[0]) != e_loc or i != ctx.hidden:
+    i = int(g.shape[-2])
+    if int(g.shape[0]) != e_loc or i != ctx.hidden:
         raise ValueError("local expert weights do not match the EPContext")
     xc = x.contiguous()
     stream = _lib.stream_of(x)
@@ -559,14 +565,14 @@ def moe_swiglu_ffn_ep_decode(x: torch.Tensor, router_w: Weight, gate_local: Weig
         e_loc = e // ctx.world
         g, u, dn = (kmajor(w, -2, n) for w, n in ((gate_local, "ffn_gate"), (up_local, "ffn_up"),
                                                    (down_local, "ffn_down")))
-        if int(g.q.shape[0]) != e_loc:
+        if int(g.shape[0]) != e_loc:
             raise ValueError("local expert weights do not match the EPContext")
         r = kmajor(router_w, -2, "router_w")
         lib = _lib.load()
         xc = x.contiguous()
         out = torch.empty((b, t, d), dtype=torch.bfloat16, device=x.device)
         _lib.check(lib.kw8_moe_ffn_ep_decode(
-            xc.data_ptr(), T, d, int(g.q.shape[-2]), e, k, -1 if capacity is None else int(capacity), r.struct(),
+            xc.data_ptr(), T, d, int(g.shape[-2]), e, k, -1 if capacity is None else int(capacity), r.struct(),
             g.struct(), u.struct(), dn.struct(), out.data_ptr(), ctypes.byref(ctx.peers), ctx.next_epoch(),
             ctx.dec_ws.data_ptr(), ctx.dec_ws.numel(), _lib.stream_of(x)))
         del r, g, u, dn

@@ -25,7 +25,7 @@ def embed_tokens(tokens: torch.Tensor, embed_table: Weight, *, compute_dtype: to
 
 def _head(x: torch.Tensor, w: Weight, name: str, out_dtype: torch.dtype | None):
     km = kmajor(w, -1, name)
-    if km.q.dim() != 2:
+    if len(km.shape) != 2:
         raise ValueError(f"{name} must be [vocab, model_dim], got {tuple(w.values.shape)}")
     return km, (out_dtype or x.dtype)
 
@@ -37,7 +37,7 @@ def logits_from_hidden(x: torch.Tensor, lm_head: Weight, *, out_dtype: torch.dty
     the fp32 sums instead.
     """
     km, dt = _head(x, lm_head, "lm_head", out_dtype)
-    V, D = (int(s) for s in km.q.shape)
+    V, D = (int(s) for s in km.shape)
     _dense.check_x(x, D)
     b, t = int(x.shape[0]), int(x.shape[1])
     return _dense.linear(x.reshape(b * t, D), km, out_dtype=dt).reshape(b, t, V)
@@ -52,7 +52,7 @@ def logits_from_hidden_last_positions(x: torch.Tensor, w: Weight, last_idx: torc
                                       out_dtype: torch.dtype | None = None) -> torch.Tensor:
     """kappa/qwen3/transformer.py:68-75: ``x`` ``[B, L, D]``, ``last_idx`` ``[B]`` -> ``[B, vocab]``."""
     km, dt = _head(x, w, "w", out_dtype)
-    V, D = (int(s) for s in km.q.shape)
+    V, D = (int(s) for s in km.shape)
     _dense.check_x(x, D)
     b, L = int(x.shape[0]), int(x.shape[1])
     if tuple(last_idx.shape) != (b,):

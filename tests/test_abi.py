@@ -28,7 +28,7 @@ def test_library_exports_every_symbol():
 
 def test_cpu_only_queries():
     lib = L.load()
-    assert lib.kw8_abi_version() == 2
+    assert lib.kw8_abi_version() == 3
     n = lib.kw8_moe_ffn_workspace_size(4096, 2048, 768, 128, 8)
     # permuted rows xs (32768 x 2048 bf16), h (32768 x 768 bf16) and the
     # fp32 combine buffer (4096 x 2048) dominate

@@ -35,7 +35,7 @@ GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 KAPPA_BF16_TOL = 3e-2
 
 
-_OPTS = (_lib.OPT_GEMM_PATH, _lib.OPT_TOKEN_TILE, _lib.OPT_DETERMINISTIC, _lib.OPT_TC_PAIR)
+_OPTS = (_lib.OPT_GEMM_PATH, _lib.OPT_TOKEN_TILE, _lib.OPT_DETERMINISTIC, _lib.OPT_TC_PAIR, _lib.OPT_EP_TIMING)
 
 
 @pytest.fixture(autouse=True)
@@ -496,7 +496,7 @@ def _ep_single_rank_peers(dev, Tm, D, E, k, dedup, ret_f32=True, red_rows=0):
         "recv": torch.zeros((world * Tm * k, D), dtype=torch.bfloat16, device=dev),
         "out": torch.zeros((Tm * k, D), dtype=torch.bfloat16, device=dev),
         "counts": torch.zeros(2 * world * (E + world), dtype=torch.int32, device=dev),
-        "flags": torch.zeros(3 * world, dtype=torch.int32, device=dev),
+        "flags": torch.zeros(3 * world + 1, dtype=torch.int32, device=dev),
         "rows": torch.zeros((world * Tm, D), dtype=torch.bfloat16, device=dev),
         "meta": torch.zeros(2 * world * Tm * k, dtype=torch.int32, device=dev),
         "ret": torch.zeros((world * Tm, D), dtype=torch.float32 if ret_f32 else torch.bfloat16, device=dev),
@@ -534,12 +534,21 @@ def test_moe_ep_single_rank(dedup, ret_f32):
     km = [kmajor(w, -2) for w in g]
     xd = to_dev(x).reshape(T, D)
     stream = torch.cuda.current_stream(dev).cuda_stream
-    for epoch in (1, 2):
-        out = torch.empty_like(xd)
-        _lib.check(lib.kw8_moe_ffn_ep(xd.data_ptr(), T, D, I, E, k, -1, *[w.struct() for w in km], out.data_ptr(),
-                                      ctypes.byref(peers), epoch, ws.data_ptr(), ws.numel(), stream))
-        assert _lib.device_status(out) == 0
-        _moe_check(x, g, o, E, k, out.reshape(1, T, D))
+    _lib.set_option(_lib.OPT_EP_TIMING, 1 if dedup else 0)
+    try:
+        for epoch in (1, 2):
+            out = torch.empty_like(xd)
+            _lib.check(lib.kw8_moe_ffn_ep(xd.data_ptr(), T, D, I, E, k, -1, *[w.struct() for w in km],
+                                          out.data_ptr(), ctypes.byref(peers), epoch, ws.data_ptr(), ws.numel(),
+                                          stream))
+            assert _lib.device_status(out) == 0
+            _moe_check(x, g, o, E, k, out.reshape(1, T, D))
+        if dedup:  # the phase times of the last call (CUDA events at its phase boundaries)
+            ms = (ctypes.c_float * 9)()
+            _lib.check(lib.kw8_ep_phase_times(ms, 9))
+            assert all(v >= 0.0 for v in ms) and sum(ms) > 0.0
+    finally:
+        _lib.set_option(_lib.OPT_EP_TIMING, 0)
     del keep
 
 
@@ -598,6 +607,34 @@ def test_dense_ffn_tp_single_rank(T, act):
     stream = torch.cuda.current_stream(dev).cuda_stream
     _lib.check(lib.kw8_dense_ffn_tp(xd.data_ptr(), T, D, H, g.struct(0), g.struct(H), l2.struct(), act,
                                     out.data_ptr(), ctypes.byref(peers), 1, ws.data_ptr(), ws.numel(), stream))
+    assert _lib.device_status(out) == 0
+    # epoch 0: the group's device-side call count (word 3 * world of the
+    # flags), three eager calls and then the call captured in a CUDA graph
+    # and replayed twice: each call takes the next tag and the same result.
+    keep[0]["flags"].zero_()
+    outs = []
+    for _ in range(3):
+        o = torch.empty_like(xd)
+        _lib.check(lib.kw8_dense_ffn_tp(xd.data_ptr(), T, D, H, g.struct(0), g.struct(H), l2.struct(), act,
+                                        o.data_ptr(), ctypes.byref(peers), 0, ws.data_ptr(), ws.numel(), stream))
+        outs.append(o)
+    assert _lib.device_status(out) == 0
+    assert int(keep[0]["flags"][3].item()) == 3
+    graph_out = torch.empty_like(xd)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        _lib.check(lib.kw8_dense_ffn_tp(xd.data_ptr(), T, D, H, g.struct(0), g.struct(H), l2.struct(), act,
+                                        graph_out.data_ptr(), ctypes.byref(peers), 0, ws.data_ptr(), ws.numel(),
+                                        side.cuda_stream))
+    for _ in range(2):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    assert int(keep[0]["flags"][3].item()) == 5
+    for o in outs + [graph_out]:
+        assert torch.equal(o, out)
+    del graph
     assert _lib.device_status(out) == 0
     ogt, olw = _oracle_q(gating, True, -1), _oracle_q(linear, True, -2)
     if act == 0:
