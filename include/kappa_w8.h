@@ -328,8 +328,10 @@ int kw8_moe_block(const void* h, int64_t T, int64_t D, int64_t I, int64_t E, int
  * kw8_moe_ffn_workspace_size() exceeds 16 MiB are rejected with
  * KW8_ERR_WORKSPACE (at the Qwen3-30B-A3B layer shape, D=2048, I=768,
  * E=128, k=8, that is above about 300 tokens).  The first call on each
- * device looks up the array's device address (cudaGetSymbolAddress) and
- * caches it; make that first call before any stream capture.  Every call
+ * device (and again after the device's context changed, e.g. after a
+ * cudaDeviceReset) looks up the array's device address
+ * (cudaGetSymbolAddress) and caches it; make that first call before any
+ * stream capture.  Every call
  * on a device shares the one array, which keeps the last call's contents
  * (nothing in it needs to start at zero; the call clears what must), so
  * calls that overlap on the same GPU (other streams or threads) race and
@@ -440,7 +442,10 @@ typedef struct kw8_ep_peers {
  * of the group (start at 1).  gate/up/down hold this rank's E/world
  * experts.  Every wait is bounded (2 s): a peer that never arrives leaves
  * KW8_ERR_DEVICE_TIMEOUT in the device status (kw8_device_status) and an
- * unspecified `out`, but no hung kernel.                                   */
+ * unspecified `out`, but no hung kernel.  After a timeout the group is out
+ * of step (a late peer may still store rows and counts into this rank's
+ * buffers during its next call), so every rank must drop the group's
+ * buffers or zero them again (after a host barrier) before calling again. */
 size_t kw8_moe_ffn_ep_workspace_size(int64_t max_tokens, int64_t D, int64_t I, int64_t E,
                                      int32_t k, int32_t world);
 int kw8_moe_ffn_ep(const void* x, int64_t T, int64_t D, int64_t I, int64_t E, int32_t k,

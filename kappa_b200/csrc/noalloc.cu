@@ -34,19 +34,41 @@ static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes]
 constexpr int kMaxDevices = 64;
 std::mutex g_noalloc_mu;
 void* g_noalloc_addr[kMaxDevices] = {};
+void* g_noalloc_ctx[kMaxDevices] = {};  // the context the address was looked up in
 
-// Device address of the scratch on the current device, looked up once per
-// device (with that device current) and cached.
+// The calling thread's current CUDA context (cuCtxGetCurrent, found through
+// the runtime's driver entry point), or null if it cannot be read.
+void* current_context() {
+  using GetCurrentFn = int (*)(void**);
+  static GetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<GetCurrentFn>(p);
+  });
+  void* ctx = nullptr;
+  if (fn == nullptr || fn(&ctx) != 0) return nullptr;
+  return ctx;
+}
+
+// Device address of the scratch on the current device, looked up (with
+// that device current) once per device and context and cached: a device
+// reset or another context on the device gets a fresh lookup.
 int noalloc_scratch(void** addr) {
   int dev = 0;
   KW8_CUDA_TRY(cudaGetDevice(&dev));
   KW8_REQUIRE(dev >= 0 && dev < kMaxDevices, KW8_ERR_UNSUPPORTED, "device %d out of range", dev);
+  void* ctx = current_context();
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_addr[dev] == nullptr) {
+  if (g_noalloc_addr[dev] == nullptr || ctx == nullptr || ctx != g_noalloc_ctx[dev]) {
     void* p = nullptr;
     KW8_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
     KW8_REQUIRE(p != nullptr, KW8_ERR_CUDA, "scratch address lookup returned null");
     g_noalloc_addr[dev] = p;
+    g_noalloc_ctx[dev] = ctx;
   }
   *addr = g_noalloc_addr[dev];
   return KW8_OK;
