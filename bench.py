@@ -343,6 +343,7 @@ def _extra_configs(lib, dev, stream, router, gate, up, down, sr, sg, su, sd):
     from kappa_b200 import _lib
     from kappa_b200.gemma3.ffn import feed_forward
     from kappa_b200.qwen3 import ffn_moe as M
+    from kappa_b200.qwen3.architecture import MoEConfig
     from kappa_b200.qwen3.quant import quantize_weight
 
     peak_tf, peak_gbs, kind = _peaks()
@@ -447,9 +448,33 @@ def _extra_configs(lib, dev, stream, router, gate, up, down, sr, sg, su, sd):
     mlp = {"workload": "gemma3-4b W8 MLP, T=256 (BASELINE configs[0])", "us_per_call": sec * 1e6,
            "tokens_per_s": tg / sec, "tflops": flops / sec / 1e12, "frac_tc": flops / sec / 1e12 / peak_tf,
            "int8_weight_gbs": 3 * dg * hg / sec / 1e9}
+    # The FFN half of a decoder block in one call (pre-norm, FFN, post-norm for Gemma, residual),
+    # beside the FFN alone: what the norms and the residual add.
+    from kappa_b200.gemma3 import block as gblock
+    from kappa_b200.qwen3 import block as qblock
+
+    pre_g = (torch.randn(dg, generator=gg, device=dev) * 0.1).to(torch.bfloat16)
+    post_g = (torch.randn(dg, generator=gg, device=dev) * 0.1).to(torch.bfloat16)
+    sec_gb = timed(lambda: gblock.ffn_sub_block(xg, pre_g, gating, linear, post_g, transpose_gating_einsum=True))
+    xm = torch.randn((1, T_TOK, D), generator=gg, device=dev).to(torch.bfloat16)
+    pre_q = (1 + torch.randn(D, generator=gg, device=dev) * 0.1).to(torch.bfloat16)
+
+    class _Moe:
+        pass
+
+    moe_p = _Moe()
+    moe_p.router, moe_p.gate_proj, moe_p.up_proj, moe_p.down_proj = router, gate, up, down
+    cfg_b = MoEConfig(use_moe=True, num_experts=E, num_experts_per_tok=K_TOP, moe_impl="ragged_jax")
+    sec_qb = timed(lambda: qblock.ffn_sub_block(xm, pre_q, moe_p, cfg=cfg_b), reps=10)
+    sec_q = timed(lambda: M.moe_swiglu_ffn(xm, router, gate, up, down, cfg=cfg_b), reps=10)
+    block = {"gemma3_block_ffn_T256_us": sec_gb * 1e6, "gemma3_mlp_alone_T256_us": sec * 1e6,
+             "qwen3_moe_block_ffn_T4096_us": sec_qb * 1e6, "qwen3_moe_layer_alone_T4096_us": sec_q * 1e6,
+             "note": "h + post_norm(FFN(pre_norm(h))) as one call (kw8_dense_block / kw8_moe_block) against "
+                     "the FFN alone through the public API; CUDA events over repeated calls"}
     stack = _gemma_stack(lib, dev, timed, graphed, peak_tf, peak_gbs)
     big = _qwen3_235b_layer(lib, dev, timed, timed_cold, graphed, peak_tf, peak_gbs)
-    return {"moe_decode": decode, "gemma_mlp": mlp, "gemma3_4b_ffn_stack": stack, "qwen3_235b_moe_layer": big,
+    return {"moe_decode": decode, "gemma_mlp": mlp, "block_ffn": block, "gemma3_4b_ffn_stack": stack,
+            "qwen3_235b_moe_layer": big,
             "peaks": f"{kind}: {peak_tf} TFLOP/s, {peak_gbs} GB/s"}
 
 

@@ -88,10 +88,16 @@ int pick_nt(int64_t rows, int64_t groups) {
 }
 
 // Token tile for a dense (single-group) tensor-core GEMM with `m_tiles`
-// feature tiles: the fewest waves over the SMs, a tile costing about
-// max(128, nt) (below ~128 tokens a tile is bound by widening its 128x64
-// int8 weight slices, not by the MMAs); ties go to the larger tile; at most
-// kTcMaxDoubleBufferNT.
+// feature tiles: the fewest waves over the SMs times a tile's cost.  A
+// tcgen05.mma (M = 128, K = 16) costs its issuing thread about the same
+// ~130-160 cycles for any N up to 256, so a tile's cost hardly depends on
+// its rows; what does: 160-row tiles hold fewer pipeline stages than
+// 128-row ones (cost ~ max(128, nt) up to 160, measured), and a 192-row
+// tile (one TMEM accumulator, three stages, five A slots) costs about 6%
+// more than a 128-row one.  Wider tiles keep only two stages and are not
+// taken.  Measured on the Gemma3-4B MLP: T = 256 -> 128-row tiles (82 us;
+// 192: 92 us), T = 512 -> 192-row tiles (118 us; 128: 139 us).  Ties go to
+// the larger tile.
 int pick_nt_dense(int64_t rows, int64_t m_tiles) {
   const int forced = g_opt_token_tile.load();
   if (forced >= 16 && forced <= kTcMaxNT && forced % 16 == 0) return forced;
@@ -100,10 +106,11 @@ int pick_nt_dense(int64_t rows, int64_t m_tiles) {
   const int64_t sms = num_sms(dev);
   int best = 16;
   int64_t best_cost = INT64_MAX;
-  for (int nt = 16; nt <= kTcMaxDoubleBufferNT; nt += 16) {
+  for (int nt = 16; nt <= 192; nt += 16) {
+    if (nt > kTcMaxDoubleBufferNT && nt != 192) continue;
     const int64_t tiles = (rows + nt - 1) / nt * m_tiles;
     const int64_t waves = (tiles + sms - 1) / sms;
-    const int64_t cost = waves * (nt > 128 ? nt : 128);
+    const int64_t cost = waves * (nt == 192 ? 136 : (nt > 128 ? nt : 128));
     if (cost < best_cost || (cost == best_cost && nt > best)) {
       best = nt;
       best_cost = cost;
