@@ -693,6 +693,8 @@ def _multi_gpu_extras(lib, dev, world, rank, x, y_ep, router, gate, up, down, ep
             dist.barrier(device_ids=[dev.index])
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             torch.cuda._sleep(2_000_000)  # the GPU waits ~1 ms while the host enqueues the call
+            # the ranks' GPUs leave a flag barrier together, so the call's time holds no host skew
+            _lib.check(lib.kw8_ep_barrier(ctypes.byref(ep_ctx.peers), 0, ep_ctx.next_epoch(), 1, stream.cuda_stream))
             e0.record(stream)
             yd = moe_swiglu_ffn_ep_decode(xd, router, g_loc, u_loc, d_loc, cfg=cfg, ctx=ep_ctx)
             e1.record(stream)
@@ -714,13 +716,13 @@ def _multi_gpu_extras(lib, dev, world, rank, x, y_ep, router, gate, up, down, ep
                     "frac_hbm": nbytes / sec / 1e9 / (world * peak_gbs),
                     "max_rel_err_vs_1gpu": _max_over_ranks(derr, dev),
                     "parity_ok": _max_over_ranks(0.0 if dok else 1.0, dev) == 0.0})
-    out["moe_decode_ep"] = {"rows": dec, "timing": "median of 15 calls, each after a 256 MB L2 flush and a "
-                            "host barrier (the call enqueued behind a GPU sleep, so host time is not timed); max "
-                            "over ranks; frac_hbm over world x measured HBM peak"}
+    out["moe_decode_ep"] = {"rows": dec, "timing": "median of 15 calls, each after a 256 MB L2 flush, a host "
+                            "barrier and a device flag barrier of the group (the call enqueued behind a GPU sleep, "
+                            "so neither host time nor rank skew is timed); max over ranks; frac_hbm over world x "
+                            "measured HBM peak"}
     del flush
     out["gemma3_4b_ffn_stack_tp"] = _gemma_stack_tp(lib, dev, world, rank, peak_tf, peak_gbs)
-    if world == 8:
-        out["qwen3_235b_moe_stack_ep"] = _qwen3_235b_stack_ep(lib, dev, world, rank, peak_tf, peak_gbs)
+    out["qwen3_235b_moe_stack_ep"] = _qwen3_235b_stack_ep(lib, dev, world, rank, peak_tf, peak_gbs)
     return out
 
 
@@ -831,7 +833,7 @@ def _gemma_stack_tp(lib, dev, world, rank, peak_tf, peak_gbs):
 
 
 def _qwen3_235b_stack_ep(lib, dev, world, rank, peak_tf, peak_gbs):
-    """BASELINE configs[4] at 8 GPUs: 94 Qwen3-235B-shaped W8 MoE layers (D=4096,
+    """BASELINE configs[4] (at 8 GPUs; 94 * world / 8 layers below that): 94 Qwen3-235B-shaped W8 MoE layers (D=4096,
     I=1536, 128 experts top-8; 227 GB of int8 experts, 28.4 GB per rank)
     expert parallel: each rank holds its 16 experts of every layer (random
     int8 values with per-channel fp32 scales of N(0, 0.02) weights' size)
@@ -846,7 +848,9 @@ def _qwen3_235b_stack_ep(lib, dev, world, rank, peak_tf, peak_gbs):
     from kappa_b200.qwen3.quant import Q8Weight, quantize_weight
     from kappa_b200.qwen3.sharding import EPContext, moe_swiglu_ffn_ep, moe_swiglu_ffn_ep_decode
 
-    n_layers, d2, i2, e2, k2, tp, bd = 94, 4096, 1536, 128, 8, 2048, 64
+    # 94 layers at 8 GPUs; with fewer GPUs 94 * world / 8 of them (the same
+    # 28.4 GB of experts per rank), reported per layer as well.
+    n_layers, d2, i2, e2, k2, tp, bd = 94 * world // 8, 4096, 1536, 128, 8, 2048, 64
     el = e2 // world
     gen = torch.Generator(device=dev)
     gen.manual_seed(40 + rank)
@@ -891,8 +895,9 @@ def _qwen3_235b_stack_ep(lib, dev, world, rank, peak_tf, peak_gbs):
     flops = n_layers * world * (2.0 * tp * k2 * 3 * d2 * i2 + 2.0 * tp * d2 * e2)
     layer_bytes = e2 * 3 * d2 * i2  # decode at B=64 activates nearly every expert
     return {
-        "workload": "qwen3-235b-a22b-shaped W8 MoE stack, 94 layers (D=4096, I=1536, 128 experts top-8), expert "
-                    f"parallel over {world} GPUs: prefill 2048 tokens per rank, decode batch 64",
+        "workload": f"qwen3-235b-a22b-shaped W8 MoE stack, {n_layers} layers (94 at 8 GPUs; D=4096, I=1536, 128 "
+                    f"experts top-8), expert parallel over {world} GPUs: prefill 2048 tokens per rank, decode batch 64",
+        "layers": n_layers, "prefill_ms_per_layer": sec_p * 1e3 / n_layers, "decode_us_per_layer": sec_d * 1e6 / n_layers,
         "prefill_ms": sec_p * 1e3, "prefill_tokens_per_s": world * tp / sec_p,
         "prefill_tflops": flops / sec_p / 1e12, "prefill_frac_tc": flops / sec_p / 1e12 / (world * peak_tf),
         "decode_ms_per_step": sec_d * 1e3, "decode_tokens_per_s": bd / sec_d,

@@ -391,7 +391,8 @@ int kw8_ep_local_offsets(const int32_t* counts, int32_t world, int32_t rank,
  *   out    : max_tokens * k rows of D bf16 (this rank's rows coming back);
  *   counts : int32 [2][world][E] (per-expert row counts of every rank, two
  *            copies alternating by call);
- *   flags  : uint32 [3][world], zero before the first call on any rank.
+ *   flags  : uint32 [3][world] + 3 words, zero before the first call on any
+ *            rank.
  * own_* are this rank's buffers again, as host-side values.
  *
  * With rows != NULL, kw8_moe_ffn_ep sends every token once per rank that
@@ -479,10 +480,12 @@ int kw8_moe_ffn_ep_decode(const void* x, int64_t T, int64_t D, int64_t I, int64_
  * the same bits on every rank).  x [T][D] bf16 (the same on every rank),
  * T <= red_rows.
  * epoch: as for kw8_moe_ffn_ep, or 0: the group keeps the call count in
- * device memory (word 3 * world of each rank's flags, which must then hold
- * 3 * world + 1 words, zero before the first call), so a sequence of calls
- * captured in a CUDA graph takes a new tag at every replay.  Every call of
- * a group uses one of the two forms.                                        */
+ * device memory (word 3 * world of each rank's flags), so a sequence of
+ * calls captured in a CUDA graph takes a new tag at every replay.  Every
+ * call of a group uses one of the two forms.  The sum runs as one
+ * cooperative launch whose CTAs count themselves in flags words
+ * 3 * world + 1 and + 2: the flags of a group that makes these calls hold
+ * 3 * world + 3 words, zero before the first call.                         */
 size_t kw8_dense_ffn_tp_workspace_size(int64_t T, int64_t D, int64_t H_local);
 int kw8_dense_ffn_tp(const void* x, int64_t T, int64_t D, int64_t H_local, kw8_weight gate,
                      kw8_weight up, kw8_weight down, int32_t act, void* out,

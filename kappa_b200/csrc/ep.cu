@@ -198,47 +198,49 @@ __device__ __forceinline__ uint32_t call_epoch(uint32_t epoch, const uint32_t* c
   return epoch != 0 ? epoch : *reinterpret_cast<const volatile uint32_t*>(ctr) + 1u;
 }
 
+// The whole sum is one cooperative launch (every CTA resident): each CTA
+// pushes its share of this rank's partial into every rank's slot; the last
+// CTA to arrive (counter at flags word 3 * world + 1) marks phase 1 of the
+// call's tag at every rank; every CTA waits (bounded) for every rank's mark
+// and adds its share of the world slots in rank order; the last CTA to
+// leave (word 3 * world + 2) resets the counters and, with a device call
+// count, stores the tag.
 __global__ void __launch_bounds__(kEpThreads)
-    ep_push_partials_kernel(const float4* __restrict__ part, int splits, int64_t split4, int64_t n4,
-                            const uint64_t* __restrict__ peer_red, int world, int rank, int64_t slot4,
-                            uint32_t epoch, const uint32_t* ctr) {
-  const uint32_t e = call_epoch(epoch, ctr);
-  const int64_t dst_off4 = static_cast<int64_t>(e & 1u) * world * slot4 + rank * slot4;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    ep_allreduce_kernel(const float4* __restrict__ part, int splits, int64_t split4, int64_t n4,
+                        const uint64_t* __restrict__ peer_red, const float4* __restrict__ own_red,
+                        const uint64_t* __restrict__ flags, uint32_t* own_flags, int world, int rank, int64_t slot4,
+                        uint32_t epoch, uint2* __restrict__ out) {
+  uint32_t* const ctr = own_flags + 3 * world;
+  uint32_t* const arrive = ctr + 1;
+  uint32_t* const depart = ctr + 2;
+  __shared__ uint32_t e_sh;
+  if (threadIdx.x == 0) e_sh = call_epoch(epoch, ctr);
+  __syncthreads();
+  const uint32_t e = e_sh;
+  const int64_t par4 = static_cast<int64_t>(e & 1u) * world * slot4;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4; i += stride) {
     float4 v = part[i];
     for (int sp = 1; sp < splits; ++sp) {
       const float4 b = part[sp * split4 + i];
       v.x += b.x; v.y += b.y; v.z += b.z; v.w += b.w;
     }
-    for (int r = 0; r < world; ++r) reinterpret_cast<float4*>(peer_red[r])[dst_off4 + i] = v;
+    for (int r = 0; r < world; ++r) reinterpret_cast<float4*>(peer_red[r])[par4 + rank * slot4 + i] = v;
   }
   __threadfence_system();
-}
-
-// Phase 1 of the call's tag: mark it at every rank, wait for every rank;
-// with a device counter, then advance it (one thread, after every wait).
-__global__ void ep_exchange_barrier_kernel(const uint64_t* __restrict__ flags, uint32_t* own_flags, int world,
-                                           int rank, uint32_t epoch, uint32_t* ctr) {
-  const int lane = threadIdx.x;
-  const uint32_t e = call_epoch(epoch, ctr);
-  if (lane < world) {
-    __threadfence_system();
-    flag_release(reinterpret_cast<uint32_t*>(flags[lane]) + world + rank, e);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (atomicAdd(arrive, 1u) == gridDim.x - 1) {  // every CTA of this rank has pushed
+      *reinterpret_cast<volatile uint32_t*>(arrive) = 0;
+      __threadfence_system();
+      for (int r = 0; r < world; ++r)
+        flag_release(reinterpret_cast<uint32_t*>(flags[r]) + world + rank, e);
+    }
+    for (int r = 0; r < world; ++r) flag_wait(own_flags + world + r, e);
   }
-  if (lane < world) flag_wait(own_flags + world + lane, e);
-  __syncwarp();
-  if (epoch == 0 && lane == 0) *reinterpret_cast<volatile uint32_t*>(ctr) = e;
-}
-
-__global__ void __launch_bounds__(kEpThreads)
-    ep_sum_partials_kernel(const float4* __restrict__ red, int world, int64_t n4, int64_t slot4, uint32_t epoch,
-                           const uint32_t* ctr, uint2* __restrict__ out) {
-  // After the barrier the counter holds this call's tag (epoch == 0).
-  const uint32_t e = epoch != 0 ? epoch : *reinterpret_cast<const volatile uint32_t*>(ctr);
-  const float4* slots = red + static_cast<int64_t>(e & 1u) * world * slot4;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+  __syncthreads();
+  const float4* slots = own_red + par4;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4; i += stride) {
     float4 a = slots[i];
     for (int r = 1; r < world; ++r) {
       const float4 b = slots[r * slot4 + i];
@@ -246,6 +248,11 @@ __global__ void __launch_bounds__(kEpThreads)
     }
     const __nv_bfloat162 lo = __floats2bfloat162_rn(a.x, a.y), hi = __floats2bfloat162_rn(a.z, a.w);
     out[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && atomicAdd(depart, 1u) == gridDim.x - 1) {  // every CTA has read e and summed
+    *reinterpret_cast<volatile uint32_t*>(depart) = 0;
+    if (epoch == 0) *reinterpret_cast<volatile uint32_t*>(ctr) = e;
   }
 }
 
@@ -336,19 +343,33 @@ int launch_ep_allreduce(const float* part, int splits, int64_t split_stride, int
   KW8_REQUIRE(((reinterpret_cast<uintptr_t>(part) | reinterpret_cast<uintptr_t>(own_red)) & 15) == 0 &&
                   (reinterpret_cast<uintptr_t>(out) & 7) == 0,
               KW8_ERR_UNSUPPORTED, "partial sums need 16-byte aligned rows");
+  // Every CTA of the launch must be resident at once (they wait for one
+  // another): a cooperative launch of at most the co-resident CTAs.
+  static int max_blocks[64] = {};
+  int dev = 0;
+  KW8_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (max_blocks[dev] == 0) {
+    int per_sm = 0;
+    KW8_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, ep_allreduce_kernel, kEpThreads, 0));
+    int sms = 0;
+    KW8_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    KW8_REQUIRE(per_sm >= 1, KW8_ERR_UNSUPPORTED, "the exchange kernel does not fit an SM");
+    max_blocks[dev] = per_sm * sms;
+  }
   const int64_t n4 = T * D / 4;
   const int64_t slot4 = red_rows * D / 4;  // one rank's slot
-  uint32_t* ctr = own_flags + 3 * world;   // device call counter (epoch == 0)
-  // Every rank takes every phase, also with no rows (the others wait on it).
-  ep_push_partials_kernel<<<ep_grid_blocks(std::max<int64_t>(n4, 1)), kEpThreads, 0, stream>>>(
-      reinterpret_cast<const float4*>(part), splits, split_stride / 4, n4, peer_red, world, rank, slot4, epoch, ctr);
-  KW8_CHECK_LAUNCH();
-  ep_exchange_barrier_kernel<<<1, 32, 0, stream>>>(flags, own_flags, world, rank, epoch, ctr);
-  KW8_CHECK_LAUNCH();
-  if (n4 == 0) return KW8_OK;
-  ep_sum_partials_kernel<<<ep_grid_blocks(n4), kEpThreads, 0, stream>>>(
-      reinterpret_cast<const float4*>(own_red), world, n4, slot4, epoch, ctr, static_cast<uint2*>(out));
-  KW8_CHECK_LAUNCH();
+  const int grid = static_cast<int>(std::max<int64_t>(
+      1, std::min<int64_t>({(n4 + kEpThreads - 1) / kEpThreads, 148 * 2, static_cast<int64_t>(max_blocks[dev])})));
+  const float4* part4 = reinterpret_cast<const float4*>(part);
+  int splits_a = splits;
+  int64_t split4 = split_stride / 4;
+  const float4* red4 = reinterpret_cast<const float4*>(own_red);
+  uint2* out2 = static_cast<uint2*>(out);
+  void* args[] = {&part4, &splits_a, &split4, const_cast<int64_t*>(&n4), &peer_red, &red4, &flags, &own_flags,
+                  &world, &rank, const_cast<int64_t*>(&slot4), &epoch, &out2};
+  KW8_CUDA_TRY(cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(ep_allreduce_kernel), dim3(grid),
+                                           dim3(kEpThreads), args, 0, stream));
   return KW8_OK;
 }
 

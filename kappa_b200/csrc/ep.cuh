@@ -22,10 +22,11 @@ int launch_ep_barrier(const uint64_t* flags, uint32_t* own_flags, int world, int
 int launch_ep_counts(const int32_t* sizes, int64_t E, const uint64_t* counts, const uint64_t* flags,
                      uint32_t* own_flags, int world, int rank, uint32_t epoch, cudaStream_t stream);
 
-// One-shot sum of fp32 partials [T][D] over the group (see ep.cu): push
-// (the sum of `splits` slices split_stride floats apart) into every rank's
-// exchange buffer [2][world][red_rows][D], flag phase 1 of `epoch`, then
-// out = bf16(sum over ranks in rank order).
+// One-shot sum of fp32 partials [T][D] over the group (see ep.cu), one
+// cooperative launch: push (the sum of `splits` slices split_stride floats
+// apart) into every rank's exchange buffer [2][world][red_rows][D], flag
+// phase 1 of `epoch`, then out = bf16(sum over ranks in rank order).  The
+// flags buffer holds 3 * world + 3 words (call count, two CTA counters).
 int launch_ep_allreduce(const float* part, int splits, int64_t split_stride, int64_t T, int64_t D,
                         const uint64_t* peer_red, float* own_red, int64_t red_rows, const uint64_t* flags,
                         uint32_t* own_flags, int world, int rank, uint32_t epoch, void* out, cudaStream_t stream);

@@ -363,7 +363,7 @@ class EPContext:
         pairs = self.world * max_tokens * k
         ret_bytes = 4 if return_fp32 else 2
         sizes = (self.recv_rows * d * 2, self.out_rows * d * 2, 2 * self.world * (num_experts + self.world) * 4,
-                 (3 * self.world + 1) * 4, self.world * max_tokens * d * 2, pairs * 8,
+                 (3 * self.world + 3) * 4, self.world * max_tokens * d * 2, pairs * 8,
                  self.world * max_tokens * d * ret_bytes, 2 * self.world * decode_tokens * d * 4)
         self._bufs = _SharedBuffers(sizes, group, self.device)
         (self.peer_recv, self.peer_out, self.peer_counts, self.peer_flags, self.peer_rows, self.peer_meta,
@@ -426,8 +426,9 @@ class TPContext:
         self.world, self.rank = _world(group)
         self.max_tokens, self.d = max_tokens, d
         self.device = torch.device("cuda", torch.cuda.current_device())
-        # flags [3][world] + the device call counter; exchange slots [2][world][max_tokens][d] fp32
-        self._bufs = _SharedBuffers(((3 * self.world + 1) * 4, 2 * self.world * max_tokens * d * 4), group,
+        # flags [3][world] + the device call counter and two CTA counters of the
+        # exchange kernel; exchange slots [2][world][max_tokens][d] fp32
+        self._bufs = _SharedBuffers(((3 * self.world + 3) * 4, 2 * self.world * max_tokens * d * 4), group,
                                     self.device)
         self.peer_flags, self.peer_red = self._bufs.peer_ptrs
         self.flags_ptr, self.red_ptr = self._bufs.own

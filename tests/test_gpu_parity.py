@@ -496,7 +496,7 @@ def _ep_single_rank_peers(dev, Tm, D, E, k, dedup, ret_f32=True, red_rows=0):
         "recv": torch.zeros((world * Tm * k, D), dtype=torch.bfloat16, device=dev),
         "out": torch.zeros((Tm * k, D), dtype=torch.bfloat16, device=dev),
         "counts": torch.zeros(2 * world * (E + world), dtype=torch.int32, device=dev),
-        "flags": torch.zeros(3 * world + 1, dtype=torch.int32, device=dev),
+        "flags": torch.zeros(3 * world + 3, dtype=torch.int32, device=dev),
         "rows": torch.zeros((world * Tm, D), dtype=torch.bfloat16, device=dev),
         "meta": torch.zeros(2 * world * Tm * k, dtype=torch.int32, device=dev),
         "ret": torch.zeros((world * Tm, D), dtype=torch.float32 if ret_f32 else torch.bfloat16, device=dev),
