@@ -26,7 +26,8 @@ exits; it is the workload the committed ncu summaries capture with the full
 metric set (the full layer is captured with single-pass metrics only).
 
 ``--profile-decode B`` runs two calls of the full configs[1] layer at a
-decode batch of B tokens (the workload of the committed decode captures).
+decode batch of B tokens (the workload of the committed decode captures);
+``--packed`` with it pre-packs the expert weights.
 ``--no-extra-configs`` leaves out the other BASELINE configs (decode
 batches, Gemma3 MLP and stack, the Qwen3-235B-shaped layer), e.g. for a
 launch list of the headline step alone.
@@ -278,8 +279,9 @@ def run_reference(args):
     return 0
 
 
-def run_profile_decode(batch: int):
-    """Two calls of the full configs[1] layer at a decode batch (ncu captures)."""
+def run_profile_decode(batch: int, packed: bool = False):
+    """Two calls of the full configs[1] layer at a decode batch (ncu captures);
+    with ``packed`` the expert weights are pre-packed (pack_weight)."""
     import torch
 
     from kappa_b200.qwen3 import ffn_moe as M
@@ -295,12 +297,17 @@ def run_profile_decode(batch: int):
         return quantize_weight(w, per_channel=True, scale_dtype=torch.float32)
 
     router, gate, up, down = q8((D, E)), q8((E, D, I)), q8((E, D, I)), q8((E, I, D))
+    if packed:
+        from kappa_b200.qwen3.quant import pack_weight
+
+        gate, up, down = (pack_weight(w) for w in (gate, up, down))
     x = torch.randn((1, batch, D), generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16)
     cfg = MoEConfig(use_moe=True, num_experts=E, num_experts_per_tok=K_TOP, moe_impl="ragged_jax")
     for _ in range(2):
         y = M.moe_swiglu_ffn(x, router, gate, up, down, cfg=cfg)
     torch.cuda.synchronize(dev)
-    print(json.dumps({"profile_decode": batch, "mean_abs_out": float(y.float().abs().mean())}), flush=True)
+    print(json.dumps({"profile_decode": batch, "packed": packed, "mean_abs_out": float(y.float().abs().mean())}),
+          flush=True)
     return 0
 
 
@@ -1186,6 +1193,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-small", action="store_true")
     ap.add_argument("--profile-decode", type=int, default=0, metavar="B")
+    ap.add_argument("--packed", action="store_true", help="with --profile-decode: pre-packed expert weights")
     ap.add_argument("--no-extra-configs", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -1193,7 +1201,7 @@ def main():
     if args.profile_small:
         return run_profile_small()
     if args.profile_decode > 0:
-        return run_profile_decode(args.profile_decode)
+        return run_profile_decode(args.profile_decode, args.packed)
     return run_gpu(args)
 
 
