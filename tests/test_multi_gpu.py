@@ -1,8 +1,10 @@
 """Multi-GPU paths on B200s (2 ranks, or KW8_TEST_WORLD ranks):
 expert-parallel MoE (prefill and decode) and tensor-parallel dense MLPs, in
-their one-call NVLink forms and their NCCL forms, each checked against the
-fp32 dequantise-then-dot reference at the 1e-2 bar (the optional bf16
-return of the expert-parallel partial sums at 2e-2).  Skipped with fewer
+their one-call NVLink forms and their NCCL forms, checked against the fp32
+dequantise-then-dot reference: the one-call forms at the 1e-2 bar; the forms
+that store each expert's output row as bf16 before the weighted sum (NCCL
+all-to-allv, one row per routed pair, staged calls) and the optional bf16
+return of the partial sums at the staged entry points' 2e-2.  Skipped with fewer
 GPUs than ranks."""
 
 from __future__ import annotations
@@ -85,14 +87,20 @@ def _rank_main(rank: int, world: int, port: int, errfile: str):
         ref, _, _ = O.moe_reference_f32(x, o_router, o_gate, o_up, o_down, num_experts=E, k=K,
                                         idx=to_np(idx), w=to_np(w))
         errs = {}
-        errs["nccl"] = parity(to_np(y), ref)
+        # The default one-call step (each token once per owner, fp32 partial
+        # sums back) meets the 1e-2 bar.  The NCCL all-to-allv form, the
+        # one-row-per-pair form and the staged calls store every expert's
+        # output row as bf16 before the weighted sum (kappa's own rounding,
+        # ffn_moe.py:213), the single-GPU staged entry points' 2e-2 bar.
+        staged_tol = 2e-2
         errs["p2p"] = parity(to_np(y2), ref)
-        errs["p2p_pair_rows"] = parity(to_np(y7), ref)
+        errs["nccl"] = parity(to_np(y), ref, tol=staged_tol)
+        errs["p2p_pair_rows"] = parity(to_np(y7), ref, tol=staged_tol)
         # buffers reused: the same result up to the order of the fp32 atomic
         # adds of the partial sums (then bf16), as in the single-GPU layer
         d23 = (y2.float() - y3.float()).abs().max().item()
         assert d23 <= 2 ** -7 * y2.float().abs().max().item(), d23
-        errs["staged"] = parity(to_np(y4), ref)
+        errs["staged"] = parity(to_np(y4), ref, tol=staged_tol)
         parity(to_np(y5), ref[:, : 37 + 100 * rank])
         if rank == 0:
             assert tuple(y6.shape) == (1, 0, D)
@@ -109,7 +117,7 @@ def _rank_main(rank: int, world: int, port: int, errfile: str):
         _, idx, w = M.route_logits(to_dev(xd, dev), router, num_experts=E, num_experts_per_tok=K)
         ref_d, _, _ = O.moe_reference_f32(xd, o_router, o_gate, o_up, o_down, num_experts=E, k=K,
                                           idx=to_np(idx), w=to_np(w))
-        errs["decode_nccl"] = parity(to_np(yd), ref_d)
+        errs["decode_nccl"] = parity(to_np(yd), ref_d, tol=staged_tol)
         for rep in range(3):  # both exchange-slot parities, then the first again
             yd2 = S.moe_swiglu_ffn_ep_decode(to_dev(xd, dev), router, gl, ul, dl, cfg=cfg, ctx=ctx)
             errs["decode_p2p"] = parity(to_np(yd2), ref_d)
