@@ -24,6 +24,7 @@ namespace kw8 {
 namespace {
 
 constexpr int kDdThreads = 256;
+constexpr int kCopyBatch = 8;  // 16-byte chunks a lane loads before storing them to a peer
 
 // tok_slot[t][r] and u_cnt[r] (see above).  One CTA of 1024 threads.
 __global__ void __launch_bounds__(1024)
@@ -94,11 +95,25 @@ __global__ void __launch_bounds__(kDdThreads)
   const int wpb = blockDim.x >> 5;
   for (int t = blockIdx.x * wpb + (threadIdx.x >> 5); t < T; t += gridDim.x * wpb) {
     const uint4* src = x + static_cast<int64_t>(t) * vec;
-    for (int r = 0; r < world; ++r) {
-      const int slot = tok_slot[static_cast<int64_t>(t) * world + r];
-      if (slot < 0) continue;  // uniform over the warp
-      uint4* dst = reinterpret_cast<uint4*>(peer_rows[r]) + static_cast<int64_t>(uoff[r] + slot) * vec;
-      for (int c = lane; c < vec; c += 32) dst[c] = __ldg(src + c);
+    for (int c0 = 0; c0 < vec; c0 += 32 * kCopyBatch) {
+      // This lane's chunks of the row in registers first, so the loads are
+      // in flight together (the peer stores may alias them for the compiler).
+      uint4 v[kCopyBatch];
+#pragma unroll
+      for (int j = 0; j < kCopyBatch; ++j) {
+        const int c = c0 + j * 32 + lane;
+        if (c < vec) v[j] = __ldg(src + c);
+      }
+      for (int r = 0; r < world; ++r) {
+        const int slot = tok_slot[static_cast<int64_t>(t) * world + r];
+        if (slot < 0) continue;  // uniform over the warp
+        uint4* dst = reinterpret_cast<uint4*>(peer_rows[r]) + static_cast<int64_t>(uoff[r] + slot) * vec;
+#pragma unroll
+        for (int j = 0; j < kCopyBatch; ++j) {
+          const int c = c0 + j * 32 + lane;
+          if (c < vec) dst[c] = v[j];
+        }
+      }
     }
   }
   const int pairs = off[E];
@@ -162,21 +177,44 @@ __global__ void __launch_bounds__(kDdThreads)
     const float4* src = part + static_cast<int64_t>(u) * (D / 4);
     const int64_t drow = static_cast<int64_t>(rank) * max_tokens + (u - start[s]);
     if (ret_f32) {
+      // Loads of a batch in registers first, then the peer stores (they
+      // may alias for the compiler, which would otherwise serialise them).
       float4* dst = reinterpret_cast<float4*>(peer_ret[s]) + drow * (D / 4);
-      for (int c = lane; c < D / 4; c += 32) dst[c] = src[c];
+      for (int c0 = 0; c0 < D / 4; c0 += 32 * kCopyBatch) {
+        float4 v[kCopyBatch];
+#pragma unroll
+        for (int j = 0; j < kCopyBatch; ++j) {
+          const int c = c0 + j * 32 + lane;
+          if (c < D / 4) v[j] = src[c];
+        }
+#pragma unroll
+        for (int j = 0; j < kCopyBatch; ++j) {
+          const int c = c0 + j * 32 + lane;
+          if (c < D / 4) dst[c] = v[j];
+        }
+      }
       continue;
     }
     uint4* dst = reinterpret_cast<uint4*>(peer_ret[s]) + drow * v8;
-    for (int c = lane; c < v8; c += 32) {
-      const float4 a = src[2 * c], b = src[2 * c + 1];
-      const __nv_bfloat162 p0 = __floats2bfloat162_rn(a.x, a.y), p1 = __floats2bfloat162_rn(a.z, a.w);
-      const __nv_bfloat162 p2 = __floats2bfloat162_rn(b.x, b.y), p3 = __floats2bfloat162_rn(b.z, b.w);
-      uint4 v;
-      v.x = *reinterpret_cast<const uint32_t*>(&p0);
-      v.y = *reinterpret_cast<const uint32_t*>(&p1);
-      v.z = *reinterpret_cast<const uint32_t*>(&p2);
-      v.w = *reinterpret_cast<const uint32_t*>(&p3);
-      dst[c] = v;
+    for (int c0 = 0; c0 < v8; c0 += 32 * kCopyBatch) {
+      uint4 o[kCopyBatch];
+#pragma unroll
+      for (int j = 0; j < kCopyBatch; ++j) {
+        const int c = c0 + j * 32 + lane;
+        if (c >= v8) continue;
+        const float4 a = src[2 * c], b = src[2 * c + 1];
+        const __nv_bfloat162 p0 = __floats2bfloat162_rn(a.x, a.y), p1 = __floats2bfloat162_rn(a.z, a.w);
+        const __nv_bfloat162 p2 = __floats2bfloat162_rn(b.x, b.y), p3 = __floats2bfloat162_rn(b.z, b.w);
+        o[j].x = *reinterpret_cast<const uint32_t*>(&p0);
+        o[j].y = *reinterpret_cast<const uint32_t*>(&p1);
+        o[j].z = *reinterpret_cast<const uint32_t*>(&p2);
+        o[j].w = *reinterpret_cast<const uint32_t*>(&p3);
+      }
+#pragma unroll
+      for (int j = 0; j < kCopyBatch; ++j) {
+        const int c = c0 + j * 32 + lane;
+        if (c < v8) dst[c] = o[j];
+      }
     }
   }
   __threadfence_system();
