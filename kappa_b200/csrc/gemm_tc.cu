@@ -352,6 +352,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int src_row = kPair ? ((lane < 16) ? (q * 16 + lane) : (64 + q * 16 + lane - 16))
                               : (q * 32 + lane);
     const int swz = src_row & 7;  // 128-byte TMA swizzle of this row
+    // Offsets of this thread's four 16-byte chunks within a stage: K-major
+    // tiles, 128-byte rows swizzled by (row & 7); tiled weights, row r's chunk
+    // c of step kh at (r/16) * 2 KB + kh * 1 KB + 512 ((r % 16) / 8) + 16 (8 c + r % 8).
+    uint32_t coff[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      coff[c] = p.a_tiled ? static_cast<uint32_t>((src_row >> 4) * 2048 + kh * 1024 + ((src_row >> 3) & 1) * 512 +
+                                                  (src_row & 7) * 16 + c * 128)
+                          : static_cast<uint32_t>(src_row * kTcBK + (((kh * 4 + c) ^ swz) << 4));
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
@@ -363,16 +372,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           ok = false;
           break;
         }
-        const uint8_t* a_src = smem + stage * stage_bytes + src_row * kTcBK;
-        // Tiled weights: row r's chunk c of step kh at (r/16) * 2 KB + kh * 1 KB
-        // + 512 ((r % 16) / 8) + 16 (8 c + r % 8).
-        const uint8_t* t_src = smem + stage * stage_bytes + (src_row >> 4) * 2048 + kh * 1024 +
-                               ((src_row >> 3) & 1) * 512 + (src_row & 7) * 16;
+        const uint8_t* a_stage = smem + stage * stage_bytes;
         uint32_t v[32];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          const uint4 w = p.a_tiled ? *reinterpret_cast<const uint4*>(t_src + c * 128)
-                                    : *reinterpret_cast<const uint4*>(a_src + (((kh * 4 + c) ^ swz) << 4));
+          const uint4 w = *reinterpret_cast<const uint4*>(a_stage + coff[c]);
           i8x4_to_bf16x4(w.x, v[c * 8 + 0], v[c * 8 + 1]);
           i8x4_to_bf16x4(w.y, v[c * 8 + 2], v[c * 8 + 3]);
           i8x4_to_bf16x4(w.z, v[c * 8 + 4], v[c * 8 + 5]);
