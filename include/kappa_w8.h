@@ -401,10 +401,20 @@ int kw8_ep_local_offsets(const int32_t* counts, int32_t world, int32_t rank,
  *   rows : world * max_tokens rows of D bf16 (tokens sent to this rank);
  *   meta : world * max_tokens * k int32 row indices, then as many fp32
  *          routing weights (one record per routed pair);
- *   ret  : [world][max_tokens] rows of D partial sums coming back, fp32
- *          with ret_f32 (the source then rounds each output once, as one
- *          GPU does) or bf16 (half the return traffic, one more rounding);
+ *   ret  : [world][max_tokens] rows of D partial sums coming back, in
+ *          ret_format: KW8_RET_F32 (4*D bytes a row; the source rounds each
+ *          output once, as one GPU does), KW8_RET_F16_SCALED (2*D bytes a
+ *          row of fp16 values divided by a per-row power of two, then
+ *          [world][max_tokens] fp32 scales after the rows: relative error
+ *          per partial up to 2^-11) or KW8_RET_BF16 (2*D bytes, up to 2^-9);
  * and counts is int32 [2][world][E + world].                               */
+/* Storage of the partial sums an expert-parallel step returns.            */
+typedef enum kw8_ret_format {
+  KW8_RET_BF16 = 0,
+  KW8_RET_F32 = 1,
+  KW8_RET_F16_SCALED = 2,
+} kw8_ret_format;
+
 typedef struct kw8_ep_peers {
   int32_t world;
   int32_t rank;
@@ -423,8 +433,7 @@ typedef struct kw8_ep_peers {
   void* own_rows;
   void* own_meta;
   void* own_ret;
-  int32_t ret_f32; /* partial sums in ret as fp32 (ret rows of 4*D bytes)
-                      instead of bf16 (2*D bytes)                            */
+  int32_t ret_format; /* kw8_ret_format of the partial sums in ret        */
   /* Exchange buffer of the one-shot sums (kw8_moe_ffn_ep_decode,
    * kw8_dense_ffn_tp): fp32 [2][world][red_rows][D] in every rank.         */
   const uint64_t* red;

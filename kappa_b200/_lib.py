@@ -36,6 +36,11 @@ ACT_SILU = 1
 LAYOUT_KMAJOR = 0
 LAYOUT_TILED = 1
 
+# kw8_ret_format (partial sums of the expert-parallel return)
+RET_BF16 = 0
+RET_F32 = 1
+RET_F16_SCALED = 2
+
 # kw8_norm_kind
 NORM_GEMMA = 0  # x * rsqrt(mean(x^2) + eps) * (1 + scale)
 NORM_QWEN = 1  # x * rsqrt(mean(x^2) + eps) * scale
@@ -102,7 +107,7 @@ class KW8EpPeers(ctypes.Structure):
         ("own_rows", ctypes.c_void_p),
         ("own_meta", ctypes.c_void_p),
         ("own_ret", ctypes.c_void_p),
-        ("ret_f32", ctypes.c_int32),
+        ("ret_format", ctypes.c_int32),
         ("red", ctypes.c_void_p),
         ("own_red", ctypes.c_void_p),
         ("red_rows", ctypes.c_int64),

@@ -45,8 +45,8 @@ int launch_ep_gather2(const void* rows, const int32_t* meta, const int32_t* loc_
                       const int32_t* counts, int world, int rank, int64_t E, int64_t D, int64_t max_pairs,
                       void* xs, float* part, cudaStream_t stream);
 int launch_ep_return2(const float* part, int64_t D, const int32_t* counts, int world, int rank, int64_t E,
-                      int64_t max_tokens, const uint64_t* peer_ret, bool ret_f32, cudaStream_t stream);
+                      int64_t max_tokens, const uint64_t* peer_ret, int ret_format, cudaStream_t stream);
 int launch_ep_final2(const void* ret, const int32_t* tok_slot, int64_t T, int world, int64_t max_tokens,
-                     int64_t D, bool ret_f32, void* out, cudaStream_t stream);
+                     int64_t D, int ret_format, void* out, cudaStream_t stream);
 
 }  // namespace kw8

@@ -230,7 +230,7 @@ int kw8_moe_ffn_ep(const void* x, int64_t T, int64_t D, int64_t I, int64_t E, in
   if (dedup) {
     // Each token once per owning rank (ep_dedup.cu).
     KW8_REQUIRE(peers->meta && peers->ret && peers->own_rows && peers->own_meta && peers->own_ret &&
-                    D % 8 == 0,
+                    D % 8 == 0 && peers->ret_format >= KW8_RET_BF16 && peers->ret_format <= KW8_RET_F16_SCALED,
                 KW8_ERR_INVALID_ARG, "incomplete peers for the deduplicated step");
     const int64_t pair_cap = recv_rows;
     rc = launch_ep_slots(b.idx, b.inv_pos, T, k, E, world, b.tok_slot, b.u_cnt, stream);
@@ -261,14 +261,14 @@ int kw8_moe_ffn_ep(const void* x, int64_t T, int64_t D, int64_t I, int64_t E, in
                     b.loc_off, gate_local, up_local, down_local, b.part, b.eb, stream, meta_u, meta_w);
     if (rc) return rc;
     clock.mark(6);
-    rc = launch_ep_return2(b.part, D, cnt, world, rank, E, peers->max_tokens, peers->ret, peers->ret_f32 != 0,
+    rc = launch_ep_return2(b.part, D, cnt, world, rank, E, peers->max_tokens, peers->ret, peers->ret_format,
                            stream);
     if (rc) return rc;
     clock.mark(7);
     rc = launch_ep_barrier(peers->flags, peers->own_flags, world, rank, 2, epoch, true, stream);
     if (rc) return rc;
     clock.mark(8);
-    rc = launch_ep_final2(peers->own_ret, b.tok_slot, T, world, peers->max_tokens, D, peers->ret_f32 != 0, out,
+    rc = launch_ep_final2(peers->own_ret, b.tok_slot, T, world, peers->max_tokens, D, peers->ret_format, out,
                           stream);
     if (!rc) clock.done();
     return rc;

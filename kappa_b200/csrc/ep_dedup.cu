@@ -16,7 +16,9 @@
 // indexed by the records); each partial goes back to its source as bf16
 // (ret[r][slot] on the source), and the source sums its partials over the
 // ranks in rank order.  The partials travel as fp32 (the sum is rounded
-// once, as on one GPU) or, to halve the return traffic, as bf16.
+// once, as on one GPU), as fp16 with a per-row power-of-two scale (half the
+// traffic, relative error per partial up to 2^-11) or as bf16 (half the
+// traffic, up to 2^-9).
 #include "ep.cuh"
 
 namespace kw8 {
@@ -152,11 +154,17 @@ __global__ void __launch_bounds__(kDdThreads)
 }
 
 // Owner side: partial row u (source s, slot u - uoff(rank, s)) into source
-// s's return buffer at [rank][slot]: fp32 as computed (ret_f32), or bf16.
+// s's return buffer at [rank][slot], in the group's return format:
+//   KW8_RET_F32        fp32 as computed;
+//   KW8_RET_BF16       bf16 (one rounding, relative error up to 2^-9);
+//   KW8_RET_F16_SCALED fp16 of the row divided by a power of two 2^(e-14),
+//                      e = floor(log2 max|row|), so every value is a normal
+//                      fp16 (relative error up to 2^-11) at bf16's size; the
+//                      scale goes to the return buffer's scale array.
 // A warp per row.
 __global__ void __launch_bounds__(kDdThreads)
     ep_return2_kernel(const float4* __restrict__ part, int D, const int32_t* __restrict__ counts, int world,
-                      int rank, int E, int64_t max_tokens, const uint64_t* __restrict__ peer_ret, int ret_f32) {
+                      int rank, int E, int64_t max_tokens, const uint64_t* __restrict__ peer_ret, int fmt) {
   __shared__ int start[kEpMaxRanks + 1];  // first row of each source
   if (threadIdx.x == 0) {
     int acc = 0;
@@ -176,7 +184,7 @@ __global__ void __launch_bounds__(kDdThreads)
     while (s + 1 < world && start[s + 1] <= u) ++s;
     const float4* src = part + static_cast<int64_t>(u) * (D / 4);
     const int64_t drow = static_cast<int64_t>(rank) * max_tokens + (u - start[s]);
-    if (ret_f32) {
+    if (fmt == KW8_RET_F32) {
       // Loads of a batch in registers first, then the peer stores (they
       // may alias for the compiler, which would otherwise serialise them).
       float4* dst = reinterpret_cast<float4*>(peer_ret[s]) + drow * (D / 4);
@@ -195,6 +203,24 @@ __global__ void __launch_bounds__(kDdThreads)
       }
       continue;
     }
+    float inv = 1.0f;  // 1 / scale (KW8_RET_F16_SCALED)
+    if (fmt == KW8_RET_F16_SCALED) {
+      float m = 0.f;
+      for (int c = lane; c < D / 4; c += 32) {
+        const float4 a = src[c];
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      int e = 0;
+      if (m > 0.f && m <= 3.0e38f) e = max(ilogbf(m), -100);  // NaN / inf rows keep scale 1
+      inv = ldexpf(1.0f, 14 - e);
+      if (lane == 0) {
+        float* scales = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(peer_ret[s]) +
+                                                 static_cast<int64_t>(world) * max_tokens * D * 2);
+        scales[drow] = ldexpf(1.0f, e - 14);
+      }
+    }
     uint4* dst = reinterpret_cast<uint4*>(peer_ret[s]) + drow * v8;
     for (int c0 = 0; c0 < v8; c0 += 32 * kCopyBatch) {
       uint4 o[kCopyBatch];
@@ -203,12 +229,23 @@ __global__ void __launch_bounds__(kDdThreads)
         const int c = c0 + j * 32 + lane;
         if (c >= v8) continue;
         const float4 a = src[2 * c], b = src[2 * c + 1];
-        const __nv_bfloat162 p0 = __floats2bfloat162_rn(a.x, a.y), p1 = __floats2bfloat162_rn(a.z, a.w);
-        const __nv_bfloat162 p2 = __floats2bfloat162_rn(b.x, b.y), p3 = __floats2bfloat162_rn(b.z, b.w);
-        o[j].x = *reinterpret_cast<const uint32_t*>(&p0);
-        o[j].y = *reinterpret_cast<const uint32_t*>(&p1);
-        o[j].z = *reinterpret_cast<const uint32_t*>(&p2);
-        o[j].w = *reinterpret_cast<const uint32_t*>(&p3);
+        uint32_t w[4];
+        if (fmt == KW8_RET_F16_SCALED) {
+          const __half2 h0 = __floats2half2_rn(a.x * inv, a.y * inv), h1 = __floats2half2_rn(a.z * inv, a.w * inv);
+          const __half2 h2 = __floats2half2_rn(b.x * inv, b.y * inv), h3 = __floats2half2_rn(b.z * inv, b.w * inv);
+          w[0] = *reinterpret_cast<const uint32_t*>(&h0);
+          w[1] = *reinterpret_cast<const uint32_t*>(&h1);
+          w[2] = *reinterpret_cast<const uint32_t*>(&h2);
+          w[3] = *reinterpret_cast<const uint32_t*>(&h3);
+        } else {
+          const __nv_bfloat162 p0 = __floats2bfloat162_rn(a.x, a.y), p1 = __floats2bfloat162_rn(a.z, a.w);
+          const __nv_bfloat162 p2 = __floats2bfloat162_rn(b.x, b.y), p3 = __floats2bfloat162_rn(b.z, b.w);
+          w[0] = *reinterpret_cast<const uint32_t*>(&p0);
+          w[1] = *reinterpret_cast<const uint32_t*>(&p1);
+          w[2] = *reinterpret_cast<const uint32_t*>(&p2);
+          w[3] = *reinterpret_cast<const uint32_t*>(&p3);
+        }
+        o[j] = make_uint4(w[0], w[1], w[2], w[3]);
       }
 #pragma unroll
       for (int j = 0; j < kCopyBatch; ++j) {
@@ -221,14 +258,16 @@ __global__ void __launch_bounds__(kDdThreads)
 }
 
 // Source side: out[t] = sum over ranks r (in order) of ret[r][tok_slot[t][r]]
-// (fp32 or bf16 partials) in fp32, then bf16 (zero for a token with no kept
-// slot).  A warp per token.
+// (partials in the group's return format) in fp32, then bf16 (zero for a
+// token with no kept slot).  A warp per token.
 __global__ void __launch_bounds__(kDdThreads)
     ep_final2_kernel(const void* __restrict__ ret, const int32_t* __restrict__ tok_slot, int T, int world,
-                     int64_t max_tokens, int D, int ret_f32, uint4* __restrict__ out) {
+                     int64_t max_tokens, int D, int fmt, uint4* __restrict__ out) {
   const int lane = threadIdx.x & 31;
   const int wpb = blockDim.x >> 5;
   const int v8 = D / 8;
+  const float* scales =
+      reinterpret_cast<const float*>(static_cast<const uint8_t*>(ret) + static_cast<int64_t>(world) * max_tokens * D * 2);
   for (int t = blockIdx.x * wpb + (threadIdx.x >> 5); t < T; t += gridDim.x * wpb) {
     for (int c = lane; c < v8; c += 32) {
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -236,7 +275,7 @@ __global__ void __launch_bounds__(kDdThreads)
         const int slot = tok_slot[static_cast<int64_t>(t) * world + r];
         if (slot < 0) continue;
         const int64_t row = static_cast<int64_t>(r) * max_tokens + slot;
-        if (ret_f32) {
+        if (fmt == KW8_RET_F32) {
           const float4* p = static_cast<const float4*>(ret) + row * (D / 4) + 2 * c;
           const float4 a = p[0], b = p[1];
           acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
@@ -245,6 +284,16 @@ __global__ void __launch_bounds__(kDdThreads)
         }
         const uint4 v = static_cast<const uint4*>(ret)[row * v8 + c];
         const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+        if (fmt == KW8_RET_F16_SCALED) {
+          const float sc = scales[row];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[i]));
+            acc[2 * i] += f.x * sc;
+            acc[2 * i + 1] += f.y * sc;
+          }
+          continue;
+        }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           acc[2 * i] += __uint_as_float(w4[i] << 16);
@@ -315,19 +364,19 @@ int launch_ep_gather2(const void* rows, const int32_t* meta, const int32_t* loc_
 }
 
 int launch_ep_return2(const float* part, int64_t D, const int32_t* counts, int world, int rank, int64_t E,
-                      int64_t max_tokens, const uint64_t* peer_ret, bool ret_f32, cudaStream_t stream) {
+                      int64_t max_tokens, const uint64_t* peer_ret, int ret_format, cudaStream_t stream) {
   ep_return2_kernel<<<ep_grid(static_cast<int64_t>(world) * max_tokens, kDdThreads / 32), kDdThreads, 0,
                       stream>>>(reinterpret_cast<const float4*>(part), static_cast<int>(D), counts, world, rank,
-                                static_cast<int>(E), max_tokens, peer_ret, ret_f32 ? 1 : 0);
+                                static_cast<int>(E), max_tokens, peer_ret, ret_format);
   KW8_CHECK_LAUNCH();
   return KW8_OK;
 }
 
 int launch_ep_final2(const void* ret, const int32_t* tok_slot, int64_t T, int world, int64_t max_tokens,
-                     int64_t D, bool ret_f32, void* out, cudaStream_t stream) {
+                     int64_t D, int ret_format, void* out, cudaStream_t stream) {
   if (T <= 0) return KW8_OK;
   ep_final2_kernel<<<ep_grid(T, kDdThreads / 32), kDdThreads, 0, stream>>>(
-      ret, tok_slot, static_cast<int>(T), world, max_tokens, static_cast<int>(D), ret_f32 ? 1 : 0,
+      ret, tok_slot, static_cast<int>(T), world, max_tokens, static_cast<int>(D), ret_format,
       static_cast<uint4*>(out));
   KW8_CHECK_LAUNCH();
   return KW8_OK;

@@ -342,7 +342,7 @@ class EPContext:
     """
 
     def __init__(self, *, max_tokens: int, d: int, k: int, hidden: int, num_experts: int, group=None,
-                 dedup: bool = True, return_fp32: bool = True, decode_tokens: int = 256):
+                 dedup: bool = True, return_format: str = "f16", decode_tokens: int = 256):
         self.group = group
         self.world, self.rank = _world(group)
         if num_experts % self.world:
@@ -357,14 +357,20 @@ class EPContext:
         # [2][world][E + world] int32, phase flags [3][world] uint32, and for
         # the deduplicated step: token rows [world * max_tokens][d], pair
         # records (int32 row + fp32 weight per received pair), partial sums
-        # [world][max_tokens][d], fp32 (return_fp32: the source rounds each
-        # output once, as one GPU does) or bf16 (half the return traffic);
+        # [world][max_tokens][d] in `return_format`: "f16" (fp16 rows scaled
+        # by a per-row power of two, + a fp32 scale per row: bf16's traffic,
+        # relative error per partial up to 2^-11), "f32" (the source rounds
+        # each output once, as one GPU does) or "bf16" (up to 2^-9);
         # and the decode exchange buffer [2][world][decode_tokens][d] fp32.
+        fmts = {"bf16": _lib.RET_BF16, "f32": _lib.RET_F32, "f16": _lib.RET_F16_SCALED}
+        if return_format not in fmts:
+            raise ValueError(f"return_format must be one of {sorted(fmts)}, got {return_format!r}")
+        self.return_format = return_format
         pairs = self.world * max_tokens * k
-        ret_bytes = 4 if return_fp32 else 2
+        ret_row = d * (4 if return_format == "f32" else 2) + (4 if return_format == "f16" else 0)
         sizes = (self.recv_rows * d * 2, self.out_rows * d * 2, 2 * self.world * (num_experts + self.world) * 4,
                  (3 * self.world + 3) * 4, self.world * max_tokens * d * 2, pairs * 8,
-                 self.world * max_tokens * d * ret_bytes, 2 * self.world * decode_tokens * d * 4)
+                 self.world * max_tokens * ret_row, 2 * self.world * decode_tokens * d * 4)
         self._bufs = _SharedBuffers(sizes, group, self.device)
         (self.peer_recv, self.peer_out, self.peer_counts, self.peer_flags, self.peer_rows, self.peer_meta,
          self.peer_ret, self.peer_red) = self._bufs.peer_ptrs
@@ -377,7 +383,7 @@ class EPContext:
             self.counts_ptr, self.flags_ptr,
             self.peer_rows.data_ptr() if dedup else None, self.peer_meta.data_ptr() if dedup else None,
             self.peer_ret.data_ptr() if dedup else None, self.rows_ptr if dedup else None,
-            self.meta_ptr if dedup else None, self.ret_ptr if dedup else None, int(bool(return_fp32)),
+            self.meta_ptr if dedup else None, self.ret_ptr if dedup else None, fmts[return_format],
             self.peer_red.data_ptr(), self.red_ptr, decode_tokens)
         self.epoch = 0  # calls of the fused steps so far (the group's phase tag)
         self.ep_ws = torch.empty(

@@ -489,7 +489,7 @@ def test_moe_errors_match_kappa():
                                                       moe_impl="fixed_capacity", moe_capacity_factor=0.0))
 
 
-def _ep_single_rank_peers(dev, Tm, D, E, k, dedup, ret_f32=True, red_rows=0):
+def _ep_single_rank_peers(dev, Tm, D, E, k, dedup, ret_format=_lib.RET_F16_SCALED, red_rows=0):
     """A one-rank expert-parallel group: its own buffers are the peers'."""
     world = 1
     bufs = {
@@ -499,7 +499,9 @@ def _ep_single_rank_peers(dev, Tm, D, E, k, dedup, ret_f32=True, red_rows=0):
         "flags": torch.zeros(3 * world + 3, dtype=torch.int32, device=dev),
         "rows": torch.zeros((world * Tm, D), dtype=torch.bfloat16, device=dev),
         "meta": torch.zeros(2 * world * Tm * k, dtype=torch.int32, device=dev),
-        "ret": torch.zeros((world * Tm, D), dtype=torch.float32 if ret_f32 else torch.bfloat16, device=dev),
+        # rows of D partial sums (4 or 2 bytes each) + one fp32 scale per row (fp16 rows)
+        "ret": torch.zeros(world * Tm * (D * (4 if ret_format == _lib.RET_F32 else 2) + 4), dtype=torch.uint8,
+                           device=dev),
         "red": torch.zeros((2, world, max(red_rows, 1), D), dtype=torch.float32, device=dev),
     }
     arr = {n: torch.tensor([t.data_ptr()], dtype=torch.int64, device=dev) for n, t in bufs.items()}
@@ -509,18 +511,19 @@ def _ep_single_rank_peers(dev, Tm, D, E, k, dedup, ret_f32=True, red_rows=0):
         bufs["flags"].data_ptr(),
         arr["rows"].data_ptr() if dedup else None, arr["meta"].data_ptr() if dedup else None,
         arr["ret"].data_ptr() if dedup else None, bufs["rows"].data_ptr() if dedup else None,
-        bufs["meta"].data_ptr() if dedup else None, bufs["ret"].data_ptr() if dedup else None, int(ret_f32),
+        bufs["meta"].data_ptr() if dedup else None, bufs["ret"].data_ptr() if dedup else None, ret_format,
         arr["red"].data_ptr(), bufs["red"].data_ptr(), red_rows)
     return p, (bufs, arr)
 
 
-@pytest.mark.parametrize("dedup,ret_f32", [(True, True), (True, False), (False, True)])
-def test_moe_ep_single_rank(dedup, ret_f32):
+@pytest.mark.parametrize("dedup,ret_format", [(True, _lib.RET_F16_SCALED), (True, _lib.RET_F32), (True, _lib.RET_BF16),
+                                               (False, _lib.RET_F16_SCALED)])
+def test_moe_ep_single_rank(dedup, ret_format):
     """kw8_moe_ffn_ep on a group of one rank: every step of the expert-parallel
     call (counts exchange, row and record dispatch, phase flags, local
     experts, return, combine) runs on one GPU against the fp32 reference, for
     two calls in a row (epochs 1 and 2, both count copies).  The partial sums
-    return as fp32 (or as bf16, one more rounding)."""
+    return as fp16 with a per-row scale, fp32 or bf16."""
     import ctypes
 
     from kappa_b200.qwen3.quant import kmajor
@@ -528,7 +531,7 @@ def test_moe_ep_single_rank(dedup, ret_f32):
     T, D, I, E, k = 200, 256, 128, 16, 4
     x, g, o = _moe_case(T, D, I, E, k, True, seed=31)
     dev = torch.device("cuda", 0)
-    peers, keep = _ep_single_rank_peers(dev, T, D, E, k, dedup, ret_f32)
+    peers, keep = _ep_single_rank_peers(dev, T, D, E, k, dedup, ret_format)
     lib = _lib.load()
     ws = torch.empty(int(lib.kw8_moe_ffn_ep_workspace_size(T, D, I, E, k, 1)), dtype=torch.uint8, device=dev)
     km = [kmajor(w, -2) for w in g]
@@ -565,7 +568,7 @@ def test_moe_ep_decode_single_rank(B):
     D, I, E, k = 512, 256, 32, 8
     x, g, o = _moe_case(B, D, I, E, k, True, seed=B + 5)
     dev = torch.device("cuda", 0)
-    peers, keep = _ep_single_rank_peers(dev, B, D, E, k, True, True, red_rows=256)
+    peers, keep = _ep_single_rank_peers(dev, B, D, E, k, True, red_rows=256)
     lib = _lib.load()
     ws = torch.empty(int(lib.kw8_moe_ffn_ep_decode_workspace_size(B, D, I, E, k)), dtype=torch.uint8, device=dev)
     km = [kmajor(w, -2) for w in g]
@@ -598,7 +601,7 @@ def test_dense_ffn_tp_single_rank(T, act):
     gating, linear = normal(rng, (2, H, D), 0.02), normal(rng, (H, D), 0.02)
     gt, lw = _gpu_q(gating, True, -1), _gpu_q(linear, True, -2)
     dev = torch.device("cuda", 0)
-    peers, keep = _ep_single_rank_peers(dev, 1, D, 4, 1, False, True, red_rows=512)
+    peers, keep = _ep_single_rank_peers(dev, 1, D, 4, 1, False, red_rows=512)
     g, l2 = kmajor(gt, -1), kmajor(lw, -2)
     lib = _lib.load()
     ws = torch.empty(int(lib.kw8_dense_ffn_tp_workspace_size(T, D, H)), dtype=torch.uint8, device=dev)

@@ -71,9 +71,12 @@ def _rank_main(rank: int, world: int, port: int, errfile: str):
         ctx_nd = S.EPContext(max_tokens=max_tok, d=D, k=K, hidden=I, num_experts=E, dedup=False)
         y7 = S.moe_swiglu_ffn_ep(to_dev(x, dev), router, gl, ul, dl, cfg=cfg, ctx=ctx_nd)  # a row per routed pair
         ctx_nd.close()
-        ctx_b = S.EPContext(max_tokens=max_tok, d=D, k=K, hidden=I, num_experts=E, return_fp32=False)
+        ctx_b = S.EPContext(max_tokens=max_tok, d=D, k=K, hidden=I, num_experts=E, return_format="bf16")
         y8 = S.moe_swiglu_ffn_ep(to_dev(x, dev), router, gl, ul, dl, cfg=cfg, ctx=ctx_b)  # bf16 partials back
         ctx_b.close()
+        ctx_f = S.EPContext(max_tokens=max_tok, d=D, k=K, hidden=I, num_experts=E, return_format="f32")
+        y9 = S.moe_swiglu_ffn_ep(to_dev(x, dev), router, gl, ul, dl, cfg=cfg, ctx=ctx_f)  # fp32 partials back
+        ctx_f.close()
         # a rank with fewer tokens than the others, then with none at all
         few = to_dev(x[:, : 37 + 100 * rank], dev)
         y5 = S.moe_swiglu_ffn_ep(few, router, gl, ul, dl, cfg=cfg, ctx=ctx)
@@ -93,7 +96,8 @@ def _rank_main(rank: int, world: int, port: int, errfile: str):
         # output row as bf16 before the weighted sum (kappa's own rounding,
         # ffn_moe.py:213), the single-GPU staged entry points' 2e-2 bar.
         staged_tol = 2e-2
-        errs["p2p"] = parity(to_np(y2), ref)
+        errs["p2p"] = parity(to_np(y2), ref)  # default: fp16 partials with a per-row scale
+        errs["p2p_f32_return"] = parity(to_np(y9), ref)
         errs["nccl"] = parity(to_np(y), ref, tol=staged_tol)
         errs["p2p_pair_rows"] = parity(to_np(y7), ref, tol=staged_tol)
         # buffers reused: the same result up to the order of the fp32 atomic
