@@ -59,3 +59,39 @@ def test_invalid_arguments_fail_before_any_launch():
     assert "null" in L.last_error()
     assert lib.kw8_set_option(0, 7) == L.KW8_ERR_INVALID_ARG
     assert lib.kw8_set_option(1, 24) == L.KW8_ERR_INVALID_ARG
+
+
+def test_new_entry_points_reject_bad_arguments_before_any_launch():
+    """Null pointers, bad shapes and bad enums of the linear, embedding,
+    norm, block, packing and group entry points fail on the host."""
+    import ctypes
+
+    lib = L.load()
+    w = L.KW8Weight(None, None, 0, 0, 0, 0)
+    ok_w = L.KW8Weight(1 << 20, 1 << 20, L.DT_F32, 1, L.LAYOUT_KMAJOR, 0)  # never dereferenced
+    assert lib.kw8_linear(None, None, 4, 64, 64, w, L.DT_BF16, None, None, 0, None) == L.KW8_ERR_INVALID_ARG
+    assert lib.kw8_linear(1 << 20, None, 4, 64, 64, ok_w, 7, 1 << 20, None, 0, None) == L.KW8_ERR_INVALID_ARG
+    bad_layout = L.KW8Weight(1 << 20, 1 << 20, L.DT_F32, 1, 5, 0)
+    assert lib.kw8_linear(1 << 20, None, 4, 64, 64, bad_layout, L.DT_BF16, 1 << 20, None, 0, None) == \
+        L.KW8_ERR_INVALID_ARG
+    assert "layout" in L.last_error()
+    assert lib.kw8_embed_gather(None, 4, w, 10, 64, L.DT_BF16, None, None) == L.KW8_ERR_INVALID_ARG
+    # D must be a multiple of 8 and at most 16384; the kind must be known
+    assert lib.kw8_rms_norm(1 << 20, 4, 12, 1 << 20, L.DT_BF16, L.NORM_GEMMA, 1e-6, 1 << 20, None) == \
+        L.KW8_ERR_UNSUPPORTED
+    assert lib.kw8_rms_norm(1 << 20, 4, 64, 1 << 20, L.DT_BF16, 9, 1e-6, 1 << 20, None) == L.KW8_ERR_INVALID_ARG
+    norms = L.KW8BlockNorms(None, None, L.DT_BF16, L.NORM_QWEN, 1e-6)
+    assert lib.kw8_dense_block(1 << 20, 4, 64, 128, ok_w, ok_w, ok_w, L.ACT_SILU, ctypes.byref(norms), 2 << 20,
+                               None, 0, None) == L.KW8_ERR_INVALID_ARG
+    assert "pre-FFN" in L.last_error()
+    assert lib.kw8_moe_block(1 << 20, 4, 64, 32, 8, 2, -1, ok_w, ok_w, ok_w, ok_w, ctypes.byref(norms), 1 << 20,
+                             None, 0, None) == L.KW8_ERR_INVALID_ARG  # out aliases h
+    assert lib.kw8_pack_weight(1 << 20, 1, 16, 24, 1 << 20, None) == L.KW8_ERR_INVALID_ARG  # K % 16
+    assert lib.kw8_packed_weight_bytes(2, 100, 208) == 2 * 7 * 4 * 1024
+    peers = L.KW8EpPeers()
+    peers.world, peers.rank = 2, 0
+    assert lib.kw8_dense_ffn_tp(1 << 20, 4, 64, 128, ok_w, ok_w, ok_w, L.ACT_SILU, 1 << 20, ctypes.byref(peers), 0,
+                                None, 0, None) == L.KW8_ERR_INVALID_ARG
+    assert "exchange buffer" in L.last_error()
+    ms = (ctypes.c_float * 9)()
+    assert lib.kw8_ep_phase_times(ms, 0) != L.KW8_OK
