@@ -1,8 +1,10 @@
 // W8 quantisation (kappa/qwen3/quant.py:41-48) and dequantisation
 // (quant.py:34-38) kernels.
 //
-// quantize: pass 1 takes the absmax of every output channel (one thread per
-// channel, walking K) and, for the per-tensor form, folds it into one word
+// quantize: pass 1 takes the absmax of every output channel (a warp per
+// channel when K is contiguous, else a thread per channel walking K, the
+// threads then reading consecutive channels) and, for the per-tensor form,
+// folds it into one word
 // with an integer atomicMax on the float's bits (valid for non-negative
 // floats; max is order independent, so the result is deterministic).
 // Pass 2 computes scale = max(amax / 127, FLT_MIN) with IEEE division,
@@ -20,6 +22,8 @@ __device__ __forceinline__ float load_w(const void* w, int dtype, int64_t i) {
   return bf16_bits_to_f32(static_cast<const uint16_t*>(w)[i]);
 }
 
+// A thread per output channel walking K: coalesced across threads when the
+// channels are contiguous (sn == 1, N-contiguous input).
 __global__ void amax_kernel(const void* __restrict__ w, int dtype, int64_t outer, int64_t K,
                             int64_t N, int64_t so, int64_t sk, int64_t sn, int per_channel,
                             float* __restrict__ ch_amax, unsigned* __restrict__ glob) {
@@ -29,6 +33,28 @@ __global__ void amax_kernel(const void* __restrict__ w, int dtype, int64_t outer
   const int64_t base = o * so + n * sn;
   float m = 0.f;
   for (int64_t k = 0; k < K; ++k) m = fmaxf(m, fabsf(load_w(w, dtype, base + k * sk)));
+  if (per_channel)
+    ch_amax[ch] = m;
+  else
+    atomicMax(glob, __float_as_uint(m));
+}
+
+// A warp per output channel with K contiguous (sk == 1): the lanes read
+// consecutive k and reduce with shuffles (max is order independent, so the
+// result equals the serial walk's).
+__global__ void amax_rows_kernel(const void* __restrict__ w, int dtype, int64_t outer, int64_t K,
+                                 int64_t N, int64_t so, int64_t sn, int per_channel,
+                                 float* __restrict__ ch_amax, unsigned* __restrict__ glob) {
+  const int lane = threadIdx.x & 31;
+  const int64_t ch = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  if (ch >= outer * N) return;  // uniform over the warp
+  const int64_t o = ch / N, n = ch - o * N;
+  const int64_t base = o * so + n * sn;
+  float m = 0.f;
+  for (int64_t k = lane; k < K; k += 32) m = fmaxf(m, fabsf(load_w(w, dtype, base + k)));
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+  if (lane != 0) return;
   if (per_channel)
     ch_amax[ch] = m;
   else
@@ -192,8 +218,13 @@ int launch_quantize(const void* w, int w_dtype, int64_t outer, int64_t K, int64_
   unsigned* glob = reinterpret_cast<unsigned*>(ch_amax + outer * N);
   KW8_CUDA_TRY(cudaMemsetAsync(glob, 0, sizeof(unsigned), stream));
   const int64_t channels = outer * N;
-  amax_kernel<<<static_cast<unsigned>((channels + 255) / 256), 256, 0, stream>>>(
-      w, w_dtype, outer, K, N, so, sk, sn, per_channel, ch_amax, glob);
+  if (sk == 1) {  // K contiguous: a warp per channel
+    amax_rows_kernel<<<static_cast<unsigned>((channels * 32 + 255) / 256), 256, 0, stream>>>(
+        w, w_dtype, outer, K, N, so, sn, per_channel, ch_amax, glob);
+  } else {
+    amax_kernel<<<static_cast<unsigned>((channels + 255) / 256), 256, 0, stream>>>(
+        w, w_dtype, outer, K, N, so, sk, sn, per_channel, ch_amax, glob);
+  }
   KW8_CHECK_LAUNCH();
   const int64_t threads = channels * ((K + 15) / 16);
   const int k_fast = (sk == 1) ? 1 : 0;
