@@ -28,7 +28,9 @@ metric set (the full layer is captured with single-pass metrics only).
 ``--profile-decode B`` runs two calls of the full configs[1] layer at a
 decode batch of B tokens (the workload of the committed decode captures);
 ``--packed`` with it pre-packs the expert weights.
-``--no-extra-configs`` leaves out the other BASELINE configs (decode
+``--profile-block`` runs two calls each of the fused FFN sub-blocks (the
+Qwen3 MoE block at configs[1], the Gemma3-4B block at T=256) for ncu launch
+lists.  ``--no-extra-configs`` leaves out the other BASELINE configs (decode
 batches, Gemma3 MLP and stack, the Qwen3-235B-shaped layer), e.g. for a
 launch list of the headline step alone.
 
@@ -307,6 +309,45 @@ def run_profile_decode(batch: int, packed: bool = False):
         y = M.moe_swiglu_ffn(x, router, gate, up, down, cfg=cfg)
     torch.cuda.synchronize(dev)
     print(json.dumps({"profile_decode": batch, "packed": packed, "mean_abs_out": float(y.float().abs().mean())}),
+          flush=True)
+    return 0
+
+
+def run_profile_block():
+    """Two calls each of the fused FFN sub-blocks (ncu launch lists): the
+    Qwen3 MoE block at configs[1] (T=4096) and the Gemma3-4B block at T=256."""
+    import torch
+
+    from kappa_b200.gemma3 import block as gblock
+    from kappa_b200.qwen3 import block as qblock
+    from kappa_b200.qwen3.architecture import MoEConfig
+    from kappa_b200.qwen3.quant import quantize_weight
+
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(0)
+
+    def q8(shape, in_axis=-2):
+        w = torch.randn(shape, generator=gen, device=dev, dtype=torch.float32) * 0.02
+        return quantize_weight(w, per_channel=True, scale_dtype=torch.float32, in_axis=in_axis)
+
+    class Moe:
+        pass
+
+    moe = Moe()
+    moe.router, moe.gate_proj, moe.up_proj, moe.down_proj = q8((D, E)), q8((E, D, I)), q8((E, D, I)), q8((E, I, D))
+    h = torch.randn((1, T_TOK, D), generator=gen, device=dev).to(torch.bfloat16)
+    pre = (1 + torch.randn(D, generator=gen, device=dev) * 0.1).to(torch.bfloat16)
+    cfg = MoEConfig(use_moe=True, num_experts=E, num_experts_per_tok=K_TOP, moe_impl="ragged_jax")
+    dg, hg = 2560, 10240
+    gating, linear = q8((2, hg, dg), in_axis=-1), q8((hg, dg))
+    hgm = torch.randn((1, 256, dg), generator=gen, device=dev).to(torch.bfloat16)
+    pg = (torch.randn(dg, generator=gen, device=dev) * 0.1).to(torch.bfloat16)
+    for _ in range(2):
+        y = qblock.ffn_sub_block(h, pre, moe, cfg=cfg)
+        z = gblock.ffn_sub_block(hgm, pg, gating, linear, pg, transpose_gating_einsum=True)
+    torch.cuda.synchronize(dev)
+    print(json.dumps({"profile_block": "ok", "mean_abs": [float(y.float().abs().mean()), float(z.float().abs().mean())]}),
           flush=True)
     return 0
 
@@ -1192,6 +1233,7 @@ def main():
     ap.add_argument("--impl", default="kappa_b200", choices=["kappa_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-small", action="store_true")
+    ap.add_argument("--profile-block", action="store_true")
     ap.add_argument("--profile-decode", type=int, default=0, metavar="B")
     ap.add_argument("--packed", action="store_true", help="with --profile-decode: pre-packed expert weights")
     ap.add_argument("--no-extra-configs", action="store_true")
@@ -1200,6 +1242,8 @@ def main():
         return run_reference(args)
     if args.profile_small:
         return run_profile_small()
+    if args.profile_block:
+        return run_profile_block()
     if args.profile_decode > 0:
         return run_profile_decode(args.profile_decode, args.packed)
     return run_gpu(args)
