@@ -2,9 +2,11 @@
 // kappa/qwen3/norms.py:10-16 with Qwen's scale) and the residual epilogue of
 // the FFN sub-block (kappa/gemma3/block.py:73-82, kappa/qwen3/block.py:68-81).
 //
-// A CTA per row.  The row is read once into registers (8-wide vectors),
-// the sum of squares is reduced over the CTA in fp32, and the row is written
-// once.  Rounding follows kappa: the norm computes in fp32 and rounds its
+// A CTA of 256 threads takes 256 / tpr rows, tpr threads per row (the
+// fewest, from 32, that hold the row in at most kNormMaxVec 8-wide vectors
+// each: one warp per 2048-wide row).  The row is read once into registers,
+// the sum of squares is reduced over the row's threads in fp32 (a fixed
+// order), and the row is written once.  Rounding follows kappa: the norm computes in fp32 and rounds its
 // output to the activation dtype once; the FFN output is rounded to bf16
 // before the post-FFN norm, and the residual add rounds once more.
 #include "norm.cuh"
@@ -13,16 +15,19 @@ namespace kw8 {
 
 namespace {
 
-__device__ __forceinline__ float block_sum(float v, float* red) {
+// Sum of v over the tpr threads of this thread's row group (every thread
+// of the CTA calls it; the result is the same in every thread of a group).
+__device__ __forceinline__ float group_sum(float v, float* red, int tpr) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if (tpr == 32) return v;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   __syncthreads();  // red may still be read by an earlier call
   if (lane == 0) red[warp] = v;
   __syncthreads();
+  const int wpg = tpr >> 5, first = (warp / wpg) * wpg;
   float s = 0.f;
-#pragma unroll
-  for (int w = 0; w < kNormThreads / 32; ++w) s += red[w];  // same order in every thread
+  for (int w = 0; w < wpg; ++w) s += red[first + w];  // the same order in every thread
   return s;
 }
 
@@ -56,54 +61,58 @@ __device__ __forceinline__ float norm_gain(const void* scale, int dtype, int kin
 // row's mean square.
 __device__ __forceinline__ void rms_apply(float (&v)[kNormMaxVec][8], int nv, int64_t D,
                                           const void* scale, int dtype, int kind, float eps,
-                                          float* red) {
+                                          float* red, int tpr, int tl) {
   float ss = 0.f;
 #pragma unroll
   for (int j = 0; j < kNormMaxVec; ++j)
     if (j < nv)
 #pragma unroll
       for (int i = 0; i < 8; ++i) ss = fmaf(v[j][i], v[j][i], ss);
-  const float total = block_sum(ss, red);
+  const float total = group_sum(ss, red, tpr);
   const float r = rsqrtf(__fdiv_rn(total, static_cast<float>(D)) + eps);
 #pragma unroll
   for (int j = 0; j < kNormMaxVec; ++j) {
     if (j >= nv) continue;
-    const int64_t d0 = (static_cast<int64_t>(j) * kNormThreads + threadIdx.x) * 8;
+    const int64_t d0 = (static_cast<int64_t>(j) * tpr + tl) * 8;
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[j][i] = __fmul_rn(__fmul_rn(v[j][i], r), norm_gain(scale, dtype, kind, d0 + i));
   }
 }
 
 __global__ void __launch_bounds__(kNormThreads)
-    rms_norm_kernel(const uint4* __restrict__ x, int64_t D, const void* __restrict__ scale, int dtype,
-                    int kind, float eps, uint4* __restrict__ out) {
+    rms_norm_kernel(const uint4* __restrict__ x, int64_t T, int64_t D, const void* __restrict__ scale, int dtype,
+                    int kind, float eps, int tpr, uint4* __restrict__ out) {
   __shared__ float red[kNormThreads / 32];
   const int64_t vec = D / 8;
-  const int nv = static_cast<int>((vec - threadIdx.x + kNormThreads - 1) / kNormThreads);
-  const uint4* xr = x + blockIdx.x * vec;
+  const int tl = threadIdx.x % tpr;
+  const int64_t row = blockIdx.x * static_cast<int64_t>(kNormThreads / tpr) + threadIdx.x / tpr;
+  const int nv = row < T ? static_cast<int>((vec - tl + tpr - 1) / tpr) : 0;
+  const uint4* xr = x + row * vec;
   float v[kNormMaxVec][8];
 #pragma unroll
   for (int j = 0; j < kNormMaxVec; ++j)
-    if (j < nv) bf16x8_to_f32(xr[j * kNormThreads + threadIdx.x], v[j]);
-  rms_apply(v, nv, D, scale, dtype, kind, eps, red);
-  uint4* orow = out + blockIdx.x * vec;
+    if (j < nv) bf16x8_to_f32(xr[j * tpr + tl], v[j]);
+  rms_apply(v, nv, D, scale, dtype, kind, eps, red, tpr, tl);
+  uint4* orow = out + row * vec;
 #pragma unroll
   for (int j = 0; j < kNormMaxVec; ++j)
-    if (j < nv) orow[j * kNormThreads + threadIdx.x] = f32x8_to_bf16(v[j]);
+    if (j < nv) orow[j * tpr + tl] = f32x8_to_bf16(v[j]);
 }
 
 __global__ void __launch_bounds__(kNormThreads)
-    block_finish_kernel(const float4* __restrict__ part, int splits, int64_t stride4, int64_t D,
+    block_finish_kernel(const float4* __restrict__ part, int splits, int64_t stride4, int64_t T, int64_t D,
                         const void* __restrict__ scale, int dtype, int kind, float eps,
-                        const uint4* __restrict__ h, uint4* __restrict__ out) {
+                        const uint4* __restrict__ h, int tpr, uint4* __restrict__ out) {
   __shared__ float red[kNormThreads / 32];
   const int64_t vec = D / 8;
-  const int nv = static_cast<int>((vec - threadIdx.x + kNormThreads - 1) / kNormThreads);
+  const int tl = threadIdx.x % tpr;
+  const int64_t row = blockIdx.x * static_cast<int64_t>(kNormThreads / tpr) + threadIdx.x / tpr;
+  const int nv = row < T ? static_cast<int>((vec - tl + tpr - 1) / tpr) : 0;
   float v[kNormMaxVec][8];
 #pragma unroll
   for (int j = 0; j < kNormMaxVec; ++j) {
     if (j >= nv) continue;
-    const int64_t e4 = (blockIdx.x * vec + j * kNormThreads + threadIdx.x) * 2;  // float4 index
+    const int64_t e4 = (row * vec + j * tpr + tl) * 2;  // float4 index
     float4 a = part[e4], b = part[e4 + 1];
     for (int s = 1; s < splits; ++s) {
       const float4 c = part[s * stride4 + e4], d = part[s * stride4 + e4 + 1];
@@ -115,7 +124,7 @@ __global__ void __launch_bounds__(kNormThreads)
     for (int i = 0; i < 8; ++i) v[j][i] = __bfloat162float(__float2bfloat16_rn(f[i]));  // the FFN output in bf16
   }
   if (scale != nullptr) {
-    rms_apply(v, nv, D, scale, dtype, kind, eps, red);
+    rms_apply(v, nv, D, scale, dtype, kind, eps, red, tpr, tl);
 #pragma unroll
     for (int j = 0; j < kNormMaxVec; ++j)
       if (j < nv)
@@ -125,7 +134,7 @@ __global__ void __launch_bounds__(kNormThreads)
 #pragma unroll
   for (int j = 0; j < kNormMaxVec; ++j) {
     if (j >= nv) continue;
-    const int64_t e = blockIdx.x * vec + j * kNormThreads + threadIdx.x;
+    const int64_t e = row * vec + j * tpr + tl;
     if (h != nullptr) {
       float hv[8];
       bf16x8_to_f32(h[e], hv);
@@ -134,6 +143,15 @@ __global__ void __launch_bounds__(kNormThreads)
     }
     out[e] = f32x8_to_bf16(v[j]);
   }
+}
+
+// Threads per row: the fewest of 32, 64, 128, 256 that hold a row in at most
+// kNormMaxVec vectors each.
+int norm_tpr(int64_t D) {
+  const int64_t vec = D / 8;
+  int tpr = 32;
+  while (tpr < kNormThreads && (vec + tpr - 1) / tpr > kNormMaxVec) tpr *= 2;
+  return tpr;
 }
 
 int check_norm(int64_t T, int64_t D, int scale_dtype, int kind, float eps) {
@@ -159,8 +177,10 @@ int launch_rms_norm(const void* x, int64_t T, int64_t D, const void* scale, int 
   KW8_REQUIRE(((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15) == 0,
               KW8_ERR_UNSUPPORTED, "RMSNorm rows must be 16-byte aligned");
   if (T == 0) return KW8_OK;
-  rms_norm_kernel<<<static_cast<unsigned>(T), kNormThreads, 0, stream>>>(
-      static_cast<const uint4*>(x), D, scale, scale_dtype, kind, eps, static_cast<uint4*>(out));
+  const int tpr = norm_tpr(D);
+  const int64_t rpc = kNormThreads / tpr;
+  rms_norm_kernel<<<static_cast<unsigned>((T + rpc - 1) / rpc), kNormThreads, 0, stream>>>(
+      static_cast<const uint4*>(x), T, D, scale, scale_dtype, kind, eps, tpr, static_cast<uint4*>(out));
   KW8_CHECK_LAUNCH();
   return KW8_OK;
 }
@@ -176,9 +196,11 @@ int launch_block_finish(const float* part, int splits, int64_t split_stride, int
                     reinterpret_cast<uintptr_t>(h)) & 15) == 0,
               KW8_ERR_UNSUPPORTED, "block epilogue rows must be 16-byte aligned");
   if (T == 0) return KW8_OK;
-  block_finish_kernel<<<static_cast<unsigned>(T), kNormThreads, 0, stream>>>(
-      reinterpret_cast<const float4*>(part), splits, split_stride / 4, D, post_scale, scale_dtype, kind, eps,
-      static_cast<const uint4*>(h), static_cast<uint4*>(out));
+  const int tpr = norm_tpr(D);
+  const int64_t rpc = kNormThreads / tpr;
+  block_finish_kernel<<<static_cast<unsigned>((T + rpc - 1) / rpc), kNormThreads, 0, stream>>>(
+      reinterpret_cast<const float4*>(part), splits, split_stride / 4, T, D, post_scale, scale_dtype, kind, eps,
+      static_cast<const uint4*>(h), tpr, static_cast<uint4*>(out));
   KW8_CHECK_LAUNCH();
   return KW8_OK;
 }

@@ -5,7 +5,8 @@
 
 namespace kw8 {
 
-// One row per CTA; D a multiple of 8, at most kNormMaxD.
+// Rows of D (a multiple of 8, at most kNormMaxD) spread over CTAs of
+// kNormThreads threads, each thread holding at most kNormMaxVec 8-wide vectors.
 constexpr int kNormThreads = 256;
 constexpr int kNormMaxVec = 8;  // 8-wide vectors per thread
 constexpr int64_t kNormMaxD = static_cast<int64_t>(kNormThreads) * 8 * kNormMaxVec;

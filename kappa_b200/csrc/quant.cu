@@ -2,9 +2,9 @@
 // (quant.py:34-38) kernels.
 //
 // quantize: pass 1 takes the absmax of every output channel (a warp per
-// channel when K is contiguous, else a thread per channel walking K, the
-// threads then reading consecutive channels) and, for the per-tensor form,
-// folds it into one word
+// channel when K is contiguous; a thread per channel and 64-k chunk when
+// the channels are contiguous) and, for the per-tensor form, folds it into
+// one word
 // with an integer atomicMax on the float's bits (valid for non-negative
 // floats; max is order independent, so the result is deterministic).
 // Pass 2 computes scale = max(amax / 127, FLT_MIN) with IEEE division,
@@ -37,6 +37,25 @@ __global__ void amax_kernel(const void* __restrict__ w, int dtype, int64_t outer
     ch_amax[ch] = m;
   else
     atomicMax(glob, __float_as_uint(m));
+}
+
+// Channels contiguous (sn == 1): a thread per channel and 64-k chunk, the
+// threads of a warp reading 32 consecutive channels; chunk maxima combine
+// with an integer atomicMax on the float's bits (values are >= 0, so the
+// order of the bits is the order of the values; ch_amax starts at zero).
+constexpr int64_t kAmaxChunk = 64;
+__global__ void amax_cols_kernel(const void* __restrict__ w, int dtype, int64_t outer, int64_t K,
+                                 int64_t N, int64_t so, int64_t sk, int per_channel,
+                                 unsigned* __restrict__ ch_amax_bits, unsigned* __restrict__ glob) {
+  const int64_t ch = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (ch >= outer * N) return;
+  const int64_t o = ch / N, n = ch - o * N;
+  const int64_t base = o * so + n;
+  const int64_t k0 = static_cast<int64_t>(blockIdx.y) * kAmaxChunk;
+  const int64_t k1 = k0 + kAmaxChunk < K ? k0 + kAmaxChunk : K;
+  float m = 0.f;
+  for (int64_t k = k0; k < k1; ++k) m = fmaxf(m, fabsf(load_w(w, dtype, base + k * sk)));
+  atomicMax(per_channel ? ch_amax_bits + ch : glob, __float_as_uint(m));
 }
 
 // A warp per output channel with K contiguous (sk == 1): the lanes read
@@ -221,6 +240,12 @@ int launch_quantize(const void* w, int w_dtype, int64_t outer, int64_t K, int64_
   if (sk == 1) {  // K contiguous: a warp per channel
     amax_rows_kernel<<<static_cast<unsigned>((channels * 32 + 255) / 256), 256, 0, stream>>>(
         w, w_dtype, outer, K, N, so, sn, per_channel, ch_amax, glob);
+  } else if (sn == 1 && (K + kAmaxChunk - 1) / kAmaxChunk <= 65535) {  // channels contiguous: split K too
+    if (per_channel) KW8_CUDA_TRY(cudaMemsetAsync(ch_amax, 0, static_cast<size_t>(channels) * sizeof(float), stream));
+    const dim3 grid(static_cast<unsigned>((channels + 255) / 256),
+                    static_cast<unsigned>((K + kAmaxChunk - 1) / kAmaxChunk));
+    amax_cols_kernel<<<grid, 256, 0, stream>>>(w, w_dtype, outer, K, N, so, sk, per_channel,
+                                               reinterpret_cast<unsigned*>(ch_amax), glob);
   } else {
     amax_kernel<<<static_cast<unsigned>((channels + 255) / 256), 256, 0, stream>>>(
         w, w_dtype, outer, K, N, so, sk, sn, per_channel, ch_amax, glob);
