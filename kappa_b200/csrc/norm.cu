@@ -2,9 +2,10 @@
 // kappa/qwen3/norms.py:10-16 with Qwen's scale) and the residual epilogue of
 // the FFN sub-block (kappa/gemma3/block.py:73-82, kappa/qwen3/block.py:68-81).
 //
-// A CTA of 256 threads takes 256 / tpr rows, tpr threads per row (the
-// fewest, from 32, that hold the row in at most kNormMaxVec 8-wide vectors
-// each: one warp per 2048-wide row).  The row is read once into registers,
+// A CTA takes up to 256 / tpr rows, tpr threads per row (the fewest, from
+// 32, that hold the row in at most kNormMaxVec 8-wide vectors each: one
+// warp per 2048-wide row), fewer rows when the grid would otherwise have
+// under two CTAs per SM.  The row is read once into registers,
 // the sum of squares is reduced over the row's threads in fp32 (a fixed
 // order), and the row is written once.  Rounding follows kappa: the norm computes in fp32 and rounds its
 // output to the activation dtype once; the FFN output is rounded to bf16
@@ -85,7 +86,7 @@ __global__ void __launch_bounds__(kNormThreads)
   __shared__ float red[kNormThreads / 32];
   const int64_t vec = D / 8;
   const int tl = threadIdx.x % tpr;
-  const int64_t row = blockIdx.x * static_cast<int64_t>(kNormThreads / tpr) + threadIdx.x / tpr;
+  const int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x / tpr) + threadIdx.x / tpr;
   const int nv = row < T ? static_cast<int>((vec - tl + tpr - 1) / tpr) : 0;
   const uint4* xr = x + row * vec;
   float v[kNormMaxVec][8];
@@ -106,7 +107,7 @@ __global__ void __launch_bounds__(kNormThreads)
   __shared__ float red[kNormThreads / 32];
   const int64_t vec = D / 8;
   const int tl = threadIdx.x % tpr;
-  const int64_t row = blockIdx.x * static_cast<int64_t>(kNormThreads / tpr) + threadIdx.x / tpr;
+  const int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x / tpr) + threadIdx.x / tpr;
   const int nv = row < T ? static_cast<int>((vec - tl + tpr - 1) / tpr) : 0;
   float v[kNormMaxVec][8];
 #pragma unroll
@@ -154,6 +155,14 @@ int norm_tpr(int64_t D) {
   return tpr;
 }
 
+// Rows per CTA: as many as kNormThreads threads hold, fewer when that would
+// leave fewer than two CTAs per SM (few rows: T = 256 gets one row a CTA).
+int64_t norm_rows_per_cta(int64_t T, int tpr) {
+  int64_t rpc = kNormThreads / tpr;
+  while (rpc > 1 && (T + rpc - 1) / rpc < 2 * 148) rpc /= 2;
+  return rpc;
+}
+
 int check_norm(int64_t T, int64_t D, int scale_dtype, int kind, float eps) {
   KW8_REQUIRE(T >= 0 && D >= 8 && D % 8 == 0 && D <= kNormMaxD, KW8_ERR_UNSUPPORTED,
               "RMSNorm rows need D %% 8 == 0 and 8 <= D <= %lld (D=%lld)", (long long)kNormMaxD,
@@ -178,8 +187,8 @@ int launch_rms_norm(const void* x, int64_t T, int64_t D, const void* scale, int 
               KW8_ERR_UNSUPPORTED, "RMSNorm rows must be 16-byte aligned");
   if (T == 0) return KW8_OK;
   const int tpr = norm_tpr(D);
-  const int64_t rpc = kNormThreads / tpr;
-  rms_norm_kernel<<<static_cast<unsigned>((T + rpc - 1) / rpc), kNormThreads, 0, stream>>>(
+  const int64_t rpc = norm_rows_per_cta(T, tpr);
+  rms_norm_kernel<<<static_cast<unsigned>((T + rpc - 1) / rpc), static_cast<unsigned>(rpc * tpr), 0, stream>>>(
       static_cast<const uint4*>(x), T, D, scale, scale_dtype, kind, eps, tpr, static_cast<uint4*>(out));
   KW8_CHECK_LAUNCH();
   return KW8_OK;
@@ -197,8 +206,8 @@ int launch_block_finish(const float* part, int splits, int64_t split_stride, int
               KW8_ERR_UNSUPPORTED, "block epilogue rows must be 16-byte aligned");
   if (T == 0) return KW8_OK;
   const int tpr = norm_tpr(D);
-  const int64_t rpc = kNormThreads / tpr;
-  block_finish_kernel<<<static_cast<unsigned>((T + rpc - 1) / rpc), kNormThreads, 0, stream>>>(
+  const int64_t rpc = norm_rows_per_cta(T, tpr);
+  block_finish_kernel<<<static_cast<unsigned>((T + rpc - 1) / rpc), static_cast<unsigned>(rpc * tpr), 0, stream>>>(
       reinterpret_cast<const float4*>(part), splits, split_stride / 4, T, D, post_scale, scale_dtype, kind, eps,
       static_cast<const uint4*>(h), tpr, static_cast<uint4*>(out));
   KW8_CHECK_LAUNCH();
