@@ -147,11 +147,14 @@ __global__ void __launch_bounds__(kNormThreads)
 }
 
 // Threads per row: the fewest of 32, 64, 128, 256 that hold a row in at most
-// kNormMaxVec vectors each.
-int norm_tpr(int64_t D) {
+// kNormMaxVec vectors each, doubled while the rows would keep fewer than
+// ~131k threads busy (few rows: more threads per row; measured at T = 256 /
+// 4096, D = 2560 / 2048).
+int norm_tpr(int64_t T, int64_t D) {
   const int64_t vec = D / 8;
   int tpr = 32;
   while (tpr < kNormThreads && (vec + tpr - 1) / tpr > kNormMaxVec) tpr *= 2;
+  while (tpr < kNormThreads && tpr < vec && T * tpr < 148 * 896) tpr *= 2;
   return tpr;
 }
 
@@ -186,7 +189,7 @@ int launch_rms_norm(const void* x, int64_t T, int64_t D, const void* scale, int 
   KW8_REQUIRE(((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15) == 0,
               KW8_ERR_UNSUPPORTED, "RMSNorm rows must be 16-byte aligned");
   if (T == 0) return KW8_OK;
-  const int tpr = norm_tpr(D);
+  const int tpr = norm_tpr(T, D);
   const int64_t rpc = norm_rows_per_cta(T, tpr);
   rms_norm_kernel<<<static_cast<unsigned>((T + rpc - 1) / rpc), static_cast<unsigned>(rpc * tpr), 0, stream>>>(
       static_cast<const uint4*>(x), T, D, scale, scale_dtype, kind, eps, tpr, static_cast<uint4*>(out));
@@ -205,7 +208,7 @@ int launch_block_finish(const float* part, int splits, int64_t split_stride, int
                     reinterpret_cast<uintptr_t>(h)) & 15) == 0,
               KW8_ERR_UNSUPPORTED, "block epilogue rows must be 16-byte aligned");
   if (T == 0) return KW8_OK;
-  const int tpr = norm_tpr(D);
+  const int tpr = norm_tpr(T, D);
   const int64_t rpc = norm_rows_per_cta(T, tpr);
   block_finish_kernel<<<static_cast<unsigned>((T + rpc - 1) / rpc), static_cast<unsigned>(rpc * tpr), 0, stream>>>(
       reinterpret_cast<const float4*>(part), splits, split_stride / 4, T, D, post_scale, scale_dtype, kind, eps,
